@@ -1,0 +1,365 @@
+"""CPU oracle for SparseDict's top-k sparse attention (test infrastructure).
+
+This module is the checker, never the product: only ``tests/``,
+``__graft_entry__.smoke()`` and the CPU-baseline legs of ``bench.py`` may
+import it.  The CUDA path in ``sparsedict_b200`` never calls into it.
+
+It restates, in numpy, the algorithm of the reference's PyTorch path:
+
+* the scaled affinity ``S = (Q @ K^T) * scale`` with
+  ``scale = 1 / (temperature * sqrt(d))``
+  (reference ``kernels/fused_topk_attn.py:997`` and
+  ``kernels/hybrid_topk.py:214-217``);
+* hard top-k selection, ordered by descending score with ties going to the
+  lower key index and NaN ranked above every number
+  (``models/modules/topk_select.py:94-103`` selects with ``torch.topk``;
+  the tie and NaN order is the comparator of
+  ``kernels/fused_topk_attn.py:67-89`` and ``kernels/hybrid_topk.py:101-106``);
+* softmax over the selected scores and the weighted sum of the gathered
+  value rows (``models/modules/topk_select.py:146-161``), with the row
+  log-sum-exp the fused path saves (``kernels/hybrid_topk.py:116-119``);
+* the sparse analytic backward
+  ``delta = sum P*G``, ``dS = P*(G - delta)``, ``dQ = scale * sum dS K``,
+  ``dK[I] += scale * dS Q``, ``dV[I] += P dO``
+  (``kernels/fused_topk_attn.py:642-648``, ``:880-887``, ``:1195-1201``);
+* a dense restatement of the same forward/backward, the way autograd runs
+  the reference CPU path (dense ``(N, M)`` scores and score gradients),
+  used as the timed CPU baseline.
+
+Parity of this oracle is pinned against golden vectors produced by running
+the reference's own ``sparse_topk_attention`` (see ``tests/golden``).  The
+lower-index tie rule is not pinned by any reference test (the reference
+avoids ties on purpose, ``kernels/fused_topk_attn.py:294-297``); the oracle
+defines it from the reference comparator cited above.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+__all__ = [
+    "round_to_bf16",
+    "round_to_f16",
+    "score_scale",
+    "affinity",
+    "quantize_to_grid",
+    "topk_order",
+    "topk_attention_forward",
+    "topk_attention_backward",
+    "dense_reference_fwd_bwd",
+    "moe_route_top1",
+    "moe_topk_attention_forward",
+    "moe_topk_attention_backward",
+    "gap_aware_index_mismatches",
+]
+
+
+def round_to_bf16(x: np.ndarray) -> np.ndarray:
+    """Round float32 values to bfloat16 (nearest-even) and widen back."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    bits = x.view(np.uint32).astype(np.uint64)
+    rounding = ((bits >> 16) & 1) + 0x7FFF
+    rounded = ((bits + rounding) >> 16) << 16
+    out = rounded.astype(np.uint32).view(np.float32).copy()
+    nan = np.isnan(x)
+    out[nan] = np.float32("nan")
+    return out
+
+
+def round_to_f16(x: np.ndarray) -> np.ndarray:
+    """Round float32 values to float16 and widen back."""
+    return np.asarray(x, dtype=np.float32).astype(np.float16).astype(np.float32)
+
+
+def score_scale(feature_dim: int, temperature: float = 1.0) -> float:
+    """``1 / (temperature * sqrt(d))`` (``kernels/fused_topk_attn.py:997``)."""
+    return 1.0 / (temperature * math.sqrt(feature_dim))
+
+
+def affinity(queries: np.ndarray, keys: np.ndarray, scale: float) -> np.ndarray:
+    """Scaled affinity ``(Q @ K^T) * scale`` in the inputs' float type.
+
+    Mirrors ``kernels/hybrid_topk.py:214-217``: the product is formed in
+    the compute dtype and then multiplied by the scale in that dtype.
+    """
+    dtype = queries.dtype
+    scores = np.matmul(queries, np.swapaxes(keys, -1, -2))
+    return (scores * dtype.type(scale)).astype(dtype, copy=False)
+
+
+def quantize_to_grid(
+    queries: np.ndarray, keys: np.ndarray, feature_dim: int, grid: int
+) -> np.ndarray:
+    """Tie-stress affinity: ``rint(grid * (Q @ K^T) / sqrt(d)) / grid`` in fp32.
+
+    The dot product is multiplied by ``grid`` (exact for a power of two),
+    divided by ``float32(sqrt(d))`` (one IEEE rounding), rounded half-to-even
+    to an integer and divided by ``grid`` (exact).  With queries and keys on
+    a 1/8 grid clamped to [-4, 4] every fp32 dot product is exact in any
+    summation order, so the selected indices are order independent.
+    """
+    dots = np.matmul(queries.astype(np.float32), np.swapaxes(keys, -1, -2).astype(np.float32))
+    root = np.float32(math.sqrt(feature_dim))
+    scaled = (dots * np.float32(grid)) / root
+    return (np.rint(scaled) / np.float32(grid)).astype(np.float32)
+
+
+def _ordered_sort_keys(scores: np.ndarray):
+    nan = np.isnan(scores)
+    value = np.where(nan, 0, scores)
+    return nan, value
+
+
+def topk_order(scores: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray]:
+    """Top-k along the last axis: NaN first, value descending, index ascending.
+
+    Returns ``(values, indices)`` with int64 indices, the layout of
+    ``torch.topk`` (``models/modules/topk_select.py:99``) and of
+    ``tiled_topk`` (``kernels/fused_topk_attn.py:290-336``).
+    """
+    if scores.ndim < 1:
+        raise ValueError("scores must have a key axis")
+    m = scores.shape[-1]
+    if not 1 <= k <= m:
+        raise ValueError(f"k must be between 1 and {m}; got {k}")
+    flat = scores.reshape(-1, m)
+    nan, value = _ordered_sort_keys(flat)
+    positions = np.broadcast_to(np.arange(m), flat.shape)
+    # lexsort sorts by the last key first: NaN rows first, then -value, then index.
+    order = np.lexsort((positions, -value.astype(np.float64), ~nan), axis=-1)
+    idx = order[:, :k]
+    vals = np.take_along_axis(flat, idx, axis=-1)
+    return vals.reshape(*scores.shape[:-1], k), idx.reshape(*scores.shape[:-1], k).astype(np.int64)
+
+
+def _softmax_lse(top_scores: np.ndarray):
+    row_max = np.max(top_scores, axis=-1, keepdims=True)
+    finite_max = np.where(np.isfinite(row_max), row_max, 0)
+    ex = np.exp(top_scores - finite_max)
+    total = np.sum(ex, axis=-1, keepdims=True)
+    weights = ex / total
+    lse = (finite_max + np.log(total))[..., 0]
+    return weights, lse
+
+
+def topk_attention_forward(
+    queries: np.ndarray,
+    keys: np.ndarray,
+    values: np.ndarray,
+    k: int,
+    scale: float,
+    *,
+    scores: np.ndarray | None = None,
+):
+    """Forward of top-k attention over ``(BH, N, d)`` / ``(BH, M, d)`` / ``(BH, M, dv)``.
+
+    Returns ``(out, indices int32, lse, top_scores)``.  The compute dtype is
+    the inputs' dtype (float32 or float64); float32 results accumulate the
+    value sum in float64 and round once, which keeps the oracle's own error
+    far below the GPU tolerances.  ``scores`` overrides the affinity (used by
+    the tie-stress grid).
+    """
+    if scores is None:
+        scores = affinity(queries, keys, scale)
+    top_scores, idx = topk_order(scores, k)
+    weights, lse = _softmax_lse(top_scores.astype(np.float64))
+    gathered = _gather_rows(values.astype(np.float64), idx)
+    out = np.einsum("bnk,bnkf->bnf", weights, gathered)
+    dtype = queries.dtype
+    return (
+        out.astype(dtype),
+        idx.astype(np.int32),
+        lse.astype(dtype),
+        top_scores.astype(dtype),
+    )
+
+
+def _gather_rows(table: np.ndarray, idx: np.ndarray) -> np.ndarray:
+    """``table[b, idx[b, n, j], :]`` for a ``(BH, M, F)`` table."""
+    bh = np.arange(table.shape[0])[:, None, None]
+    return table[bh, idx]
+
+
+def topk_attention_backward(
+    queries: np.ndarray,
+    keys: np.ndarray,
+    values: np.ndarray,
+    indices: np.ndarray,
+    grad_out: np.ndarray,
+    scale: float,
+    *,
+    scores: np.ndarray | None = None,
+):
+    """Sparse analytic backward on the saved support, in float64.
+
+    ``scores`` (optional) supplies the affinity the selection and softmax
+    used; gradients then pass straight through it, which is how the grid
+    quantisation of the tie-stress configuration is differentiated.
+    Returns ``(dq, dk, dv)`` in float64.
+    """
+    q = queries.astype(np.float64)
+    kk = keys.astype(np.float64)
+    v = values.astype(np.float64)
+    do = grad_out.astype(np.float64)
+    idx = indices.astype(np.int64)
+    k_sel = _gather_rows(kk, idx)  # (BH, N, k, d)
+    v_sel = _gather_rows(v, idx)  # (BH, N, k, dv)
+    if scores is None:
+        s = np.einsum("bnd,bnkd->bnk", q, k_sel) * scale
+    else:
+        s = np.take_along_axis(scores.astype(np.float64), idx, axis=-1)
+    p, _ = _softmax_lse(s)
+    g = np.einsum("bnf,bnkf->bnk", do, v_sel)
+    delta = np.sum(p * g, axis=-1, keepdims=True)
+    ds = p * (g - delta)
+    dq = scale * np.einsum("bnk,bnkd->bnd", ds, k_sel)
+    dk = np.zeros_like(kk)
+    dv = np.zeros_like(v)
+    bh = np.broadcast_to(np.arange(q.shape[0])[:, None, None], idx.shape)
+    np.add.at(dk, (bh, idx), scale * ds[..., None] * q[:, :, None, :])
+    np.add.at(dv, (bh, idx), p[..., None] * do[:, :, None, :])
+    return dq, dk, dv
+
+
+def dense_reference_fwd_bwd(
+    queries: np.ndarray,
+    keys: np.ndarray,
+    values: np.ndarray,
+    grad_out: np.ndarray,
+    k: int,
+    scale: float,
+):
+    """Forward and backward the way autograd runs the reference CPU path.
+
+    Dense ``(N, M)`` scores, hard top-k, softmax over the selected scores,
+    the dense ``weights`` scatter and the gathered weighted sum
+    (``models/modules/topk_select.py:119-161``); the backward materialises
+    the dense score gradient and contracts it with dense matmuls, as the
+    autograd graph of ``q @ k^T / sqrt(d)`` does.  Computes in the inputs'
+    float dtype.  Returns ``(out, indices, dq, dk, dv)``.
+    """
+    dtype = queries.dtype
+    scores = affinity(queries, keys, scale)
+    top_scores, idx = topk_order(scores, k)
+    row_max = top_scores.max(axis=-1, keepdims=True)
+    ex = np.exp(top_scores - row_max)
+    sel_w = ex / ex.sum(axis=-1, keepdims=True)
+    bh = np.broadcast_to(np.arange(scores.shape[0])[:, None, None], idx.shape)
+    rows = np.broadcast_to(np.arange(scores.shape[1])[None, :, None], idx.shape)
+    weights = np.zeros_like(scores)
+    weights[bh, rows, idx] = sel_w
+    out = np.matmul(weights, values)
+    # backward through the gathered softmax and the dense score product
+    g_sel = np.take_along_axis(np.matmul(grad_out, np.swapaxes(values, -1, -2)), idx, axis=-1)
+    delta = np.sum(sel_w * g_sel, axis=-1, keepdims=True)
+    d_sel = sel_w * (g_sel - delta)
+    d_scores = np.zeros_like(scores)
+    d_scores[bh, rows, idx] = d_sel
+    d_scores *= dtype.type(scale)
+    dq = np.matmul(d_scores, keys)
+    dk = np.matmul(np.swapaxes(d_scores, -1, -2), queries)
+    dv = np.matmul(np.swapaxes(weights, -1, -2), grad_out)
+    return out.astype(dtype), idx, dq.astype(dtype), dk.astype(dtype), dv.astype(dtype)
+
+
+def moe_route_top1(router_logits: np.ndarray) -> np.ndarray:
+    """Top-1 expert per token (``models/modules/router.py:139-145``).
+
+    With one active expert the softmax gate is exactly 1, so the gate fold
+    of ``models/modules/dual_domain_moe.py:158-173`` adds ``log(1) = 0`` to
+    the chosen expert's scores and ``-inf`` to every other expert's: the
+    top-k runs inside the chosen expert's atoms.  Ties go to the lower
+    expert index.
+    """
+    return np.argmax(router_logits, axis=-1).astype(np.int32)
+
+
+def moe_topk_attention_forward(
+    queries: np.ndarray,
+    dictionaries: np.ndarray,
+    experts: np.ndarray,
+    k: int,
+    scale: float,
+):
+    """Routed dictionary attention: token ``n`` attends within ``dictionaries[experts[n]]``.
+
+    ``queries`` is ``(N, d)``, ``dictionaries`` is ``(E, M, d)`` and serves
+    as both keys and values.  Indices are local to the chosen expert.
+    Returns ``(out, indices int32, lse)``.
+    """
+    n, d = queries.shape
+    out = np.zeros((n, dictionaries.shape[2]), dtype=queries.dtype)
+    idx = np.zeros((n, k), dtype=np.int32)
+    lse = np.zeros((n,), dtype=queries.dtype)
+    for e in range(dictionaries.shape[0]):
+        rows = np.nonzero(experts == e)[0]
+        if rows.size == 0:
+            continue
+        dic = dictionaries[e][None]
+        o, i, l, _ = topk_attention_forward(queries[rows][None], dic, dic, k, scale)
+        out[rows], idx[rows], lse[rows] = o[0], i[0], l[0]
+    return out, idx, lse
+
+
+def moe_topk_attention_backward(
+    queries: np.ndarray,
+    dictionaries: np.ndarray,
+    experts: np.ndarray,
+    indices: np.ndarray,
+    grad_out: np.ndarray,
+    scale: float,
+):
+    """Gradients of the routed attention: ``(dq, d_dictionaries)``, float64.
+
+    Keys and values are the same dictionary, so its gradient is
+    ``dK + dV`` per expert.
+    """
+    dq = np.zeros(queries.shape, dtype=np.float64)
+    ddict = np.zeros(dictionaries.shape, dtype=np.float64)
+    for e in range(dictionaries.shape[0]):
+        rows = np.nonzero(experts == e)[0]
+        if rows.size == 0:
+            continue
+        dic = dictionaries[e][None]
+        gq, gk, gv = topk_attention_backward(
+            queries[rows][None], dic, dic, indices[rows][None], grad_out[rows][None], scale
+        )
+        dq[rows] = gq[0]
+        ddict[e] = gk[0] + gv[0]
+    return dq, ddict
+
+
+def gap_aware_index_mismatches(
+    actual: np.ndarray, expected: np.ndarray, scores: np.ndarray, tol: float
+) -> int:
+    """Count rows whose selected sets differ by more than a near-tie.
+
+    A row passes when the index lists are equal, or when every key that is
+    in one selection but not the other scores within ``tol`` of the
+    oracle's k-th selected score (a flip inside the rounding noise of two
+    different summation orders).  Returns the number of failing rows.
+    """
+    act = actual.reshape(-1, actual.shape[-1]).astype(np.int64)
+    exp = expected.reshape(-1, expected.shape[-1]).astype(np.int64)
+    sc = scores.reshape(-1, scores.shape[-1])
+    bad = 0
+    for r in np.nonzero(np.any(act != exp, axis=1))[0]:
+        a, e = set(act[r].tolist()), set(exp[r].tolist())
+        boundary = sc[r, exp[r, -1]]
+        diff = list(a ^ e)
+        if any(i < 0 or i >= sc.shape[1] for i in diff):
+            bad += 1
+            continue
+        if not diff:
+            # same set, different order: only allowed among near-equal scores
+            pos = np.nonzero(act[r] != exp[r])[0]
+            if np.all(np.abs(sc[r, act[r, pos]] - sc[r, exp[r, pos]]) <= tol):
+                continue
+            bad += 1
+            continue
+        if np.all(np.abs(sc[r, diff] - boundary) <= tol):
+            continue
+        bad += 1
+    return bad
