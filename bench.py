@@ -1,0 +1,340 @@
+#!/usr/bin/env python
+"""Throughput of fused top-k sparse attention, forward + backward, on B200.
+
+Workload (the headline configuration): B=16, H=8, N=M=16384 tokens, d=64,
+k=64, bf16 inputs with fp32 accumulation; Q, K, V, dO iid N(0,1) from a
+seed.  A step is one forward and one backward over all B*H*N query rows,
+split as whole (b, h) slices across the ranks with K and V replicated and the
+fp32 dK/dV accumulators all-reduced over NVLink (strong scaling: the total
+work is fixed).  Inputs (268 MB each) are larger than the 126 MB L2.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Prints one JSON line (rank 0).  ``--impl reference`` times the CPU
+restatement of the reference path (dense scores, hard top-k, softmax,
+gather, dense autograd-style backward) on this host's cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "top-k attn fwd+bwd queries/sec @1/2/4/8 B200; % tensor-pipe & HBM roofline"
+UNIT = "queries/s"
+CFG = dict(B=16, H=8, N=16384, M=16384, d=64, k=64)
+WORKLOAD = "sharded bf16 fwd+bwd, B=16 H=8 N=M=16384 d=64 k=64"
+
+
+def roofline_terms(b, h, n, m, d, k, elem):
+    """Algorithmic work of one fwd+bwd over all slices (see DESIGN.md roofline)."""
+    flops_tc = 2.0 * n * m * d * b * h  # the dense affinity, the only dense contraction
+    bytes_fb = ((5 * n + 6 * m) * d * elem + 8 * n * (k + 1)) * b * h
+    return flops_tc, bytes_fb
+
+
+def load_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        p = json.loads(path.read_text())
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained", p["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def load_traffic():
+    path = ROOT / "profiles" / "traffic.json"
+    if path.exists():
+        try:
+            return json.loads(path.read_text())
+        except ValueError:
+            return {}
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi samples (every 200 ms) while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------- CPU arms --
+
+
+def cpu_reference_sample(rows=256, seed=0):
+    """Time the CPU restatement of the reference path on one bounded slice.
+
+    One (b, h) slice of the workload: ``rows`` query rows against all M keys
+    (bf16-rounded inputs, fp32 compute), forward and backward.  Returns
+    (queries/s, seconds, description).
+    """
+    import numpy as np
+
+    import oracle
+
+    c = CFG
+    rng = np.random.default_rng(seed)
+    q = oracle.round_to_bf16(rng.standard_normal((1, rows, c["d"]), dtype=np.float32))
+    k = oracle.round_to_bf16(rng.standard_normal((1, c["M"], c["d"]), dtype=np.float32))
+    v = oracle.round_to_bf16(rng.standard_normal((1, c["M"], c["d"]), dtype=np.float32))
+    do = rng.standard_normal((1, rows, c["d"]), dtype=np.float32)
+    t0 = time.perf_counter()
+    oracle.dense_reference_fwd_bwd(q, k, v, do, c["k"], 1 / math.sqrt(c["d"]))
+    dt = time.perf_counter() - t0
+    return rows / dt, dt, f"one (b,h) slice: {rows} query rows x M={c['M']} keys, d={c['d']}, k={c['k']}, fp32 " \
+                          "on bf16-rounded inputs, dense fwd+bwd; queries/s extrapolated from the slice"
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    cores = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        cpu_reference_sample(rows=args.ref_rows)
+    rates, secs = [], []
+    for i in range(args.steps):
+        r, s, desc = cpu_reference_sample(rows=args.ref_rows, seed=i + 1)
+        rates.append(r)
+        secs.append(s)
+    value = statistics.median(rates)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * statistics.median(secs),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, **CFG, "sample_rows": args.ref_rows},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------- GPU arm --
+
+
+def run_native_arm(args):
+    import torch
+    import torch.distributed as dist
+
+    from sparsedict_b200 import _native
+    from sparsedict_b200 import fused_topk_attention
+    from sparsedict_b200.sharded import ShardedTopKAttention, ShardPlan
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    _native.load()
+    group = None
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+        group = dist.group.WORLD
+
+    c = CFG
+    slices = c["B"] * c["H"]
+    plan = ShardPlan(slices, world, rank)
+    gen = torch.Generator(device=dev).manual_seed(1234)
+    dtype = torch.bfloat16
+    keys = torch.randn(slices, c["M"], c["d"], device=dev, generator=gen).to(dtype)
+    values = torch.randn(slices, c["M"], c["d"], device=dev, generator=gen).to(dtype)
+    gen.manual_seed(1234 + 1000 * (rank + 1))
+    q_rows = torch.randn(plan.per_rank, c["N"], c["d"], device=dev, generator=gen).to(dtype)
+    dout_rows = torch.randn(plan.per_rank, c["N"], c["d"], device=dev, generator=gen).to(dtype)
+    runner = ShardedTopKAttention(plan, c["M"], c["d"], c["d"], c["k"], dtype, dev, group=group,
+                                  reduce=args.reduce, buckets=args.buckets)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        runner.step(q_rows, keys, values, dout_rows)
+    barrier()
+
+    stream = torch.cuda.current_stream(dev)
+    fwd_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        start.record(stream)
+        for i in range(args.steps):
+            runner.step(q_rows, keys, values, dout_rows, fwd_timer=fwd_events[i])
+        stop.record(stream)
+        barrier()
+    elapsed = start.elapsed_time(stop) / 1000.0
+    fwd_ms = statistics.mean(a.elapsed_time(b) for a, b in fwd_events)
+    t = torch.tensor([elapsed, fwd_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed, fwd_ms = float(t[0]), float(t[1])
+
+    total_queries = slices * c["N"]
+    value = total_queries * args.steps / elapsed
+    ms_per_step = 1000 * elapsed / args.steps
+
+    # end to end through the public API: pinned host inputs copied in, fwd+bwd,
+    # a scalar result read back, every step (the rank's own rows).
+    e2e = None
+    if not args.skip_e2e:
+        host = [t.cpu().pin_memory() for t in (q_rows, keys, values, dout_rows)]
+        h2d = sum(t.numel() * t.element_size() for t in host)
+        dq_, dk_, dv_ = (torch.empty_like(t) for t in (q_rows, keys, values))
+
+        def e2e_step():
+            qd, kd, vd, dod = (t.to(dev, non_blocking=True) for t in host)
+            if world == 1:
+                qd4, kd4, vd4 = (x.view(c["B"], c["H"], -1, c["d"]).requires_grad_(True) for x in (qd, kd, vd))
+                out = fused_topk_attention(qd4, kd4, vd4, c["k"])
+                grads = torch.autograd.grad(out, (qd4, kd4, vd4), dod.view_as(out))
+                res = (out.float() * dod.view_as(out).float()).sum()
+            else:
+                out, dq, dk, dv = runner.step(qd, kd, vd, dod)
+                res = (out.float() * dod.float()).sum()
+            return res.cpu()
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        barrier()
+        e2e_s = torch.tensor([time.perf_counter() - t0], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
+        e2e = {"value": total_queries * args.e2e_steps / float(e2e_s[0]), "unit": UNIT,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4,
+               "note": "public API, inputs copied from pinned host memory every step, scalar read back"}
+        del host, dq_, dk_, dv_
+
+    peaks = load_peaks()
+    flops_tc, bytes_fb = roofline_terms(c["B"], c["H"], c["N"], c["M"], c["d"], c["k"], 2)
+    # dominant kernel: the fused forward (affinity MMA + selection + aggregate)
+    fwd_flops_per_launch = flops_tc / world
+    achieved = fwd_flops_per_launch / (fwd_ms / 1000.0) / 1e12
+    peak_tc = peaks["bf16_tflops_sustained"]
+    traffic = load_traffic().get("fused_fwd_cfg4")
+    t_roof = max(flops_tc / world / (peak_tc * 1e12), bytes_fb / world / (peaks["hbm_gbs"] * 1e9))
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, **CFG, "parallelism": f"rows{world}", "reduce": args.reduce,
+                   "l2": "inputs larger than L2 (268 MB per tensor)"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tc, "unit": "TFLOP/s",
+                     "frac": achieved / peak_tc, "traffic": traffic, "kernel": "fused forward",
+                     "fwd_ms": fwd_ms, "peak_source": f"{peaks['source']} bf16_tflops_sustained",
+                     "step_frac_combined": t_roof / (ms_per_step / 1000.0)},
+        "gpu_launches": 4 * args.steps,
+    }
+    if e2e is not None:
+        line["e2e"] = e2e
+    if rank == 0 and not args.skip_cpu:
+        r, s, desc = cpu_reference_sample(rows=args.ref_rows)
+        rates = [r]
+        budget = time.perf_counter() + 10
+        i = 1
+        while time.perf_counter() < budget and i < 8:
+            rates.append(cpu_reference_sample(rows=args.ref_rows, seed=i)[0])
+            i += 1
+        line["cpu_baseline"] = {"value": statistics.median(rates), "unit": UNIT, "cores": os.cpu_count() or 1,
+                                "kind": "port", "sample": desc + f"; median of {len(rates)}"}
+    line["clocks"] = clocks.summary()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["native", "reference"], default="native")
+    ap.add_argument("--reduce", choices=["allreduce", "allgather", "none"], default="allreduce")
+    ap.add_argument("--buckets", type=int, default=4)
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--ref-rows", type=int, default=256)
+    ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--skip-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_native_arm(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

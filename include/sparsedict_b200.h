@@ -1,0 +1,151 @@
+/*
+ * sparsedict_b200 — C ABI of the B200 (sm_100a) top-k sparse attention path.
+ *
+ * Plain pointers and sizes only: every tensor argument is a device pointer to
+ * a dense row-major buffer, every size is an element count, `stream` is a
+ * cudaStream_t passed as void* (NULL = the legacy default stream).  No call
+ * allocates device memory, synchronises the host, or throws: each returns 0
+ * (SDK_OK) or one of the status codes below; sdk_status_string() names it.
+ *
+ * Layout conventions (the reference's flattened layout,
+ * kernels/fused_topk_attn.py:999-1001):
+ *   q    [rows, d]        rows = slices * n (uniform) or offsets[slices]
+ *   k    [slices, m, d]   keys of slice s start at k + s*m*d
+ *   v    [slices, m, dv]
+ *   out  [rows, dv], top_idx [rows, topk] int32, lse [rows]
+ * Element types: SDK_DTYPE_* for q/k/v/out/dout/dq; lse, top_scores and the
+ * gradient accumulators are float64 for SDK_DTYPE_F64 and float32 otherwise.
+ */
+#ifndef SPARSEDICT_B200_H_
+#define SPARSEDICT_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  SDK_DTYPE_F32 = 0,
+  SDK_DTYPE_F64 = 1,
+  SDK_DTYPE_BF16 = 2,
+  SDK_DTYPE_F16 = 3,
+};
+
+enum {
+  SDK_OK = 0,
+  SDK_ERR_INVALID_ARGUMENT = 1, /* a size, pointer or dtype the call cannot accept */
+  SDK_ERR_UNSUPPORTED = 2,      /* valid request outside this build's kernels (e.g. k too large) */
+  SDK_ERR_CUDA = 3,             /* a CUDA runtime call or launch failed */
+  SDK_ERR_NO_DEVICE = 4,        /* no sm_100 device is current */
+};
+
+/* Library version, (major << 16) | minor. */
+int sdk_version(void);
+
+/* Human-readable name of a status code returned by any sdk_* call. */
+const char* sdk_status_string(int status);
+
+/* Text of the last CUDA error recorded by this thread (empty if none). */
+const char* sdk_last_cuda_error(void);
+
+/* Largest top-k the fused kernels accept for `dtype` and feature width `d`. */
+int sdk_max_topk(int32_t dtype, int32_t d);
+
+/* Reads the device status word of the current device into *bits (bit 1: an
+ * index outside [0, m) was met and skipped; bit 2: a bounded wait gave up),
+ * clearing it when `clear` is nonzero.  Synchronises `stream`. */
+int sdk_device_status(unsigned int* bits, int32_t clear, void* stream);
+
+/*
+ * Fused forward, stages 1-3: scaled affinity q·kᵀ, per-row top-k selection
+ * (NaN first, larger score first, lower key index on ties), softmax over the
+ * selected scores and the weighted sum of the gathered value rows.
+ *
+ * Replaces FusedTopKAttentionFunction.forward (kernels/fused_topk_attn.py:989-1094)
+ * and _hybrid_topk_attention_with_aux (kernels/hybrid_topk.py:153-290), whose
+ * outputs (top_scores, top_indices int32, lse, out) it writes.
+ *   scale       score multiplier 1/(temperature*sqrt(d)) (fused_topk_attn.py:997)
+ *   score_grid  0, or G > 0 for the tie-stress affinity rint(G*dot/root)/G with
+ *               root = float(1/scale)
+ *   row_offsets nullable: when set, slice s owns rows [row_offsets[s],
+ *               row_offsets[s+1]) and n is the total row count (grouped /
+ *               routed dictionaries)
+ *   row_index   nullable: logical row r reads q/writes out at physical row
+ *               row_index[r] (a routing permutation); top_idx/lse/top_scores
+ *               stay in logical order
+ *   top_scores  nullable
+ */
+int sdk_topk_attn_fwd(const void* q, const void* k, const void* v, void* out, int32_t* top_idx,
+                      void* lse, void* top_scores, const int32_t* row_offsets,
+                      const int32_t* row_index, int64_t slices, int64_t n, int64_t m, int32_t d,
+                      int32_t dv, int32_t topk, double scale, int32_t score_grid, int32_t dtype,
+                      void* stream);
+
+/*
+ * Sparse backward on the saved support (replaces
+ * FusedTopKAttentionFunction.backward, kernels/fused_topk_attn.py:1096-1201,
+ * i.e. kernels B1 _backward_dq :609-846 and B2 _backward_dkv :848-977):
+ *   dq      = scale * sum_j dS_ij k_j               (written, dtype)
+ *   dk_acc += scale * dS_ij q_i  at row top_idx_ij  (accumulator dtype)
+ *   dv_acc += P_ij dout_i        at row top_idx_ij  (accumulator dtype)
+ * with P = exp(S - lse), G = dout·v_j, dS = P (G - sum_j P G).  The
+ * accumulators are zeroed first unless `accumulate` is nonzero; dk_acc and
+ * dv_acc may alias (keys and values that are the same dictionary).  For
+ * SDK_DTYPE_F32/F64 the accumulators can be the dK/dV outputs themselves.
+ */
+int sdk_topk_attn_bwd(const void* q, const void* k, const void* v, const void* dout,
+                      const int32_t* top_idx, const void* lse, void* dq, void* dk_acc,
+                      void* dv_acc, const int32_t* row_offsets, const int32_t* row_index,
+                      int64_t slices, int64_t n, int64_t m, int32_t d, int32_t dv, int32_t topk,
+                      double scale, int32_t score_grid, int32_t accumulate, int32_t dtype,
+                      void* stream);
+
+/* Converts `count` accumulator elements (float32; float64 for F64) into
+ * `dtype`, multiplying by `multiplier`.  `out` may alias `acc` only when the
+ * element sizes match. */
+int sdk_finalize_grad(const void* acc, void* out, int64_t count, double multiplier, int32_t dtype,
+                      void* stream);
+
+/*
+ * Stage 1 alone: dense scores[n, m] (float32) = q[n, d] · k[m, d]ᵀ, with
+ * row strides in elements.  Replaces tiled_affinity
+ * (kernels/fused_topk_attn.py:227-287); dtype F32 or F16.
+ */
+int sdk_affinity(const void* q, const void* k, float* scores, int64_t n, int64_t m, int32_t d,
+                 int64_t q_row_stride, int64_t k_row_stride, int32_t dtype, void* stream);
+
+/*
+ * Stage 2 alone: per-row top-k of scores[rows, m] (row stride in elements),
+ * writing values (input dtype) and int64 indices.  Replaces tiled_topk
+ * (kernels/fused_topk_attn.py:290-336); dtype F32 or F16.
+ */
+int sdk_topk_select(const void* scores, void* top_values, int64_t* top_idx, int64_t rows, int64_t m,
+                    int64_t row_stride, int32_t topk, int32_t dtype, void* stream);
+
+/*
+ * Stage 3 alone: out[rows, dv] (float32) = softmax(top_scores) · values[top_idx].
+ * Replaces tiled_topk_aggregate (kernels/fused_topk_attn.py:339-408).
+ * score_dtype / value_dtype: F32 or F16; idx_bits: 32 or 64.  Indices outside
+ * [0, m) contribute nothing and set device status bit 1.
+ */
+int sdk_topk_aggregate(const void* top_scores, const void* top_idx, const void* values, float* out,
+                       int64_t rows, int32_t topk, int64_t m, int32_t dv, int64_t score_row_stride,
+                       int64_t idx_row_stride, int64_t value_row_stride, int32_t score_dtype,
+                       int32_t idx_bits, int32_t value_dtype, void* stream);
+
+/*
+ * Top-1 routing for the routed-dictionary configuration: expert[i] =
+ * argmax_e logits[i, e] (lowest e on ties; models/modules/router.py:139-145),
+ * then a stable counting sort: order[] lists rows grouped by expert and
+ * offsets[e] .. offsets[e+1] delimits expert e's rows in it.
+ * offsets needs experts+1 entries.  logits are float32.
+ */
+int sdk_route_top1(const float* logits, int64_t n, int32_t experts, int32_t* expert,
+                   int32_t* order, int32_t* offsets, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPARSEDICT_B200_H_ */

@@ -125,6 +125,8 @@ def topk_order(scores: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray]:
     if not 1 <= k <= m:
         raise ValueError(f"k must be between 1 and {m}; got {k}")
     flat = scores.reshape(-1, m)
+    if m > 64 and not np.isnan(flat).any():
+        return _topk_order_partition(flat, k, scores.shape)
     nan, value = _ordered_sort_keys(flat)
     positions = np.broadcast_to(np.arange(m), flat.shape)
     # lexsort sorts by the last key first: NaN rows first, then -value, then index.
@@ -132,6 +134,27 @@ def topk_order(scores: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray]:
     idx = order[:, :k]
     vals = np.take_along_axis(flat, idx, axis=-1)
     return vals.reshape(*scores.shape[:-1], k), idx.reshape(*scores.shape[:-1], k).astype(np.int64)
+
+
+def _topk_order_partition(flat: np.ndarray, k: int, shape) -> tuple[np.ndarray, np.ndarray]:
+    """NaN-free rows: the same order as the lexsort path in O(M) per row.
+
+    Takes every score above the row's k-th largest value plus, among the
+    scores equal to it, the lowest indices; then orders those k by value
+    (descending) with a stable sort, which keeps ascending index on ties.
+    """
+    m = flat.shape[1]
+    kth = np.partition(flat, m - k, axis=-1)[:, m - k][:, None]
+    greater = flat > kth
+    equal = flat == kth
+    need = k - greater.sum(axis=-1, keepdims=True)
+    take = greater | (equal & (np.cumsum(equal, axis=-1) <= need))
+    cols = np.nonzero(take)[1].reshape(-1, k)
+    vals = np.take_along_axis(flat, cols, axis=-1)
+    order = np.argsort(-vals.astype(np.float64), axis=-1, kind="stable")
+    cols = np.take_along_axis(cols, order, axis=-1)
+    vals = np.take_along_axis(vals, order, axis=-1)
+    return vals.reshape(*shape[:-1], k), cols.reshape(*shape[:-1], k).astype(np.int64)
 
 
 def _softmax_lse(top_scores: np.ndarray):

@@ -1,0 +1,26 @@
+"""sparsedict_b200: SparseDict's fused top-k sparse attention, native to B200 (sm_100a).
+
+Public API (the reference's names and signatures):
+    fused_topk_attention, FusedTopKAttentionFunction, hybrid_topk_attention,
+    tiled_affinity, tiled_topk, tiled_topk_aggregate
+plus routed dictionary attention (``routed_dictionary_attention``) and the
+row-sharded multi-GPU step (``sparsedict_b200.sharded``).
+"""
+
+from .kernels.fused_topk_attn import (
+    FusedTopKAttentionFunction,
+    fused_topk_attention,
+    tiled_affinity,
+    tiled_topk,
+    tiled_topk_aggregate,
+)
+from .kernels.hybrid_topk import _hybrid_topk_attention_with_aux, hybrid_topk_attention
+
+__all__ = [
+    "FusedTopKAttentionFunction",
+    "fused_topk_attention",
+    "hybrid_topk_attention",
+    "tiled_affinity",
+    "tiled_topk",
+    "tiled_topk_aggregate",
+]

@@ -1,0 +1,158 @@
+"""Tensor-level calls into the C ABI: allocate outputs, launch on the current stream.
+
+Callers own every buffer (the reference convention, outputs made with
+``torch.empty``/``torch.zeros``); inputs must already be contiguous.  These
+helpers do no argument validation beyond what the C ABI itself rejects —
+the public modules validate first, with the reference's messages.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _native as nat
+
+
+def acc_dtype(dtype: torch.dtype) -> torch.dtype:
+    """Accumulator / LSE dtype for an input dtype."""
+    return torch.float64 if dtype == torch.float64 else torch.float32
+
+
+def topk_attn_fwd(
+    q2: torch.Tensor,
+    k2: torch.Tensor,
+    v2: torch.Tensor,
+    topk: int,
+    scale: float,
+    *,
+    score_grid: int = 0,
+    want_scores: bool = False,
+    row_offsets: torch.Tensor | None = None,
+    row_index: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+):
+    """Fused forward over ``q2 [rows or (S, n), d]``, ``k2 [S, m, d]``, ``v2 [S, m, dv]``.
+
+    Returns ``(out, top_idx int32 [rows, k], lse [rows], top_scores|None)``
+    where ``rows`` is ``S * n`` (uniform slices) or the grouped row count.
+    """
+    slices, m, d = k2.shape
+    dv = v2.shape[-1]
+    if row_offsets is None:
+        n = q2.shape[-2]
+        rows = slices * n
+    else:
+        n = rows = q2.reshape(-1, d).shape[0]
+    dev = q2.device
+    acc = acc_dtype(q2.dtype)
+    if out is None:
+        out = torch.empty((*q2.shape[:-1], dv), device=dev, dtype=q2.dtype)
+    idx = torch.empty((rows, topk), device=dev, dtype=torch.int32)
+    lse = torch.empty((rows,), device=dev, dtype=acc)
+    scores = torch.empty((rows, topk), device=dev, dtype=acc) if want_scores else None
+    with torch.cuda.device(dev):
+        nat.call(
+            "sdk_topk_attn_fwd",
+            q2.data_ptr(), k2.data_ptr(), v2.data_ptr(), out.data_ptr(), idx.data_ptr(), lse.data_ptr(),
+            nat.ptr(scores), nat.ptr(row_offsets), nat.ptr(row_index),
+            slices, n, m, d, dv, topk, float(scale), int(score_grid), nat.TORCH_TO_SDK[q2.dtype],
+            nat.stream_of(dev),
+        )
+    return out, idx, lse, scores
+
+
+def topk_attn_bwd(
+    q2: torch.Tensor,
+    k2: torch.Tensor,
+    v2: torch.Tensor,
+    dout2: torch.Tensor,
+    top_idx: torch.Tensor,
+    lse: torch.Tensor,
+    scale: float,
+    *,
+    score_grid: int = 0,
+    dk_acc: torch.Tensor | None = None,
+    dv_acc: torch.Tensor | None = None,
+    accumulate: bool = False,
+    row_offsets: torch.Tensor | None = None,
+    row_index: torch.Tensor | None = None,
+    dq: torch.Tensor | None = None,
+):
+    """Sparse backward; returns ``(dq, dk_acc, dv_acc)`` (accumulators in ``acc_dtype``)."""
+    slices, m, d = k2.shape
+    dv = v2.shape[-1]
+    topk = top_idx.shape[-1]
+    n = q2.shape[-2] if row_offsets is None else q2.reshape(-1, d).shape[0]
+    dev = q2.device
+    acc = acc_dtype(q2.dtype)
+    if dq is None:
+        dq = torch.empty_like(q2)
+    if dk_acc is None:
+        dk_acc = torch.empty((slices, m, d), device=dev, dtype=acc)
+    if dv_acc is None:
+        dv_acc = torch.empty((slices, m, dv), device=dev, dtype=acc)
+    with torch.cuda.device(dev):
+        nat.call(
+            "sdk_topk_attn_bwd",
+            q2.data_ptr(), k2.data_ptr(), v2.data_ptr(), dout2.data_ptr(), top_idx.data_ptr(), lse.data_ptr(),
+            dq.data_ptr(), dk_acc.data_ptr(), dv_acc.data_ptr(), nat.ptr(row_offsets), nat.ptr(row_index),
+            slices, n, m, d, dv, topk, float(scale), int(score_grid), int(accumulate), nat.TORCH_TO_SDK[q2.dtype],
+            nat.stream_of(dev),
+        )
+    return dq, dk_acc, dv_acc
+
+
+def finalize_grad(acc: torch.Tensor, dtype: torch.dtype, multiplier: float = 1.0) -> torch.Tensor:
+    """Accumulator -> ``dtype`` (returns ``acc`` itself when no conversion is needed)."""
+    if acc.dtype == dtype and multiplier == 1.0:
+        return acc
+    out = torch.empty(acc.shape, device=acc.device, dtype=dtype)
+    with torch.cuda.device(acc.device):
+        nat.call("sdk_finalize_grad", acc.data_ptr(), out.data_ptr(), acc.numel(), float(multiplier),
+                 nat.TORCH_TO_SDK[dtype], nat.stream_of(acc.device))
+    return out
+
+
+def affinity(queries: torch.Tensor, keys: torch.Tensor) -> torch.Tensor:
+    n, d = queries.shape
+    m = keys.shape[0]
+    scores = torch.empty((n, m), device=queries.device, dtype=torch.float32)
+    with torch.cuda.device(queries.device):
+        nat.call("sdk_affinity", queries.data_ptr(), keys.data_ptr(), scores.data_ptr(), n, m, d,
+                 queries.stride(0), keys.stride(0), nat.TORCH_TO_SDK[queries.dtype], nat.stream_of(queries.device))
+    return scores
+
+
+def select(scores: torch.Tensor, k: int):
+    rows, m = scores.shape
+    vals = torch.empty((rows, k), device=scores.device, dtype=scores.dtype)
+    idx = torch.empty((rows, k), device=scores.device, dtype=torch.int64)
+    with torch.cuda.device(scores.device):
+        nat.call("sdk_topk_select", scores.data_ptr(), vals.data_ptr(), idx.data_ptr(), rows, m, scores.stride(0),
+                 k, nat.TORCH_TO_SDK[scores.dtype], nat.stream_of(scores.device))
+    return vals, idx
+
+
+def aggregate(top_scores: torch.Tensor, top_indices: torch.Tensor, values: torch.Tensor) -> torch.Tensor:
+    rows, k = top_scores.shape
+    m, dv = values.shape
+    out = torch.empty((rows, dv), device=values.device, dtype=torch.float32)
+    with torch.cuda.device(values.device):
+        nat.call("sdk_topk_aggregate", top_scores.data_ptr(), top_indices.data_ptr(), values.data_ptr(),
+                 out.data_ptr(), rows, k, m, dv, top_scores.stride(0), top_indices.stride(0), values.stride(0),
+                 nat.TORCH_TO_SDK[top_scores.dtype], 64 if top_indices.dtype == torch.int64 else 32,
+                 nat.TORCH_TO_SDK[values.dtype], nat.stream_of(values.device))
+    return out
+
+
+def route_top1(logits: torch.Tensor):
+    """Top-1 routing: ``(expert [n], order [n], offsets [E+1])`` as int32 device tensors."""
+    n, experts = logits.shape
+    dev = logits.device
+    expert = torch.empty((n,), device=dev, dtype=torch.int32)
+    order = torch.empty((n,), device=dev, dtype=torch.int32)
+    offsets = torch.empty((experts + 1,), device=dev, dtype=torch.int32)
+    with torch.cuda.device(dev):
+        nat.call("sdk_route_top1", logits.data_ptr(), n, experts, expert.data_ptr(), order.data_ptr(),
+                 offsets.data_ptr(), nat.stream_of(dev))
+    return expert, order, offsets

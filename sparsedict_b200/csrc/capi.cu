@@ -1,0 +1,193 @@
+// extern "C" entry points of libsparsedict_b200.so (declared in
+// include/sparsedict_b200.h).  Each validates its arguments, picks the
+// kernel for the dtype/shape and launches on the caller's stream.  No
+// exceptions cross this boundary and nothing here allocates device memory.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace sdk {
+
+__device__ unsigned int g_device_status;
+
+namespace {
+thread_local char g_last_cuda_error[256] = "";
+std::mutex g_status_mutex;
+unsigned int* g_status_ptr[64] = {};
+
+int record(cudaError_t err) {
+  if (err == cudaSuccess) return SDK_OK;
+  std::snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "%s: %s", cudaGetErrorName(err),
+                cudaGetErrorString(err));
+  return SDK_ERR_CUDA;
+}
+
+int finish(int rc) {
+  if (rc == SDK_ERR_CUDA) {
+    const cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) record(err);
+  }
+  return rc;
+}
+
+bool dtype_ok(int32_t dtype) {
+  return dtype == SDK_DTYPE_F32 || dtype == SDK_DTYPE_F64 || dtype == SDK_DTYPE_BF16 || dtype == SDK_DTYPE_F16;
+}
+
+int check_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return SDK_ERR_NO_DEVICE;
+  }
+  int major = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return SDK_ERR_NO_DEVICE;
+  }
+  return major == 10 ? SDK_OK : SDK_ERR_NO_DEVICE;
+}
+}  // namespace
+
+// Device address of this library's status word on the current device, looked
+// up once per device with that device current.
+unsigned int* device_status_ptr() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(g_status_mutex);
+  if (!g_status_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    g_status_ptr[dev] = static_cast<unsigned int*>(p);
+  }
+  return g_status_ptr[dev];
+}
+
+}  // namespace sdk
+
+using namespace sdk;
+
+extern "C" {
+
+int sdk_version(void) { return (0 << 16) | 1; }
+
+const char* sdk_status_string(int status) {
+  switch (status) {
+    case SDK_OK: return "ok";
+    case SDK_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case SDK_ERR_UNSUPPORTED: return "unsupported by this build's kernels";
+    case SDK_ERR_CUDA: return "CUDA error";
+    case SDK_ERR_NO_DEVICE: return "no sm_100 CUDA device is current";
+    default: return "unknown status";
+  }
+}
+
+const char* sdk_last_cuda_error(void) { return g_last_cuda_error; }
+
+int sdk_max_topk(int32_t dtype, int32_t d) {
+  if (!dtype_ok(dtype) || d <= 0) return 0;
+  return max_topk_generic(dtype, d);
+}
+
+int sdk_device_status(unsigned int* bits, int32_t clear, void* stream) {
+  if (!bits) return SDK_ERR_INVALID_ARGUMENT;
+  if (int rc = check_device()) return rc;
+  unsigned int* p = device_status_ptr();
+  if (!p) return record(cudaErrorInvalidSymbol);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int rc = record(cudaMemcpyAsync(bits, p, sizeof(unsigned int), cudaMemcpyDeviceToHost, st))) return rc;
+  if (clear)
+    if (int rc = record(cudaMemsetAsync(p, 0, sizeof(unsigned int), st))) return rc;
+  return record(cudaStreamSynchronize(st));
+}
+
+int sdk_topk_attn_fwd(const void* q, const void* k, const void* v, void* out, int32_t* top_idx, void* lse,
+                      void* top_scores, const int32_t* row_offsets, const int32_t* row_index, int64_t slices,
+                      int64_t n, int64_t m, int32_t d, int32_t dv, int32_t topk, double scale, int32_t score_grid,
+                      int32_t dtype, void* stream) {
+  if (!q || !k || !v || !out || !top_idx || !lse) return SDK_ERR_INVALID_ARGUMENT;
+  if (!dtype_ok(dtype) || slices <= 0 || n < 0 || m <= 0 || d <= 0 || dv <= 0) return SDK_ERR_INVALID_ARGUMENT;
+  if (topk < 1 || topk > m || m > 0x7ffffffe || !(scale > 0) || score_grid < 0) return SDK_ERR_INVALID_ARGUMENT;
+  if (int rc = check_device()) return rc;
+  if (topk > max_topk_generic(dtype, d)) return SDK_ERR_UNSUPPORTED;
+  FwdLaunch L{q, k, v, out, top_idx, lse, top_scores, row_offsets, row_index, slices, n, m, d, dv, topk,
+              scale, score_grid, dtype, device_status_ptr(), static_cast<cudaStream_t>(stream)};
+  if (fwd_tensorcore_supports(L)) return finish(fwd_tensorcore(L));
+  return finish(fwd_generic(L));
+}
+
+int sdk_topk_attn_bwd(const void* q, const void* k, const void* v, const void* dout, const int32_t* top_idx,
+                      const void* lse, void* dq, void* dk_acc, void* dv_acc, const int32_t* row_offsets,
+                      const int32_t* row_index, int64_t slices, int64_t n, int64_t m, int32_t d, int32_t dv,
+                      int32_t topk, double scale, int32_t score_grid, int32_t accumulate, int32_t dtype,
+                      void* stream) {
+  if (!q || !k || !v || !dout || !top_idx || !lse || !dq || !dk_acc || !dv_acc) return SDK_ERR_INVALID_ARGUMENT;
+  if (!dtype_ok(dtype) || slices <= 0 || n < 0 || m <= 0 || d <= 0 || dv <= 0) return SDK_ERR_INVALID_ARGUMENT;
+  if (topk < 1 || topk > m || !(scale > 0) || score_grid < 0) return SDK_ERR_INVALID_ARGUMENT;
+  if (int rc = check_device()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t acc_sz = dtype == SDK_DTYPE_F64 ? 8 : 4;
+  if (!accumulate) {
+    if (int rc = record(cudaMemsetAsync(dk_acc, 0, (size_t)slices * m * d * acc_sz, st))) return rc;
+    if (dv_acc != dk_acc)
+      if (int rc = record(cudaMemsetAsync(dv_acc, 0, (size_t)slices * m * dv * acc_sz, st))) return rc;
+  }
+  BwdLaunch L{q, k, v, dout, top_idx, lse, dq, dk_acc, dv_acc, row_offsets, row_index, slices, n, m, d, dv, topk,
+              scale, score_grid, dtype, device_status_ptr(), st};
+  return finish(bwd_sparse(L));
+}
+
+int sdk_finalize_grad(const void* acc, void* out, int64_t count, double multiplier, int32_t dtype, void* stream) {
+  if (!acc || !out || count < 0 || !dtype_ok(dtype)) return SDK_ERR_INVALID_ARGUMENT;
+  if (int rc = check_device()) return rc;
+  return finish(finalize_grad(acc, out, count, multiplier, dtype, static_cast<cudaStream_t>(stream)));
+}
+
+int sdk_affinity(const void* q, const void* k, float* scores, int64_t n, int64_t m, int32_t d, int64_t q_row_stride,
+                 int64_t k_row_stride, int32_t dtype, void* stream) {
+  if (!q || !k || !scores || n <= 0 || m <= 0 || d <= 0 || q_row_stride < d || k_row_stride < d)
+    return SDK_ERR_INVALID_ARGUMENT;
+  if (dtype != SDK_DTYPE_F32 && dtype != SDK_DTYPE_F16) return SDK_ERR_INVALID_ARGUMENT;
+  if (int rc = check_device()) return rc;
+  return finish(affinity(q, k, scores, n, m, d, q_row_stride, k_row_stride, dtype, static_cast<cudaStream_t>(stream)));
+}
+
+int sdk_topk_select(const void* scores, void* top_values, int64_t* top_idx, int64_t rows, int64_t m,
+                    int64_t row_stride, int32_t topk, int32_t dtype, void* stream) {
+  if (!scores || !top_values || !top_idx || rows <= 0 || m <= 0 || row_stride < m) return SDK_ERR_INVALID_ARGUMENT;
+  if (topk < 1 || topk > m || m > 0x7ffffffe) return SDK_ERR_INVALID_ARGUMENT;
+  if (dtype != SDK_DTYPE_F32 && dtype != SDK_DTYPE_F16) return SDK_ERR_INVALID_ARGUMENT;
+  if (int rc = check_device()) return rc;
+  return finish(topk_select(scores, top_values, top_idx, rows, m, row_stride, topk, dtype,
+                            static_cast<cudaStream_t>(stream)));
+}
+
+int sdk_topk_aggregate(const void* top_scores, const void* top_idx, const void* values, float* out, int64_t rows,
+                       int32_t topk, int64_t m, int32_t dv, int64_t score_row_stride, int64_t idx_row_stride,
+                       int64_t value_row_stride, int32_t score_dtype, int32_t idx_bits, int32_t value_dtype,
+                       void* stream) {
+  if (!top_scores || !top_idx || !values || !out || rows <= 0 || topk <= 0 || m <= 0 || dv <= 0)
+    return SDK_ERR_INVALID_ARGUMENT;
+  if (score_row_stride < topk || idx_row_stride < topk || value_row_stride < dv) return SDK_ERR_INVALID_ARGUMENT;
+  if (idx_bits != 32 && idx_bits != 64) return SDK_ERR_INVALID_ARGUMENT;
+  if (int rc = check_device()) return rc;
+  return finish(topk_aggregate(top_scores, top_idx, values, out, rows, topk, m, dv, score_row_stride,
+                               idx_row_stride, value_row_stride, score_dtype, idx_bits, value_dtype,
+                               device_status_ptr(), static_cast<cudaStream_t>(stream)));
+}
+
+int sdk_route_top1(const float* logits, int64_t n, int32_t experts, int32_t* expert, int32_t* order,
+                   int32_t* offsets, void* stream) {
+  if (!logits || !expert || !order || !offsets || n <= 0 || n > 0x7fffffff || experts <= 0)
+    return SDK_ERR_INVALID_ARGUMENT;
+  if (int rc = check_device()) return rc;
+  return finish(route_top1(logits, n, experts, expert, order, offsets, static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

@@ -1,0 +1,84 @@
+// Internal launch descriptors shared by the C ABI (capi.cu) and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace sdk {
+
+constexpr size_t kMaxDynamicSmem = 227 * 1024;
+
+inline int next_pow2_host(int x) {
+  int p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+struct FwdLaunch {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  int32_t* top_idx;
+  void* lse;
+  void* top_scores;
+  const int32_t* row_offsets;
+  const int32_t* row_index;
+  int64_t slices, n, m;
+  int d, dv, topk;
+  double scale;
+  int score_grid;
+  int dtype;
+  unsigned int* status;
+  cudaStream_t stream;
+};
+
+struct BwdLaunch {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* dout;
+  const int32_t* top_idx;
+  const void* lse;
+  void* dq;
+  void* dk_acc;
+  void* dv_acc;
+  const int32_t* row_offsets;
+  const int32_t* row_index;
+  int64_t slices, n, m;
+  int d, dv, topk;
+  double scale;
+  int score_grid;
+  int dtype;
+  unsigned int* status;
+  cudaStream_t stream;
+};
+
+// CUDA-core fused forward (fwd_generic.cu).
+int fwd_generic(const FwdLaunch& L);
+int max_topk_generic(int dtype, int d);
+
+// Tensor-core (tcgen05) bf16/fp16 forward (fwd_tc.cu); returns
+// SDK_ERR_UNSUPPORTED for shapes it does not take.
+int fwd_tensorcore(const FwdLaunch& L);
+bool fwd_tensorcore_supports(const FwdLaunch& L);
+
+// Sparse backward (bwd.cu).
+int bwd_sparse(const BwdLaunch& L);
+int finalize_grad(const void* acc, void* out, int64_t count, double multiplier, int dtype,
+                  cudaStream_t stream);
+
+// Stage ops (stages.cu).
+int affinity(const void* q, const void* k, float* scores, int64_t n, int64_t m, int d,
+             int64_t q_stride, int64_t k_stride, int dtype, cudaStream_t stream);
+int topk_select(const void* scores, void* top_values, int64_t* top_idx, int64_t rows, int64_t m,
+                int64_t row_stride, int topk, int dtype, cudaStream_t stream);
+int topk_aggregate(const void* top_scores, const void* top_idx, const void* values, float* out,
+                   int64_t rows, int topk, int64_t m, int dv, int64_t score_stride,
+                   int64_t idx_stride, int64_t value_stride, int score_dtype, int idx_bits,
+                   int value_dtype, unsigned int* status, cudaStream_t stream);
+int route_top1(const float* logits, int64_t n, int experts, int32_t* expert, int32_t* order,
+               int32_t* offsets, cudaStream_t stream);
+
+}  // namespace sdk

@@ -1,0 +1,279 @@
+// Stand-alone stage ops of the top-k attention path and the top-1 router.
+//
+//   affinity   dense scores = q·kᵀ (fp32), reference tiled_affinity
+//              (kernels/fused_topk_attn.py:227-287)
+//   select     per-row top-k of a score matrix, reference tiled_topk
+//              (kernels/fused_topk_attn.py:290-336)
+//   aggregate  softmax over selected scores and weighted gather of value
+//              rows, reference tiled_topk_aggregate
+//              (kernels/fused_topk_attn.py:339-408)
+//   route      top-1 expert per token and a stable grouping of tokens by
+//              expert (models/modules/router.py:139-145)
+#include "common.cuh"
+#include "kernels.h"
+
+namespace sdk {
+namespace {
+
+// ------------------------------------------------------------ affinity ---
+constexpr int A_BM = 64, A_BN = 64, A_FC = 16, A_NT = 256;
+
+template <typename T>
+__global__ void __launch_bounds__(A_NT) affinity_kernel(const T* __restrict__ q, const T* __restrict__ k,
+                                                        float* __restrict__ s, int64_t n, int64_t m, int d,
+                                                        int64_t qs, int64_t ks) {
+  __shared__ __align__(16) float Qs[A_FC][A_BM];
+  __shared__ __align__(16) float Ks[A_FC][A_BN];
+  const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+  const int64_t r0 = (int64_t)blockIdx.y * A_BM, c0 = (int64_t)blockIdx.x * A_BN;
+  float acc[4][4] = {};
+  for (int fc = 0; fc < d; fc += A_FC) {
+    for (int e = tid; e < A_BM * A_FC; e += A_NT) {
+      const int r = e / A_FC, f = e % A_FC;
+      Qs[f][r] = (r0 + r < n && fc + f < d) ? to_acc(q[(r0 + r) * qs + fc + f]) : 0.f;
+      Ks[f][r] = (c0 + r < m && fc + f < d) ? to_acc(k[(c0 + r) * ks + fc + f]) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int f = 0; f < A_FC; ++f) {
+      const float4 a = *reinterpret_cast<const float4*>(&Qs[f][4 * ty]);
+      const float4 b = *reinterpret_cast<const float4*>(&Ks[f][4 * tx]);
+      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t r = r0 + 4 * ty + i, c = c0 + 4 * tx + j;
+      if (r < n && c < m) s[r * m + c] = acc[i][j];
+    }
+}
+
+// -------------------------------------------------------------- select ---
+// One warp per row streams the row 32 keys at a time, keeps keys that beat
+// the running k-th best in a shared-memory list and re-ranks the list with a
+// warp bitonic sort when it could overflow.
+template <typename T>
+__global__ void select_kernel(const T* __restrict__ s, T* __restrict__ vals_out, int64_t* __restrict__ idx_out,
+                              int64_t rows, int64_t m, int64_t stride, int topk, int capp) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+  float* cv = reinterpret_cast<float*>(smem_raw) + warp * capp;
+  int* ci = reinterpret_cast<int*>(reinterpret_cast<float*>(smem_raw) + warps * capp) + warp * capp;
+  for (int64_t r = (int64_t)blockIdx.x * warps + warp; r < rows; r += (int64_t)gridDim.x * warps) {
+    const T* row = s + r * stride;
+    float tau = quiet_nan<float>();
+    int cnt = 0;
+    for (int64_t c0 = 0; c0 < m; c0 += kWarp) {
+      const int64_t c = c0 + lane;
+      const bool ok = c < m;
+      const float x = ok ? to_acc(row[c]) : 0.f;
+      const bool pass = ok && !(x <= tau);
+      const unsigned b = __ballot_sync(0xffffffffu, pass);
+      if (pass) {
+        const int pos = cnt + __popc(b & ((1u << lane) - 1u));
+        cv[pos] = x;
+        ci[pos] = (int)c;
+      }
+      cnt += __popc(b);
+      __syncwarp();
+      if (cnt > capp - kWarp) {
+        const int P = next_pow2_dev(cnt);
+        for (int i = cnt + lane; i < P; i += kWarp) { cv[i] = neg_inf<float>(); ci[i] = kPadIndex; }
+        __syncwarp();
+        warp_bitonic_sort(cv, ci, P, lane);
+        cnt = topk;
+        tau = cv[topk - 1];
+      }
+    }
+    const int P = next_pow2_dev(cnt);
+    for (int i = cnt + lane; i < P; i += kWarp) { cv[i] = neg_inf<float>(); ci[i] = kPadIndex; }
+    __syncwarp();
+    warp_bitonic_sort(cv, ci, P, lane);
+    for (int j = lane; j < topk; j += kWarp) {
+      vals_out[r * topk + j] = from_acc<T>(cv[j]);
+      idx_out[r * topk + j] = ci[j];
+    }
+    __syncwarp();
+  }
+}
+
+// ----------------------------------------------------------- aggregate ---
+template <typename TS, typename TI, typename TV>
+__global__ void aggregate_kernel(const TS* __restrict__ ts, const TI* __restrict__ ti, const TV* __restrict__ vals,
+                                 float* __restrict__ out, int64_t rows, int topk, int64_t m, int dv,
+                                 int64_t ss, int64_t is, int64_t vs, unsigned int* status) {
+  const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+  for (int64_t r = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); r < rows; r += (int64_t)gridDim.x * warps) {
+    const TS* srow = ts + r * ss;
+    const TI* irow = ti + r * is;
+    float mx = neg_inf<float>();
+    for (int j = lane; j < topk; j += kWarp) mx = fmaxf(mx, to_acc(srow[j]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float total = 0.f;
+    for (int j = lane; j < topk; j += kWarp) total += expf(to_acc(srow[j]) - mx);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+    for (int f0 = 0; f0 < dv; f0 += kWarp) {
+      const int f = f0 + lane;
+      float acc = 0.f;
+      for (int j = 0; j < topk; ++j) {
+        const int64_t key = (int64_t)irow[j];
+        if (key < 0 || key >= m) {
+          if (lane == 0 && f0 == 0) raise_device_status(status, kStatusIndexOutOfRange);
+          continue;
+        }
+        const float w = expf(to_acc(srow[j]) - mx) / total;
+        if (f < dv) acc = fmaf(w, to_acc(vals[key * vs + f]), acc);
+      }
+      if (f < dv) out[r * dv + f] = acc;
+    }
+  }
+}
+
+// --------------------------------------------------------------- route ---
+constexpr int R_NT = 512, R_MAXE = 16;
+
+__global__ void __launch_bounds__(R_NT) route_kernel(const float* __restrict__ logits, int64_t n, int experts,
+                                                     int32_t* __restrict__ expert, int32_t* __restrict__ order,
+                                                     int32_t* __restrict__ offsets) {
+  __shared__ int counts[R_MAXE][R_NT];
+  __shared__ int totals[R_MAXE + 1];
+  const int t = threadIdx.x;
+  const int64_t per = (n + R_NT - 1) / R_NT;
+  const int64_t b = t * per, e = b + per < n ? b + per : n;
+  int local[R_MAXE];
+#pragma unroll
+  for (int x = 0; x < R_MAXE; ++x) local[x] = 0;
+  for (int64_t i = b; i < e; ++i) {
+    const float* row = logits + i * experts;
+    int best = 0;
+    float bv = row[0];
+    for (int x = 1; x < experts; ++x)
+      if (ranks_above(row[x], x, bv, best)) { bv = row[x]; best = x; }
+    expert[i] = best;
+#pragma unroll
+    for (int x = 0; x < R_MAXE; ++x) local[x] += (x == best);
+  }
+#pragma unroll
+  for (int x = 0; x < R_MAXE; ++x) counts[x][t] = local[x];
+  __syncthreads();
+  if (t < experts) {  // serial exclusive scan of one expert's per-thread counts
+    int run = 0;
+    for (int u = 0; u < R_NT; ++u) { const int c = counts[t][u]; counts[t][u] = run; run += c; }
+    totals[t] = run;
+  }
+  __syncthreads();
+  if (t == 0) {
+    int run = 0;
+    for (int x = 0; x < experts; ++x) { const int c = totals[x]; totals[x] = run; offsets[x] = run; run += c; }
+    offsets[experts] = run;
+  }
+  __syncthreads();
+  int cursor[R_MAXE];
+#pragma unroll
+  for (int x = 0; x < R_MAXE; ++x) cursor[x] = (x < experts) ? totals[x] + counts[x][t] : 0;
+  for (int64_t i = b; i < e; ++i) {
+    const int x = expert[i];
+#pragma unroll
+    for (int y = 0; y < R_MAXE; ++y)
+      if (y == x) order[cursor[y]++] = (int32_t)i;
+  }
+}
+
+template <typename TS, typename TI>
+int aggregate_v(const void* ts, const void* ti, const void* v, float* out, int64_t rows, int topk, int64_t m,
+                int dv, int64_t ss, int64_t is, int64_t vs, int vdt, unsigned int* status, cudaStream_t st,
+                unsigned grid) {
+  if (vdt == SDK_DTYPE_F32)
+    aggregate_kernel<TS, TI, float><<<grid, 128, 0, st>>>(static_cast<const TS*>(ts), static_cast<const TI*>(ti),
+                                                         static_cast<const float*>(v), out, rows, topk, m, dv,
+                                                         ss, is, vs, status);
+  else if (vdt == SDK_DTYPE_F16)
+    aggregate_kernel<TS, TI, __half><<<grid, 128, 0, st>>>(static_cast<const TS*>(ts), static_cast<const TI*>(ti),
+                                                          static_cast<const __half*>(v), out, rows, topk, m, dv,
+                                                          ss, is, vs, status);
+  else
+    return SDK_ERR_INVALID_ARGUMENT;
+  return SDK_OK;
+}
+
+}  // namespace
+
+int affinity(const void* q, const void* k, float* scores, int64_t n, int64_t m, int d, int64_t qs, int64_t ks,
+             int dtype, cudaStream_t stream) {
+  const dim3 grid((unsigned)((m + A_BN - 1) / A_BN), (unsigned)((n + A_BM - 1) / A_BM));
+  if (grid.y > 65535u) return SDK_ERR_UNSUPPORTED;
+  if (dtype == SDK_DTYPE_F32)
+    affinity_kernel<float><<<grid, A_NT, 0, stream>>>(static_cast<const float*>(q), static_cast<const float*>(k),
+                                                       scores, n, m, d, qs, ks);
+  else if (dtype == SDK_DTYPE_F16)
+    affinity_kernel<__half><<<grid, A_NT, 0, stream>>>(static_cast<const __half*>(q), static_cast<const __half*>(k),
+                                                        scores, n, m, d, qs, ks);
+  else
+    return SDK_ERR_INVALID_ARGUMENT;
+  return cudaPeekAtLastError() == cudaSuccess ? SDK_OK : SDK_ERR_CUDA;
+}
+
+int topk_select(const void* scores, void* top_values, int64_t* top_idx, int64_t rows, int64_t m, int64_t stride,
+                int topk, int dtype, cudaStream_t stream) {
+  const int capp = next_pow2_host(topk + kWarp);
+  int warps = 4;
+  while (warps > 1 && (size_t)warps * capp * 8 > kMaxDynamicSmem) warps >>= 1;
+  const size_t smem = (size_t)warps * capp * 8;
+  if (smem > kMaxDynamicSmem) return SDK_ERR_UNSUPPORTED;
+  const int64_t want = (rows + warps - 1) / warps;
+  const unsigned grid = (unsigned)(want < 148 * 64 ? want : 148 * 64);
+  if (dtype == SDK_DTYPE_F32) {
+    auto kern = select_kernel<float>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return SDK_ERR_CUDA;
+    kern<<<grid, warps * kWarp, smem, stream>>>(static_cast<const float*>(scores), static_cast<float*>(top_values),
+                                                top_idx, rows, m, stride, topk, capp);
+  } else if (dtype == SDK_DTYPE_F16) {
+    auto kern = select_kernel<__half>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return SDK_ERR_CUDA;
+    kern<<<grid, warps * kWarp, smem, stream>>>(static_cast<const __half*>(scores), static_cast<__half*>(top_values),
+                                                top_idx, rows, m, stride, topk, capp);
+  } else {
+    return SDK_ERR_INVALID_ARGUMENT;
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? SDK_OK : SDK_ERR_CUDA;
+}
+
+int topk_aggregate(const void* ts, const void* ti, const void* v, float* out, int64_t rows, int topk, int64_t m,
+                   int dv, int64_t ss, int64_t is, int64_t vs, int sdt, int idx_bits, int vdt, unsigned int* status,
+                   cudaStream_t stream) {
+  const int64_t want = (rows + 3) / 4;
+  const unsigned grid = (unsigned)(want < 148 * 64 ? want : 148 * 64);
+  int rc;
+  if (sdt == SDK_DTYPE_F32 && idx_bits == 32)
+    rc = aggregate_v<float, int32_t>(ts, ti, v, out, rows, topk, m, dv, ss, is, vs, vdt, status, stream, grid);
+  else if (sdt == SDK_DTYPE_F32 && idx_bits == 64)
+    rc = aggregate_v<float, int64_t>(ts, ti, v, out, rows, topk, m, dv, ss, is, vs, vdt, status, stream, grid);
+  else if (sdt == SDK_DTYPE_F16 && idx_bits == 32)
+    rc = aggregate_v<__half, int32_t>(ts, ti, v, out, rows, topk, m, dv, ss, is, vs, vdt, status, stream, grid);
+  else if (sdt == SDK_DTYPE_F16 && idx_bits == 64)
+    rc = aggregate_v<__half, int64_t>(ts, ti, v, out, rows, topk, m, dv, ss, is, vs, vdt, status, stream, grid);
+  else
+    return SDK_ERR_INVALID_ARGUMENT;
+  if (rc != SDK_OK) return rc;
+  return cudaPeekAtLastError() == cudaSuccess ? SDK_OK : SDK_ERR_CUDA;
+}
+
+int route_top1(const float* logits, int64_t n, int experts, int32_t* expert, int32_t* order, int32_t* offsets,
+               cudaStream_t stream) {
+  if (experts < 1 || experts > R_MAXE) return SDK_ERR_UNSUPPORTED;
+  route_kernel<<<1, R_NT, 0, stream>>>(logits, n, experts, expert, order, offsets);
+  return cudaPeekAtLastError() == cudaSuccess ? SDK_OK : SDK_ERR_CUDA;
+}
+
+}  // namespace sdk

@@ -1,0 +1,73 @@
+"""The C-ABI library loads on a CPU-only machine and exports every declared
+entry point; argument checks answer without touching a GPU."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from sparsedict_b200 import _native
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared_symbols():
+    names = set()
+    for header in (ROOT / "include").glob("*.h"):
+        text = header.read_text()
+        names.update(re.findall(r"^\s*(?:const\s+)?[a-z_0-9]+\**\s+\**(sdk_[a-z0-9_]+)\(", text, re.M))
+    return sorted(names)
+
+
+def test_header_declares_the_entry_points():
+    names = declared_symbols()
+    for required in ("sdk_topk_attn_fwd", "sdk_topk_attn_bwd", "sdk_topk_select", "sdk_topk_aggregate",
+                     "sdk_affinity", "sdk_status_string", "sdk_device_status"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(str(_native.LIB_PATH))
+    missing = [n for n in declared_symbols() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_binding_covers_every_declared_symbol():
+    assert sorted(_native.SIGNATURES) == declared_symbols()
+
+
+def test_status_strings_and_version():
+    lib = _native.load()
+    assert lib.sdk_version() >= 1
+    assert lib.sdk_status_string(0) == b"ok"
+    assert b"invalid" in lib.sdk_status_string(1)
+    assert lib.sdk_status_string(99) == b"unknown status"
+
+
+def test_invalid_arguments_are_rejected_before_any_device_work():
+    lib = _native.load()
+    # null tensors
+    rc = lib.sdk_topk_attn_fwd(None, None, None, None, None, None, None, None, None,
+                               1, 4, 8, 16, 16, 2, 0.25, 0, 0, None)
+    assert rc == _native.SDK_ERR_INVALID_ARGUMENT
+    # k > m and bad dtype with non-null pointers (never dereferenced)
+    fake = 0x1000
+    rc = lib.sdk_topk_attn_fwd(fake, fake, fake, fake, fake, fake, None, None, None,
+                               1, 4, 8, 16, 16, 9, 0.25, 0, 0, None)
+    assert rc == _native.SDK_ERR_INVALID_ARGUMENT
+    rc = lib.sdk_topk_attn_fwd(fake, fake, fake, fake, fake, fake, None, None, None,
+                               1, 4, 8, 16, 16, 2, 0.25, 0, 7, None)
+    assert rc == _native.SDK_ERR_INVALID_ARGUMENT
+    rc = lib.sdk_topk_select(fake, fake, fake, 4, 8, 4, 2, 0, None)  # row stride < m
+    assert rc == _native.SDK_ERR_INVALID_ARGUMENT
+    rc = lib.sdk_topk_aggregate(fake, fake, fake, fake, 4, 2, 8, 16, 2, 2, 16, 0, 48, 0, None)
+    assert rc == _native.SDK_ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("dtype", [0, 1, 2, 3])
+def test_max_topk_covers_the_benchmark_configurations(dtype):
+    lib = _native.load()
+    assert lib.sdk_max_topk(dtype, 64) >= 64
+    assert lib.sdk_max_topk(dtype, 128) >= 128
+    assert lib.sdk_max_topk(9, 64) == 0

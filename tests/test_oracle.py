@@ -189,3 +189,18 @@ def test_gap_aware_mismatch_counter():
     scores = np.array([[5.0, 4.0, 3.99999, 1.0]], dtype=np.float32)
     assert oracle.gap_aware_index_mismatches(np.array([[0, 2]]), np.array([[0, 1]]), scores, 1e-4) == 0
     assert oracle.gap_aware_index_mismatches(np.array([[0, 3]]), np.array([[0, 1]]), scores, 1e-4) == 1
+
+
+def test_partition_top_k_matches_lexsort_order():
+    from oracle.topk_attention import _topk_order_partition
+
+    rng = np.random.default_rng(12)
+    for dist in ("ints", "floats"):
+        x = rng.integers(-4, 5, size=(30, 300)).astype(np.float32) if dist == "ints" else \
+            rng.standard_normal((30, 300)).astype(np.float32)
+        x[4, :50] = -np.inf
+        for k in (1, 7, 64, 299, 300):
+            v1, i1 = _topk_order_partition(x, k, x.shape)
+            nan, value = np.isnan(x), x
+            order = np.lexsort((np.broadcast_to(np.arange(300), x.shape), -value.astype(np.float64), ~nan), axis=-1)
+            assert np.array_equal(i1, order[:, :k])

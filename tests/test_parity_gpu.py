@@ -1,0 +1,439 @@
+"""GPU parity of the CUDA path against the reference's golden vectors and the
+CPU oracle.  Mirrors the reference's own GPU tests
+(tests/test_triton_autograd.py, tests/test_hybrid_topk.py,
+tests/test_fused_topk_attn.py) and adds bf16, tie-stress, routed and
+full-size sampled-row cases.
+
+Tolerances: fp32 outputs atol 1e-5 (reference pins) and gradients atol 1e-4 /
+rtol 1e-3; fp64 atol 1e-9; bf16 rtol 2e-2.  Indices are compared exactly; on
+non-quantised fp32 data a difference is accepted only between keys whose
+oracle scores lie within 1e-5 of the k-th selected score (two summation
+orders can swap a true near-tie).
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from sparsedict_b200 import (
+    FusedTopKAttentionFunction,
+    _native,
+    fused_topk_attention,
+    hybrid_topk_attention,
+    tiled_affinity,
+    tiled_topk,
+    tiled_topk_aggregate,
+)
+from sparsedict_b200.kernels.hybrid_topk import _hybrid_topk_attention_with_aux
+from sparsedict_b200.routed import routed_dictionary_attention
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _t(x, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(x)).to(DEV)
+    return t.to(dtype) if dtype is not None else t
+
+
+def _flat(x):
+    return x.reshape(-1, *x.shape[-2:])
+
+
+def _oracle_scores64(q, k, scale):
+    return np.einsum("bnd,bmd->bnm", _flat(q).astype(np.float64), _flat(k).astype(np.float64)) * scale
+
+
+def _assert_indices(actual, expected, scores, tol=1e-5):
+    bad = oracle.gap_aware_index_mismatches(actual, expected, scores, tol)
+    assert bad == 0, f"{bad} rows select different keys"
+
+
+# --- compile smoke -----------------------------------------------------------
+
+
+def test_compile_smoke_fp32():
+    torch.manual_seed(1234)
+    q = torch.randn(1, 1, 512, 32, device=DEV)
+    k = torch.randn(1, 1, 256, 32, device=DEV)
+    v = torch.randn(1, 1, 256, 24, device=DEV)
+    out = fused_topk_attention(q, k, v, 16)
+    assert out.shape == (1, 1, 512, 24)
+    assert torch.isfinite(out).all()
+
+
+# --- forward parity against the reference's outputs --------------------------
+
+
+@pytest.mark.parametrize("grid", [(1, 13, 1, 24), (7, 64, 5, 67), (65, 129, 17, 33), (3, 73, 73, 7)])
+def test_forward_parity_fp32(golden, grid):
+    tag = "grid_%d_%d_%d_%d" % grid
+    q, k, v = (golden[f"{tag}_{n}"] for n in "qkv")
+    out = fused_topk_attention(_t(q), _t(k), _t(v), grid[2])
+    np.testing.assert_allclose(out.cpu().numpy(), golden[f"{tag}_out"], atol=1e-5, rtol=0)
+
+
+def test_forward_parity_fp32_large_grid(golden):
+    torch.manual_seed(1234)
+    q = torch.randn(1, 1, 4096, 64)
+    k = torch.randn(1, 1, 256, 64)
+    v = torch.randn(1, 1, 256, 64)
+    out = fused_topk_attention(q.to(DEV), k.to(DEV), v.to(DEV), 16)
+    tag = "grid_4096_256_16_64"
+    np.testing.assert_allclose(out.cpu().numpy()[..., ::8, :], golden[f"{tag}_out_rows8"], atol=1e-5, rtol=0)
+    _, idx, _, _ = _hybrid_topk_attention_with_aux(q.to(DEV), k.to(DEV), v.to(DEV), 16, 1 / 8)
+    _assert_indices(idx.cpu().numpy(), _flat(golden[f"{tag}_idx"]), _oracle_scores64(q.numpy(), k.numpy(), 1 / 8))
+
+
+def test_forward_parity_fp64(golden):
+    q, k, v = (_t(golden[f"f64fwd_{n}"]) for n in "qkv")
+    out = fused_topk_attention(q, k, v, 5)
+    assert out.dtype == torch.float64
+    np.testing.assert_allclose(out.cpu().numpy(), golden["f64fwd_out"], atol=1e-9, rtol=0)
+
+
+def test_configuration_1_forward_backward(golden):
+    g = {k[5:]: v for k, v in golden.items() if k.startswith("cfg1_")}
+    q, k, v = (_t(g[n]).requires_grad_(True) for n in "qkv")
+    out = fused_topk_attention(q, k, v, 8)
+    np.testing.assert_allclose(out.detach().cpu().numpy(), g["out"], atol=1e-5, rtol=0)
+    dq, dk, dv = torch.autograd.grad((out * _t(g["do"])).sum(), (q, k, v))
+    for got, name in ((dq, "dq"), (dk, "dk"), (dv, "dv")):
+        np.testing.assert_allclose(got.cpu().numpy(), g[name], atol=1e-4, rtol=1e-3)
+    scale = 1 / math.sqrt(32)
+    _, idx, _, _ = _hybrid_topk_attention_with_aux(q.detach(), k.detach(), v.detach(), 8, scale)
+    _assert_indices(idx.cpu().numpy(), _flat(g["idx"]), _oracle_scores64(g["q"], g["k"], scale))
+
+
+# --- gradients ---------------------------------------------------------------
+
+
+@pytest.mark.parametrize(("n", "m", "k", "dk", "dv"), [(8, 12, 5, 4, 3), (16, 32, 8, 8, 8)])
+def test_gradcheck_fp64(n, m, k, dk, dv):
+    torch.manual_seed(7)
+    q = torch.randn(1, 1, n, dk, dtype=torch.float64, device=DEV, requires_grad=True)
+    kk = torch.randn(1, 1, m, dk, dtype=torch.float64, device=DEV, requires_grad=True)
+    v = torch.randn(1, 1, m, dv, dtype=torch.float64, device=DEV, requires_grad=True)
+    torch.autograd.gradcheck(fused_topk_attention, (q, kk, v, k), eps=1e-6, atol=1e-4, nondet_tol=1e-5)
+
+
+def test_forward_saves_inputs_support_indices_and_lse_only():
+    torch.manual_seed(1234)
+    q = torch.randn(1, 1, 8, 4, dtype=torch.float64, device=DEV, requires_grad=True)
+    k = torch.randn(1, 1, 12, 4, dtype=torch.float64, device=DEV, requires_grad=True)
+    v = torch.randn(1, 1, 12, 3, dtype=torch.float64, device=DEV, requires_grad=True)
+    saved = []
+
+    def pack(t):
+        saved.append((tuple(t.shape), t.dtype))
+        return t
+
+    with torch.autograd.graph.saved_tensors_hooks(pack, lambda t: t):
+        fused_topk_attention(q, k, v, 5)
+    assert saved == [
+        ((1, 8, 4), torch.float64),
+        ((1, 12, 4), torch.float64),
+        ((1, 12, 3), torch.float64),
+        ((1, 8, 5), torch.int32),
+        ((1, 8), torch.float64),
+    ]
+
+
+def test_backward_matches_reference_autograd_fp64(golden):
+    g = {k[7:]: v for k, v in golden.items() if k.startswith("f64bwd_")}
+    q, k, v = (_t(g[n]).requires_grad_(True) for n in "qkv")
+    out = fused_topk_attention(q, k, v, 7)
+    grads = torch.autograd.grad((out * _t(g["do"])).sum(), (q, k, v))
+    for got, name in zip(grads, ("dq", "dk", "dv")):
+        err = np.abs(got.cpu().numpy() - g[name]).max()
+        assert err < 1e-9, f"{name} max abs err {err}"
+
+
+def test_dq_is_bitwise_deterministic():
+    torch.manual_seed(11)
+    q = torch.randn(2, 2, 300, 64, device=DEV, requires_grad=True)
+    k = torch.randn(2, 2, 700, 64, device=DEV)
+    v = torch.randn(2, 2, 700, 64, device=DEV)
+    do = torch.randn(2, 2, 300, 64, device=DEV)
+    g1 = torch.autograd.grad((fused_topk_attention(q, k, v, 16) * do).sum(), q)[0]
+    g2 = torch.autograd.grad((fused_topk_attention(q, k, v, 16) * do).sum(), q)[0]
+    assert torch.equal(g1, g2)
+
+
+# --- edge cases ---------------------------------------------------------------
+
+
+def _oracle_out(q, k, v, topk, temperature=1.0):
+    scale = oracle.score_scale(q.shape[-1], temperature)
+    o, idx, lse, _ = oracle.topk_attention_forward(_flat(q), _flat(k), _flat(v), topk, scale)
+    return o.reshape(*q.shape[:-1], v.shape[-1]), idx
+
+
+def test_full_width_k_equals_m_fp32():
+    torch.manual_seed(1234)
+    q, k, v = torch.randn(1, 1, 32, 8), torch.randn(1, 1, 32, 8), torch.randn(1, 1, 32, 5)
+    out = fused_topk_attention(q.to(DEV), k.to(DEV), v.to(DEV), 32)
+    expected, _ = _oracle_out(q.numpy(), k.numpy(), v.numpy(), 32)
+    np.testing.assert_allclose(out.cpu().numpy(), expected, atol=1e-5, rtol=0)
+
+
+def test_single_key_for_64_dimensional_head():
+    torch.manual_seed(1234)
+    q, k, v = torch.randn(1, 1, 64, 64), torch.randn(1, 1, 1, 64), torch.randn(1, 1, 1, 3)
+    out = fused_topk_attention(q.to(DEV), k.to(DEV), v.to(DEV), 1)
+    expected, _ = _oracle_out(q.numpy(), k.numpy(), v.numpy(), 1)
+    np.testing.assert_allclose(out.cpu().numpy(), expected, atol=1e-5, rtol=0)
+
+
+def test_padded_candidates_zero_mass():
+    torch.manual_seed(1234)
+    q, k, v = (torch.randn(1, 1, 8, 4, device=DEV), torch.randn(1, 1, 5, 4, device=DEV),
+               torch.randn(1, 1, 5, 4, device=DEV))
+    assert torch.isfinite(fused_topk_attention(q, k, v, 2)).all()
+
+
+@pytest.mark.parametrize("temperature", [0.5, 2.0])
+def test_temperature_scales_scores(temperature):
+    torch.manual_seed(3)
+    q, k, v = torch.randn(2, 1, 50, 16), torch.randn(2, 1, 90, 16), torch.randn(2, 1, 90, 8)
+    out = fused_topk_attention(q.to(DEV), k.to(DEV), v.to(DEV), 7, temperature)
+    expected, _ = _oracle_out(q.numpy(), k.numpy(), v.numpy(), 7, temperature)
+    np.testing.assert_allclose(out.cpu().numpy(), expected, atol=1e-5, rtol=0)
+
+
+def test_ties_and_minus_inf_rows_follow_the_reference_order():
+    # exact ties everywhere: integer-valued keys and a one-hot query
+    q = torch.zeros(1, 1, 4, 4)
+    q[..., 0] = 1.0
+    k = torch.tensor([[3.0, 1, 3, 2, 3, 0, 2, 3, 1]]).T.repeat(1, 4).reshape(1, 1, 9, 4)
+    v = torch.arange(9 * 2, dtype=torch.float32).reshape(1, 1, 9, 2)
+    _, idx, _, _ = _hybrid_topk_attention_with_aux(q.to(DEV), k.to(DEV), v.to(DEV), 5, 1.0)
+    assert idx[0, 0].tolist() == [0, 2, 4, 7, 3]
+
+
+# --- hybrid ------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 7, 129, 8, 5, 7), (2, 2, 5, 263, 16, 33, 11)])
+def test_hybrid_forward_matches_reference(golden, shape):
+    tag = "hyb_" + "_".join(map(str, shape))
+    q, k, v = (_t(golden[f"{tag}_{n}"]) for n in "qkv")
+    out = hybrid_topk_attention(q, k, v, shape[-1])
+    assert out.shape == (shape[0], shape[1], shape[2], shape[5])
+    np.testing.assert_allclose(out.cpu().numpy(), golden[f"{tag}_out"], atol=1e-5, rtol=0)
+
+
+def test_hybrid_custom_autograd_matches_reference(golden):
+    g = {k[8:]: v for k, v in golden.items() if k.startswith("hybgrad_")}
+    q, k, v = (_t(g[n]).requires_grad_(True) for n in "qkv")
+    out = fused_topk_attention(q, k, v, 5)
+    grads = torch.autograd.grad((out * _t(g["do"])).sum(), (q, k, v))
+    np.testing.assert_allclose(out.detach().cpu().numpy(), g["out"], atol=1e-5, rtol=0)
+    for got, name in zip(grads, ("dq", "dk", "dv")):
+        np.testing.assert_allclose(got.cpu().numpy(), g[name], atol=1e-4, rtol=0)
+
+
+def test_hybrid_aux_layout_and_lse():
+    torch.manual_seed(5)
+    q, k, v = torch.randn(2, 3, 40, 16), torch.randn(2, 3, 200, 16), torch.randn(2, 3, 200, 12)
+    ts, ti, lse, out = _hybrid_topk_attention_with_aux(q.to(DEV), k.to(DEV), v.to(DEV), 9, 0.25)
+    assert ts.shape == (6, 40, 9) and ts.dtype == torch.float32
+    assert ti.shape == (6, 40, 9) and ti.dtype == torch.int32
+    assert lse.shape == (6, 40) and out.shape == (6, 40, 12)
+    o, idx, l, s = oracle.topk_attention_forward(_flat(q.numpy()), _flat(k.numpy()), _flat(v.numpy()), 9, 0.25)
+    np.testing.assert_allclose(ts.cpu().numpy(), s, atol=1e-5, rtol=0)
+    np.testing.assert_allclose(lse.cpu().numpy(), l, atol=1e-5, rtol=0)
+    np.testing.assert_allclose(out.cpu().numpy(), o, atol=1e-5, rtol=0)
+    with pytest.raises(ValueError, match="hybrid selector requires"):
+        _hybrid_topk_attention_with_aux(q.to(DEV), k.to(DEV), v.to(DEV), 200, 0.25)
+
+
+# --- stage ops -----------------------------------------------------------------
+
+
+def test_tiled_affinity_matches_torch_fp16():
+    torch.manual_seed(0)
+    q = torch.randn(67, 24, device=DEV, dtype=torch.float16)
+    k = torch.randn(129, 24, device=DEV, dtype=torch.float16)
+    out = tiled_affinity(q, k)
+    assert out.shape == (67, 129)
+    assert torch.allclose(out, q.float() @ k.float().T, atol=1e-2, rtol=1e-2)
+
+
+def test_tiled_affinity_fp32_strided_rows():
+    torch.manual_seed(1)
+    base = torch.randn(70, 48, device=DEV)
+    q = base[:, :40]
+    k = torch.randn(130, 40, device=DEV)
+    out = tiled_affinity(q, k)
+    np.testing.assert_allclose(out.cpu().numpy(), q.cpu().double().numpy() @ k.cpu().double().numpy().T,
+                               atol=1e-4, rtol=1e-5)
+
+
+@pytest.mark.parametrize("case", [(1, 1, 1), (7, 64, 5), (65, 129, 17), (8, 256, 64), (3, 73, 73)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_tiled_topk_matches_torch_topk_indices(golden, case, dtype):
+    tag = "topk_%d_%d_%d" % case
+    vals, idx = tiled_topk(_t(golden[f"{tag}_scores"]).to(dtype), case[2])
+    assert torch.equal(idx.cpu(), torch.from_numpy(golden[f"{tag}_idx"]))
+    assert torch.equal(vals.cpu().float(), torch.from_numpy(golden[f"{tag}_vals"]))
+    assert vals.dtype == dtype and idx.dtype == torch.int64
+
+
+def test_tiled_topk_ties_and_nan_order():
+    s = torch.tensor([[1.0, 3.0, 3.0, float("nan"), 2.0, 3.0, float("nan"), -float("inf")]], device=DEV)
+    vals, idx = tiled_topk(s, 6)
+    assert idx.tolist() == [[3, 6, 1, 2, 5, 4]]
+    big = torch.randint(-2, 3, (40, 700), device=DEV).float()
+    _, idx2 = tiled_topk(big, 65)
+    _, exp_idx = oracle.topk_order(big.cpu().numpy(), 65)
+    assert np.array_equal(idx2.cpu().numpy(), exp_idx)
+
+
+@pytest.mark.parametrize("case", [(1, 13, 1, 24), (7, 64, 5, 67), (65, 129, 17, 33), (3, 73, 73, 7)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_tiled_topk_aggregate_matches_torch_reference(golden, case, dtype):
+    tag = "agg_%d_%d_%d_%d" % case
+    ts = _t(golden[f"{tag}_ts"]).to(dtype)
+    ti = _t(golden[f"{tag}_ti"])
+    vals = _t(golden[f"{tag}_values"]).to(dtype)
+    out = tiled_topk_aggregate(ts, ti, vals)
+    assert out.shape == (case[0], case[3]) and out.dtype == torch.float32
+    w = torch.softmax(ts.float(), dim=1)
+    expected = torch.sum(w.unsqueeze(-1) * vals.float()[ti], dim=1)
+    assert (out - expected).abs().max().item() <= 1e-5
+    if dtype == torch.float32:
+        np.testing.assert_allclose(out.cpu().numpy(), golden[f"{tag}_out"], atol=1e-5, rtol=0)
+    out32 = tiled_topk_aggregate(ts, ti.int(), vals)
+    assert torch.equal(out, out32)
+
+
+def test_aggregate_flags_out_of_range_indices():
+    _native.device_status(clear=True)
+    ts = torch.zeros(2, 3, device=DEV)
+    ti = torch.tensor([[0, 1, 2], [0, 1, 9]], device=DEV)
+    vals = torch.ones(4, 5, device=DEV)
+    out = tiled_topk_aggregate(ts, ti, vals)
+    assert _native.device_status(clear=True) & 1
+    assert torch.allclose(out[0], torch.ones(5, device=DEV))
+    assert torch.allclose(out[1], torch.full((5,), 2 / 3, device=DEV))
+
+
+# --- bf16 / fp16 -------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_low_precision_forward_backward_vs_oracle(dtype):
+    torch.manual_seed(21)
+    b, h, n, m, d, k = 2, 2, 384, 1000, 64, 32
+    q, kk, v, do = (torch.randn(b, h, x, d) for x in (n, m, m, n))
+    qd, kd, vd = (t.to(DEV, dtype).requires_grad_(True) for t in (q, kk, v))
+    dod = do.to(DEV, dtype)
+    out = fused_topk_attention(qd, kd, vd, k)
+    assert out.dtype == dtype
+    grads = torch.autograd.grad((out.float() * dod.float()).sum(), (qd, kd, vd))
+    qr, kr, vr, dor = (t.detach().float().cpu().numpy() for t in (qd, kd, vd, dod))
+    scale = 1 / 8
+    o, idx, _, _ = oracle.topk_attention_forward(_flat(qr), _flat(kr), _flat(vr), k, scale)
+    from sparsedict_b200 import _ops
+
+    _, gidx, _, _ = _ops.topk_attn_fwd(*(t.detach().reshape(b * h, -1, d) for t in (qd, kd, vd)), k, scale)
+    gidx = gidx.cpu().numpy().reshape(idx.shape)
+    # selected sets agree wherever the affinity gap exceeds bf16 rounding (here: 1e-4)
+    _assert_indices(gidx, idx, _oracle_scores64(qr, kr, scale), tol=1e-4)
+    np.testing.assert_allclose(out.float().detach().cpu().numpy().reshape(o.shape), o, rtol=2e-2, atol=2e-2)
+    # backward checked on the support the GPU selected
+    ref = oracle.topk_attention_backward(_flat(qr), _flat(kr), _flat(vr), gidx, _flat(dor), scale)
+    for got, exp in zip(grads, ref):
+        got = got.float().cpu().numpy().reshape(exp.shape)
+        assert np.abs(got - exp).max() <= 2e-2 * max(1.0, np.abs(exp).max())
+
+
+# --- tie stress (configuration 5 shape family, reduced size) ----------------------
+
+
+def _grid_inputs(seed, bh, n, m, d):
+    rng = np.random.default_rng(seed)
+    q = np.clip(np.round(rng.standard_normal((bh, n, d)) * 8) / 8, -4, 4).astype(np.float32)
+    k = np.clip(np.round(rng.standard_normal((bh, m, d)) * 8) / 8, -4, 4).astype(np.float32)
+    v = rng.standard_normal((bh, m, d)).astype(np.float32)
+    do = rng.standard_normal((bh, n, d)).astype(np.float32)
+    return q, k, v, do
+
+
+@pytest.mark.parametrize("topk", [1, 128])
+def test_tie_stress_grid_indices_bit_exact(topk):
+    bh, n, m, d = 4, 512, 1024, 128
+    q, k, v, do = _grid_inputs(17 + topk, bh, n, m, d)
+    qd, kd, vd = (_t(x.reshape(1, bh, *x.shape[1:])).requires_grad_(True) for x in (q, k, v))
+    out = FusedTopKAttentionFunction.apply(qd, kd, vd, topk, 1.0, 64)
+    scores = oracle.quantize_to_grid(q, k, d, 64)
+    _, exp_idx = oracle.topk_order(scores, topk)
+    o, _, _, _ = oracle.topk_attention_forward(q, k, v, topk, 1 / math.sqrt(d), scores=scores)
+    np.testing.assert_allclose(out.detach().cpu().numpy().reshape(o.shape), o, atol=1e-5, rtol=1e-5)
+    grads = torch.autograd.grad((out * _t(do.reshape(1, bh, n, d))).sum(), (qd, kd, vd))
+    ref = oracle.topk_attention_backward(q, k, v, exp_idx, do, 1 / math.sqrt(d), scores=scores)
+    for got, exp in zip(grads, ref):
+        np.testing.assert_allclose(got.cpu().numpy().reshape(exp.shape), exp, atol=1e-4, rtol=1e-3)
+    # bit-exact indices through the forward with saved support
+    from sparsedict_b200 import _ops
+
+    _, idx, _, _ = _ops.topk_attn_fwd(_t(q), _t(k), _t(v), topk, 1 / math.sqrt(d), score_grid=64)
+    assert np.array_equal(idx.cpu().numpy().reshape(exp_idx.shape), exp_idx)
+
+
+# --- routed dictionaries (configuration 3 shape family, reduced size) -------------
+
+
+def test_routed_dictionary_attention_matches_reference(golden):
+    g = {k[4:]: v for k, v in golden.items() if k.startswith("moe_")}
+    q = _t(g["q"]).requires_grad_(True)
+    atoms = _t(g["atoms"]).requires_grad_(True)
+    out, expert, _ = routed_dictionary_attention(q, atoms, _t(g["logits"]), 8, 1.0, return_routing=True)
+    assert np.array_equal(expert.cpu().numpy(), oracle.moe_route_top1(g["logits"]))
+    np.testing.assert_allclose(out.detach().cpu().numpy(), g["out"], atol=1e-5, rtol=0)
+    dq, datoms = torch.autograd.grad((out * _t(g["do"])).sum(), (q, atoms))
+    np.testing.assert_allclose(dq.cpu().numpy(), g["dq"], atol=1e-4, rtol=1e-3)
+    np.testing.assert_allclose(datoms.cpu().numpy(), g["datoms"], atol=1e-4, rtol=1e-3)
+
+
+def test_routed_bf16_full_configuration_sampled_rows():
+    torch.manual_seed(3)
+    n, d, e, m, k = 16384, 64, 8, 1024, 16
+    q = torch.randn(n, d)
+    atoms = torch.randn(e, m, d) / math.sqrt(d)
+    logits = torch.randn(n, e)
+    qd, ad = q.to(DEV, torch.bfloat16), atoms.to(DEV, torch.bfloat16)
+    out = routed_dictionary_attention(qd, ad, logits.to(DEV), k, 1.0)
+    rows = np.random.default_rng(0).choice(n, 256, replace=False)
+    experts = oracle.moe_route_top1(logits.numpy())
+    qr, ar = qd.float().cpu().numpy(), ad.float().cpu().numpy()
+    o, _, _ = oracle.moe_topk_attention_forward(qr[rows], ar, experts[rows], k, 1.0)
+    np.testing.assert_allclose(out.float().cpu().numpy()[rows], o, rtol=2e-2, atol=2e-2)
+
+
+# --- full-size configurations, sampled rows against the oracle --------------------
+
+
+@pytest.mark.parametrize(("b", "h", "n", "m", "d", "k"), [(8, 8, 4096, 4096, 64, 32), (16, 8, 16384, 16384, 64, 64)])
+def test_full_size_bf16_sampled_rows(b, h, n, m, d, k):
+    gen = torch.Generator(device=DEV).manual_seed(2024)
+    q = torch.randn(b, h, n, d, device=DEV, generator=gen).to(torch.bfloat16)
+    kk = torch.randn(b, h, m, d, device=DEV, generator=gen).to(torch.bfloat16)
+    v = torch.randn(b, h, m, d, device=DEV, generator=gen).to(torch.bfloat16)
+    out = fused_topk_attention(q, kk, v, k)
+    rng = np.random.default_rng(1)
+    slices = rng.choice(b * h, 4, replace=False)
+    rows = rng.choice(n, 48, replace=False)
+    qf, kf, vf = (t.reshape(b * h, -1, d) for t in (q, kk, v))
+    for s in slices:
+        qs = qf[s, rows].float().cpu().numpy()[None]
+        ks = kf[s].float().cpu().numpy()[None]
+        vs = vf[s].float().cpu().numpy()[None]
+        o, idx, _, _ = oracle.topk_attention_forward(qs, ks, vs, k, 1 / math.sqrt(d))
+        got = out.reshape(b * h, n, d)[s, rows].float().cpu().numpy()
+        np.testing.assert_allclose(got, o[0], rtol=2e-2, atol=2e-2)
