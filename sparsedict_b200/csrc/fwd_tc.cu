@@ -1,8 +1,465 @@
-// Tensor-core (tcgen05) forward: placeholder until the sm_100a kernel lands.
+// Fused top-k attention forward on the 5th-generation tensor cores (sm_100a).
+//
+// One CTA owns 128 query rows of one (b, h) slice (d = dv = 64, bf16 or fp16)
+// and streams the slice's keys in tiles of 128:
+//
+//   warp 0      TMA producer: the Q tile once, then K tiles into a 3-stage
+//               ring of 128-byte-swizzled shared-memory buffers;
+//   warp 1      allocates 256 TMEM columns and issues tcgen05.mma
+//               (M=128, N=128, K=16 x 4) of S = Q·Kᵀ into one of two TMEM
+//               accumulators, committing to the "S full" and "stage free"
+//               mbarriers;
+//   warps 4..7  selection: thread i owns query row i (TMEM lane i), reads
+//               its 128 scores of the tile with tcgen05.ld 32 columns at a
+//               time, keeps every key that beats the row's running
+//               threshold in a shared-memory candidate list and, when the
+//               list could overflow, raises the threshold with a sampled
+//               pivot and compacts the list.  The score row never reaches
+//               global memory.
+//
+// After the last tile each selection thread trims its list to exactly k
+// keys (lowest-rank-first removal; ties at the k-th score keep the lower
+// key index), writes the indices, the row LSE, and the softmax-weighted
+// sum of the gathered value rows.  The k indices of a row are written in no
+// particular order; the set is the reference's top-k set.
+//
+// Selection runs on the raw dot products; scale = 1/(T·sqrt(d)) > 0 is
+// applied in the epilogue (for d = 64 the scale is a power of two, so the
+// order is exactly that of the scaled scores).
+#include <cuda.h>
+
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
+#include "sm100.cuh"
 
 namespace sdk {
-bool fwd_tensorcore_supports(const FwdLaunch&) { return false; }
-int fwd_tensorcore(const FwdLaunch&) { return SDK_ERR_UNSUPPORTED; }
+namespace {
+
+using namespace sm100;
+
+constexpr int TQ = 128;  // query rows per CTA (TMEM lanes)
+constexpr int TK = 128;  // keys per score tile (MMA N)
+constexpr int D = 64;    // feature width (one 128-byte swizzle row)
+constexpr int KSTAGES = 3;
+constexpr int CAP = 192;  // candidate slots per row
+constexpr int NT = 256;
+constexpr uint32_t TMEM_COLS = 256;
+constexpr uint32_t TILE_BYTES = TK * D * 2;
+
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = OFF_Q + TQ * D * 2;
+constexpr int OFF_CV = OFF_K + KSTAGES * (int)TILE_BYTES;
+constexpr int OFF_CI = OFF_CV + CAP * TQ * 4;
+constexpr int OFF_BAR = OFF_CI + CAP * TQ * 2;
+constexpr int NBARS = 1 + 2 * KSTAGES + 4;
+constexpr int OFF_MISC = OFF_BAR + NBARS * 8;
+constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
+
+struct TcArgs {
+  const void* v;
+  void* out;
+  int32_t* top_idx;
+  float* lse;
+  float* top_scores;
+  int64_t n, m;
+  int tiles_per_slice, topk;
+  float scale;
+  unsigned int* status;
+};
+
+// ----------------------------------------------------------- selection ---
+// Candidate list of row r: slots s = 0..cnt-1 at cv[s*TQ + r] / ci[s*TQ + r]
+// (row-fastest, so the 32 lanes of a warp hit 32 distinct banks).
+
+__device__ __forceinline__ int count_at_least(const float* cv, int r, int cnt, float pivot) {
+  int c = 0;
+  for (int s = 0; s < cnt; ++s) c += !(cv[s * TQ + r] < pivot);
+  return c;
+}
+
+__device__ __forceinline__ void sort16_desc(float (&x)[16]) {
+#pragma unroll
+  for (int size = 2; size <= 16; size <<= 1)
+#pragma unroll
+    for (int st = size >> 1; st > 0; st >>= 1)
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int j = i ^ st;
+        if (j > i) {
+          const bool desc = (i & size) == 0;
+          const float hi = fmaxf(x[i], x[j]), lo = fminf(x[i], x[j]);
+          x[i] = desc ? hi : lo;
+          x[j] = desc ? lo : hi;
+        }
+      }
+}
+
+// Raise the row's threshold to a pivot that at least `topk` listed keys meet
+// (keys seen later rank below those on equal scores) and drop the keys below
+// it.  The pivot is one of 16 sampled list values, chosen so that a little
+// more than `topk` keys survive.
+__device__ void compact_list(float* cv, uint16_t* ci, int r, int& cnt, float& tau, int topk, int slack) {
+  float smp[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float x = cv[((j * cnt) >> 4) * TQ + r];
+    smp[j] = (x != x) ? __int_as_float(0x7f800000) : x;
+  }
+  sort16_desc(smp);
+  int target = (16 * topk) / (cnt > 0 ? cnt : 1) + slack;
+  target = target > 15 ? 15 : target;
+  float pivot = smp[0];
+#pragma unroll
+  for (int j = 1; j < 16; ++j)
+    if (j == target) pivot = smp[j];
+  if (count_at_least(cv, r, cnt, pivot) < topk) {
+    pivot = smp[15];
+    if (count_at_least(cv, r, cnt, pivot) < topk) pivot = __int_as_float(0xff800000);
+  }
+  int w = 0;
+  for (int s = 0; s < cnt; ++s) {
+    const float x = cv[s * TQ + r];
+    const uint16_t i = ci[s * TQ + r];
+    if (!(x < pivot)) {
+      cv[w * TQ + r] = x;
+      ci[w * TQ + r] = i;
+      ++w;
+    }
+  }
+  cnt = w;
+  tau = pivot;
+}
+
+// Remove lowest-ranked keys until exactly `topk` remain (lowest rank: NaN
+// last removed, then the smallest score, and among equal scores the largest
+// key index).  Returns the threshold the survivors all meet.
+__device__ void trim_to_topk(float* cv, uint16_t* ci, int r, int& cnt, float& tau, int topk) {
+  while (cnt > topk) {
+    int worst = 0;
+    float wv = cv[r];
+    int wi = ci[r];
+    for (int s = 1; s < cnt; ++s) {
+      const float x = cv[s * TQ + r];
+      const int i = ci[s * TQ + r];
+      if (ranks_above(wv, wi, x, i)) {
+        worst = s;
+        wv = x;
+        wi = i;
+      }
+    }
+    const int last = cnt - 1;
+    cv[worst * TQ + r] = cv[last * TQ + r];
+    ci[worst * TQ + r] = ci[last * TQ + r];
+    cnt = last;
+    tau = wv;
+  }
+}
+
+__device__ __forceinline__ float chunk_max(const uint32_t (&v)[32]) {
+  float a[11];
+#pragma unroll
+  for (int g = 0; g < 10; ++g)
+    a[g] = max3_nan(__uint_as_float(v[3 * g]), __uint_as_float(v[3 * g + 1]), __uint_as_float(v[3 * g + 2]));
+  a[10] = max_nan(__uint_as_float(v[30]), __uint_as_float(v[31]));
+  const float b0 = max3_nan(a[0], a[1], a[2]), b1 = max3_nan(a[3], a[4], a[5]),
+              b2 = max3_nan(a[6], a[7], a[8]);
+  const float b3 = max_nan(a[9], a[10]);
+  return max_nan(max3_nan(b0, b1, b2), b3);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(NT, 1)
+    fused_fwd_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
+                 TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
+  uint8_t* qs = sm + OFF_Q;
+  uint8_t* ks = sm + OFF_K;
+  float* cv = reinterpret_cast<float*>(sm + OFF_CV);
+  uint16_t* ci = reinterpret_cast<uint16_t*>(sm + OFF_CI);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = bars + 1 + KSTAGES;
+  uint64_t* s_full = bars + 1 + 2 * KSTAGES;
+  uint64_t* s_empty = s_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + OFF_MISC + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t slice = blockIdx.x / a.tiles_per_slice;
+  const int64_t local0 = (int64_t)(blockIdx.x % a.tiles_per_slice) * TQ;
+  const int rows = (int)((a.n - local0) < TQ ? (a.n - local0) : TQ);
+  const int64_t row0 = slice * a.n + local0;
+  const int ntiles = (int)((a.m + TK - 1) / TK);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < KSTAGES; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_empty[b], 4 * kWarp);
+    }
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      mbar_arrive_expect_tx(q_full, TQ * D * 2);
+      tma_load_2d(qs, &tmap_q, 0, (int)row0, q_full);
+      for (int t = 0; t < ntiles; ++t) {
+        const int s = t % KSTAGES;
+        const uint32_t ph = (uint32_t)(t / KSTAGES) & 1u;
+        if (!mbar_wait(&k_empty[s], ph ^ 1u, abort_flag)) break;
+        mbar_arrive_expect_tx(&k_full[s], TILE_BYTES);
+        tma_load_2d(ks + s * TILE_BYTES, &tmap_k, 0, (int)(slice * a.m + (int64_t)t * TK), &k_full[s]);
+        ++issued;
+      }
+      if (*abort_flag) {
+        // let the copies already in flight land before the CTA exits
+        for (int t = (issued > KSTAGES ? issued - KSTAGES : 0); t < issued; ++t) {
+          const uint64_t t0 = global_timer();
+          while (!mbar_try_wait(&k_full[t % KSTAGES], (uint32_t)(t / KSTAGES) & 1u) &&
+                 global_timer() - t0 < kWaitLimitNs) {
+          }
+        }
+        const uint64_t t0 = global_timer();
+        while (!mbar_try_wait(q_full, 0) && global_timer() - t0 < kWaitLimitNs) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = instr_desc_f16(sizeof(T) == 2 && !std::is_same<T, __half>::value, TQ, TK);
+      const uint32_t q_addr = smem_addr(qs);
+      int committed = -1;
+      if (mbar_wait(q_full, 0, abort_flag)) {
+        for (int t = 0; t < ntiles; ++t) {
+          const int s = t % KSTAGES, b = t & 1;
+          if (!mbar_wait(&k_full[s], (uint32_t)(t / KSTAGES) & 1u, abort_flag)) break;
+          if (!mbar_wait(&s_empty[b], ((uint32_t)(t >> 1) & 1u) ^ 1u, abort_flag)) break;
+          tc_fence_after();
+          const uint32_t k_addr = smem_addr(ks + s * TILE_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            mma_f16(tmem + b * TK, smem_desc_k128(q_addr + kk * 32), smem_desc_k128(k_addr + kk * 32), idesc,
+                    kk > 0);
+          mma_commit(&k_empty[s]);
+          mma_commit(&s_full[b]);
+          committed = t;
+        }
+      }
+      if (*abort_flag && committed >= 0) {
+        // wait for the last MMAs before TMEM is released
+        const int b = committed & 1;
+        const uint64_t t0 = global_timer();
+        while (!mbar_try_wait(&s_full[b], (uint32_t)(committed >> 1) & 1u) && global_timer() - t0 < kWaitLimitNs) {
+        }
+      }
+    }
+  } else if (warp >= 4) {
+    const int r = threadIdx.x - 4 * kWarp;  // row within the tile == TMEM lane
+    const uint32_t lane_base = (uint32_t)((warp - 4) * kWarp) << 16;
+    float tau = __int_as_float(0x7fc00000);  // "no threshold yet"
+    int cnt = 0;
+    bool ok = true;
+    for (int t = 0; t < ntiles && ok; ++t) {
+      const int b = t & 1;
+      if (!mbar_wait(&s_full[b], (uint32_t)(t >> 1) & 1u, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int64_t key_tile = (int64_t)t * TK;
+      const int tile_valid = (int)((a.m - key_tile) < TK ? (a.m - key_tile) : TK);
+#pragma unroll 1
+      for (int c = 0; c < TK / 32; ++c) {
+        uint32_t v[32];
+        tmem_load_32cols(tmem + lane_base + b * TK + c * 32, v);
+        tmem_wait_load();
+        if (c == TK / 32 - 1) {
+          tc_fence_before();
+          mbar_arrive(&s_empty[b]);
+        }
+        const int valid = tile_valid - c * 32;
+        if (valid <= 0) continue;  // warp-uniform
+        const int key0 = (int)(key_tile + c * 32);
+        float mx;
+        if (valid >= 32) {
+          mx = chunk_max(v);
+        } else {
+          mx = __int_as_float(0xff800000);
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (i < valid) mx = max_nan(mx, __uint_as_float(v[i]));
+        }
+        if (!__any_sync(0xffffffffu, !(mx <= tau))) continue;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float x = __uint_as_float(v[i]);
+          if (i < valid && !(x <= tau)) {
+            cv[cnt * TQ + r] = x;
+            ci[cnt * TQ + r] = (uint16_t)(key0 + i);
+            ++cnt;
+          }
+        }
+        if (__any_sync(0xffffffffu, cnt > CAP - 32)) {
+          if (cnt > CAP - 32) {
+            compact_list(cv, ci, r, cnt, tau, a.topk, 2);
+            if (cnt > CAP - 32) trim_to_topk(cv, ci, r, cnt, tau, a.topk);
+          }
+        }
+      }
+    }
+    if (ok && !*abort_flag) {
+      if (cnt > a.topk + 24) compact_list(cv, ci, r, cnt, tau, a.topk, 1);
+      trim_to_topk(cv, ci, r, cnt, tau, a.topk);
+      if (r < rows) {
+        const int64_t gr = row0 + r;
+        float mx = cv[r];
+        for (int j = 1; j < a.topk; ++j) mx = fmaxf(mx, cv[j * TQ + r]);
+        const float mxs = mx * a.scale;
+        float total = 0.f;
+        for (int j = 0; j < a.topk; ++j) total += expf(cv[j * TQ + r] * a.scale - mxs);
+        const float lse = mxs + logf(total);
+        a.lse[gr] = lse;
+        int32_t* idx_row = a.top_idx + gr * a.topk;
+        for (int j = 0; j < a.topk; ++j) {
+          idx_row[j] = ci[j * TQ + r];
+          if (a.top_scores) a.top_scores[gr * a.topk + j] = cv[j * TQ + r] * a.scale;
+        }
+        float acc[D];
+#pragma unroll
+        for (int f = 0; f < D; ++f) acc[f] = 0.f;
+        const T* vbase = static_cast<const T*>(a.v) + slice * a.m * D;
+        for (int j = 0; j < a.topk; ++j) {
+          const float p = expf(cv[j * TQ + r] * a.scale - lse);
+          const uint4* vrow = reinterpret_cast<const uint4*>(vbase + (int64_t)ci[j * TQ + r] * D);
+#pragma unroll
+          for (int q4 = 0; q4 < D / 8; ++q4) {
+            const uint4 u = __ldg(vrow + q4);
+            const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+            for (int h = 0; h < 8; ++h) acc[q4 * 8 + h] = fmaf(p, to_acc(e[h]), acc[q4 * 8 + h]);
+          }
+        }
+        uint4* orow = reinterpret_cast<uint4*>(static_cast<T*>(a.out) + gr * D);
+#pragma unroll
+        for (int q4 = 0; q4 < D / 8; ++q4) {
+          uint4 u;
+          T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+          for (int h = 0; h < 8; ++h) e[h] = from_acc<T>(acc[q4 * 8 + h]);
+          orow[q4] = u;
+        }
+      }
+    }
+  }
+
+  __syncthreads();
+  if (*abort_flag && threadIdx.x == 0) raise_device_status(a.status, kStatusWaitTimeout);
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host ---
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    else
+      cudaGetLastError();
+  }
+  return fn;
+}
+
+// Row-major [rows, 64] 16-bit matrix, 128-row boxes, 128-byte swizzle.
+bool make_rows_map(CUtensorMap* map, const void* base, int64_t rows, bool bf16) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)D, (cuuint32_t)TQ};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+            const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename T>
+int launch(const FwdLaunch& L) {
+  CUtensorMap tq, tk;
+  const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  if (!make_rows_map(&tq, L.q, L.slices * L.n, bf16)) return SDK_ERR_CUDA;
+  if (!make_rows_map(&tk, L.k, L.slices * L.m, bf16)) return SDK_ERR_CUDA;
+  TcArgs a;
+  a.v = L.v;
+  a.out = L.out;
+  a.top_idx = L.top_idx;
+  a.lse = static_cast<float*>(L.lse);
+  a.top_scores = static_cast<float*>(L.top_scores);
+  a.n = L.n;
+  a.m = L.m;
+  a.tiles_per_slice = (int)((L.n + TQ - 1) / TQ);
+  a.topk = L.topk;
+  a.scale = (float)L.scale;
+  a.status = L.status;
+  const int64_t grid = L.slices * a.tiles_per_slice;
+  if (grid <= 0) return SDK_OK;
+  auto kern = fused_fwd_tc<T>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
+    return SDK_ERR_CUDA;
+  kern<<<(unsigned)grid, NT, SMEM_BYTES, L.stream>>>(tq, tk, a);
+  return cudaPeekAtLastError() == cudaSuccess ? SDK_OK : SDK_ERR_CUDA;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+bool fwd_tensorcore_supports(const FwdLaunch& L) {
+  if (L.dtype != SDK_DTYPE_BF16 && L.dtype != SDK_DTYPE_F16) return false;
+  if (L.d != D || L.dv != D || L.score_grid != 0) return false;
+  if (L.row_offsets || L.row_index) return false;
+  if (L.m > 65536 || L.topk > 64 || L.n < 1) return false;
+  if (L.slices * L.n > 0x7fffffff || L.slices * L.m > 0x7fffffff) return false;
+  if (!aligned16(L.q) || !aligned16(L.k) || !aligned16(L.v) || !aligned16(L.out)) return false;
+  return encode_fn() != nullptr;
+}
+
+int fwd_tensorcore(const FwdLaunch& L) {
+  if (L.dtype == SDK_DTYPE_BF16) return launch<__nv_bfloat16>(L);
+  if (L.dtype == SDK_DTYPE_F16) return launch<__half>(L);
+  return SDK_ERR_UNSUPPORTED;
+}
+
 }  // namespace sdk

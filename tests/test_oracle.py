@@ -204,3 +204,11 @@ def test_partition_top_k_matches_lexsort_order():
             nan, value = np.isnan(x), x
             order = np.lexsort((np.broadcast_to(np.arange(300), x.shape), -value.astype(np.float64), ~nan), axis=-1)
             assert np.array_equal(i1, order[:, :k])
+
+
+def test_unordered_set_comparison():
+    scores = np.array([[5.0, 4.0, 3.99999, 1.0]], dtype=np.float32)
+    assert oracle.gap_aware_index_mismatches(np.array([[1, 0]]), np.array([[0, 1]]), scores, 1e-4, ordered=False) == 0
+    assert oracle.gap_aware_index_mismatches(np.array([[2, 0]]), np.array([[0, 1]]), scores, 1e-4, ordered=False) == 0
+    assert oracle.gap_aware_index_mismatches(np.array([[3, 0]]), np.array([[0, 1]]), scores, 1e-4, ordered=False) == 1
+    assert oracle.gap_aware_index_mismatches(np.array([[1, 0]]), np.array([[0, 1]]), scores, 1e-4, ordered=True) == 1

@@ -48,8 +48,8 @@ def _oracle_scores64(q, k, scale):
     return np.einsum("bnd,bmd->bnm", _flat(q).astype(np.float64), _flat(k).astype(np.float64)) * scale
 
 
-def _assert_indices(actual, expected, scores, tol=1e-5):
-    bad = oracle.gap_aware_index_mismatches(actual, expected, scores, tol)
+def _assert_indices(actual, expected, scores, tol=1e-5, ordered=True):
+    bad = oracle.gap_aware_index_mismatches(actual, expected, scores, tol, ordered)
     assert bad == 0, f"{bad} rows select different keys"
 
 
@@ -343,8 +343,9 @@ def test_low_precision_forward_backward_vs_oracle(dtype):
 
     _, gidx, _, _ = _ops.topk_attn_fwd(*(t.detach().reshape(b * h, -1, d) for t in (qd, kd, vd)), k, scale)
     gidx = gidx.cpu().numpy().reshape(idx.shape)
-    # selected sets agree wherever the affinity gap exceeds bf16 rounding (here: 1e-4)
-    _assert_indices(gidx, idx, _oracle_scores64(qr, kr, scale), tol=1e-4)
+    # selected sets agree wherever the affinity gap exceeds bf16 rounding (here: 1e-4);
+    # the tensor-core kernel returns each row's top-k set unordered
+    _assert_indices(gidx, idx, _oracle_scores64(qr, kr, scale), tol=1e-4, ordered=False)
     np.testing.assert_allclose(out.float().detach().cpu().numpy().reshape(o.shape), o, rtol=2e-2, atol=2e-2)
     # backward checked on the support the GPU selected
     ref = oracle.topk_attention_backward(_flat(qr), _flat(kr), _flat(vr), gidx, _flat(dor), scale)
