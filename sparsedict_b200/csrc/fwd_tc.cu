@@ -73,10 +73,19 @@ struct TcArgs {
 // Candidate list of row r: slots s = 0..cnt-1 at cv[s*TQ + r] / ci[s*TQ + r]
 // (row-fastest, so the 32 lanes of a warp hit 32 distinct banks).
 
-__device__ __forceinline__ int count_at_least(const float* cv, int r, int cnt, float pivot) {
-  int c = 0;
-  for (int s = 0; s < cnt; ++s) c += !(cv[s * TQ + r] < pivot);
-  return c;
+// Order-preserving 64-bit rank key: larger key = ranks higher.  The high
+// word maps the float onto an unsigned order (NaN highest, -0 == +0); the
+// low word is the complemented key index, so equal scores rank the lower
+// index higher.
+__device__ __forceinline__ uint64_t rank_key(float x, uint32_t idx) {
+  uint32_t u;
+  if (x != x) {
+    u = 0xffffffffu;
+  } else {
+    u = __float_as_uint(x + 0.0f);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  }
+  return ((uint64_t)u << 32) | (uint64_t)(0xffffffffu - idx);
 }
 
 __device__ __forceinline__ void sort16_desc(float (&x)[16]) {
@@ -96,10 +105,22 @@ __device__ __forceinline__ void sort16_desc(float (&x)[16]) {
       }
 }
 
-// Raise the row's threshold to a pivot that at least `topk` listed keys meet
-// (keys seen later rank below those on equal scores) and drop the keys below
-// it.  The pivot is one of 16 sampled list values, chosen so that a little
-// more than `topk` keys survive.
+// Counts of listed values >= each of four pivots, in one pass.
+__device__ __forceinline__ void count4(const float* cv, int r, int cnt, const float (&p)[4], int (&c)[4]) {
+  c[0] = c[1] = c[2] = c[3] = 0;
+#pragma unroll 4
+  for (int s = 0; s < cnt; ++s) {
+    const float x = cv[s * TQ + r];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) c[q] += !(x < p[q]);
+  }
+}
+
+// Raise the row's threshold to the highest of 16 sampled list values that at
+// least `topk` listed keys meet (keys seen later rank below these on equal
+// scores, so `!(s <= tau)` stays exact) and drop the keys below it.  The
+// search starts near the sample rank expected to keep about
+// topk + slack*cnt/16 keys and tests four candidate pivots per pass.
 __device__ void compact_list(float* cv, uint16_t* ci, int r, int& cnt, float& tau, int topk, int slack) {
   float smp[16];
 #pragma unroll
@@ -108,15 +129,30 @@ __device__ void compact_list(float* cv, uint16_t* ci, int r, int& cnt, float& ta
     smp[j] = (x != x) ? __int_as_float(0x7f800000) : x;
   }
   sort16_desc(smp);
-  int target = (16 * topk) / (cnt > 0 ? cnt : 1) + slack;
-  target = target > 15 ? 15 : target;
-  float pivot = smp[0];
+  int t = (16 * topk) / (cnt > 0 ? cnt : 1) + slack - 1;
+  t = t < 0 ? 0 : (t > 12 ? 12 : t);
+  float pivot = __int_as_float(0xff800000);
+  bool found = false;
+  for (int pass = 0; pass < 4 && !found; ++pass) {
+    float p[4];
 #pragma unroll
-  for (int j = 1; j < 16; ++j)
-    if (j == target) pivot = smp[j];
-  if (count_at_least(cv, r, cnt, pivot) < topk) {
-    pivot = smp[15];
-    if (count_at_least(cv, r, cnt, pivot) < topk) pivot = __int_as_float(0xff800000);
+    for (int q = 0; q < 4; ++q) {
+      const int want = t + q;
+      float v = smp[15];
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (j == want) v = smp[j];
+      p[q] = v;
+    }
+    int c[4];
+    count4(cv, r, cnt, p, c);
+#pragma unroll
+    for (int q = 3; q >= 0; --q)
+      if (c[q] >= topk) {
+        pivot = p[q];
+        found = true;
+      }
+    t = t + 4 > 12 ? 12 : t + 4;
   }
   int w = 0;
   for (int s = 0; s < cnt; ++s) {
@@ -132,29 +168,45 @@ __device__ void compact_list(float* cv, uint16_t* ci, int r, int& cnt, float& ta
   tau = pivot;
 }
 
-// Remove lowest-ranked keys until exactly `topk` remain (lowest rank: NaN
-// last removed, then the smallest score, and among equal scores the largest
-// key index).  Returns the threshold the survivors all meet.
+// Remove lowest-ranked keys until exactly `topk` remain; the survivors are
+// the list's top-k by (score descending, index ascending).
 __device__ void trim_to_topk(float* cv, uint16_t* ci, int r, int& cnt, float& tau, int topk) {
   while (cnt > topk) {
-    int worst = 0;
-    float wv = cv[r];
-    int wi = ci[r];
-    for (int s = 1; s < cnt; ++s) {
-      const float x = cv[s * TQ + r];
-      const int i = ci[s * TQ + r];
-      if (ranks_above(wv, wi, x, i)) {
-        worst = s;
-        wv = x;
-        wi = i;
-      }
+    uint64_t worst = ~0ull;
+    int pos = 0;
+#pragma unroll 4
+    for (int s = 0; s < cnt; ++s) {
+      const uint64_t key = rank_key(cv[s * TQ + r], ci[s * TQ + r]);
+      const bool lower = key < worst;
+      worst = lower ? key : worst;
+      pos = lower ? s : pos;
     }
+    tau = cv[pos * TQ + r];
     const int last = cnt - 1;
-    cv[worst * TQ + r] = cv[last * TQ + r];
-    ci[worst * TQ + r] = ci[last * TQ + r];
+    cv[pos * TQ + r] = cv[last * TQ + r];
+    ci[pos * TQ + r] = ci[last * TQ + r];
     cnt = last;
-    tau = wv;
   }
+}
+
+// Append every key of a 32-key chunk whose score passes !(x <= tau) to the
+// row's list.  Branch-free: each key's slot is the running count, and the
+// store is predicated on the test.
+__device__ __forceinline__ void append_chunk(const uint32_t* v, int valid, float tau, int key0, float* cv,
+                                             uint16_t* ci, int r, int& cnt) {
+  uint32_t slot = (uint32_t)cnt;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float x = __uint_as_float(v[i]);
+    const uint32_t take = (uint32_t)(i < valid && !(x <= tau));
+    const uint32_t off = slot * TQ + r;
+    if (take) {
+      cv[off] = x;
+      ci[off] = (uint16_t)(key0 + i);
+    }
+    slot += take;
+  }
+  cnt = (int)slot;
 }
 
 __device__ __forceinline__ float chunk_max(const uint32_t (&v)[32]) {
@@ -287,39 +339,38 @@ __global__ void __launch_bounds__(NT, 1)
       tc_fence_after();
       const int64_t key_tile = (int64_t)t * TK;
       const int tile_valid = (int)((a.m - key_tile) < TK ? (a.m - key_tile) : TK);
-#pragma unroll 1
+      // All four 32-column chunks of this tile go to registers at once; the
+      // TMEM buffer is released before any selection work so the next MMA
+      // into it can start.
+      uint32_t v[TK];
+#pragma unroll
+      for (int c = 0; c < TK / 32; ++c)
+        tmem_load_32cols(tmem + lane_base + b * TK + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
+      tmem_wait_load();
+      tc_fence_before();
+      mbar_arrive(&s_empty[b]);
+      float mx[TK / 32];
+#pragma unroll
       for (int c = 0; c < TK / 32; ++c) {
-        uint32_t v[32];
-        tmem_load_32cols(tmem + lane_base + b * TK + c * 32, v);
-        tmem_wait_load();
-        if (c == TK / 32 - 1) {
-          tc_fence_before();
-          mbar_arrive(&s_empty[b]);
-        }
-        const int valid = tile_valid - c * 32;
-        if (valid <= 0) continue;  // warp-uniform
-        const int key0 = (int)(key_tile + c * 32);
-        float mx;
-        if (valid >= 32) {
-          mx = chunk_max(v);
+        if (tile_valid >= TK) {
+          mx[c] = chunk_max(*reinterpret_cast<const uint32_t(*)[32]>(&v[c * 32]));
         } else {
-          mx = __int_as_float(0xff800000);
+          float m = __int_as_float(0xff800000);
 #pragma unroll
           for (int i = 0; i < 32; ++i)
-            if (i < valid) mx = max_nan(mx, __uint_as_float(v[i]));
+            if (c * 32 + i < tile_valid) m = max_nan(m, __uint_as_float(v[c * 32 + i]));
+          mx[c] = m;
         }
-        if (!__any_sync(0xffffffffu, !(mx <= tau))) continue;
+      }
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float x = __uint_as_float(v[i]);
-          if (i < valid && !(x <= tau)) {
-            cv[cnt * TQ + r] = x;
-            ci[cnt * TQ + r] = (uint16_t)(key0 + i);
-            ++cnt;
-          }
-        }
+      for (int c = 0; c < TK / 32; ++c) {
+        if (!__any_sync(0xffffffffu, !(mx[c] <= tau))) continue;
+        append_chunk(&v[c * 32], tile_valid - c * 32, tau, (int)(key_tile + c * 32), cv, ci, r, cnt);
+        // When one lane's list could overflow, every lane holding well over
+        // k keys compacts in the same pass: under SIMT the warp pays for the
+        // longest list either way.
         if (__any_sync(0xffffffffu, cnt > CAP - 32)) {
-          if (cnt > CAP - 32) {
+          if (cnt > a.topk + 32) {
             compact_list(cv, ci, r, cnt, tau, a.topk, 2);
             if (cnt > CAP - 32) trim_to_topk(cv, ci, r, cnt, tau, a.topk);
           }
@@ -327,7 +378,7 @@ __global__ void __launch_bounds__(NT, 1)
       }
     }
     if (ok && !*abort_flag) {
-      if (cnt > a.topk + 24) compact_list(cv, ci, r, cnt, tau, a.topk, 1);
+      if (cnt > a.topk + 16) compact_list(cv, ci, r, cnt, tau, a.topk, 1);
       trim_to_topk(cv, ci, r, cnt, tau, a.topk);
       if (r < rows) {
         const int64_t gr = row0 + r;
@@ -347,6 +398,7 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
         for (int f = 0; f < D; ++f) acc[f] = 0.f;
         const T* vbase = static_cast<const T*>(a.v) + slice * a.m * D;
+#pragma unroll 2
         for (int j = 0; j < a.topk; ++j) {
           const float p = expf(cv[j * TQ + r] * a.scale - lse);
           const uint4* vrow = reinterpret_cast<const uint4*>(vbase + (int64_t)ci[j * TQ + r] * D);

@@ -53,6 +53,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// As mbar_try_wait, but lets the thread sleep (up to `hint_ns`) until the
+// phase completes instead of returning at once, so waiting warps do not
+// take issue slots from working ones.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return done != 0;
+}
+
 // Waits for the phase of `bar` with parity `parity` to complete.  Gives up
 // (returns false) when `abort_flag` is raised by another warp or after
 // kWaitLimitNs, in which case it raises the flag itself.
@@ -60,7 +75,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
     if (*abort_flag) return false;
     if (global_timer() - t0 > kWaitLimitNs) {
       *abort_flag = 1;
