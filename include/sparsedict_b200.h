@@ -38,6 +38,7 @@ enum {
   SDK_ERR_UNSUPPORTED = 2,      /* valid request outside this build's kernels (e.g. k too large) */
   SDK_ERR_CUDA = 3,             /* a CUDA runtime call or launch failed */
   SDK_ERR_NO_DEVICE = 4,        /* no sm_100 device is current */
+  SDK_ERR_TOO_LARGE = 5,        /* request exceeds the fixed scratch of sdk_topk_attn_bwd_noalloc */
 };
 
 /* Library version, (major << 16) | minor. */
@@ -100,6 +101,38 @@ int sdk_topk_attn_bwd(const void* q, const void* k, const void* v, const void* d
                       int64_t slices, int64_t n, int64_t m, int32_t d, int32_t dv, int32_t topk,
                       double scale, int32_t score_grid, int32_t accumulate, int32_t dtype,
                       void* stream);
+
+/* Capacity, in fp32 elements (16 MiB), of the library-owned scratch array
+ * that sdk_topk_attn_bwd_noalloc accumulates dK and dV in. */
+#define SDK_NOALLOC_SCRATCH_FLOATS (4u * 1024u * 1024u)
+
+/*
+ * Backward without device allocation.  No counterpart in the reference: it
+ * exists for callers that cannot allocate device memory — code running under
+ * a memory budget owned by someone else (a host framework's pool, another
+ * runtime that reserved the device) or on a latency-critical path where
+ * cudaMalloc, which may synchronise the device, is not allowed — and so
+ * cannot pass the accumulator buffers sdk_topk_attn_bwd needs.
+ *
+ * Computes the same gradients as sdk_topk_attn_bwd followed by
+ * sdk_finalize_grad (uniform slices, no routing, score_grid 0), writing dq,
+ * dk [slices, m, d] and dv [slices, m, dv_dim] in `dtype` (F32, BF16 or F16).
+ * The fp32 accumulators live in a file-scope device array of
+ * SDK_NOALLOC_SCRATCH_FLOATS elements that every GPU loading the library
+ * holds until the process exits; a request needing more than
+ * slices*m*(d+dv_dim) <= SDK_NOALLOC_SCRATCH_FLOATS is refused with
+ * SDK_ERR_TOO_LARGE before anything runs.  The call allocates nothing.
+ *
+ * The first call on each device looks up that array's device address
+ * (cudaGetSymbolAddress, with the device current); make that first call
+ * before any stream capture.  All calls share the one array: each clears the
+ * part it uses before accumulating, and calls that overlap on the GPU (on
+ * different streams or from different host threads) race on it.
+ */
+int sdk_topk_attn_bwd_noalloc(const void* q, const void* k, const void* v, const void* dout,
+                              const int32_t* top_idx, const float* lse, void* dq, void* dk, void* dv,
+                              int64_t slices, int64_t n, int64_t m, int32_t d, int32_t dv_dim, int32_t topk,
+                              double scale, int32_t dtype, void* stream);
 
 /* Converts `count` accumulator elements (float32; float64 for F64) into
  * `dtype`, multiplying by `multiplier`.  `out` may alias `acc` only when the

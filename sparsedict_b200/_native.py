@@ -15,7 +15,8 @@ import torch
 LIB_PATH = Path(__file__).resolve().parent / "libsparsedict_b200.so"
 
 DTYPE_F32, DTYPE_F64, DTYPE_BF16, DTYPE_F16 = 0, 1, 2, 3
-SDK_OK, SDK_ERR_INVALID_ARGUMENT, SDK_ERR_UNSUPPORTED, SDK_ERR_CUDA, SDK_ERR_NO_DEVICE = range(5)
+SDK_OK, SDK_ERR_INVALID_ARGUMENT, SDK_ERR_UNSUPPORTED, SDK_ERR_CUDA, SDK_ERR_NO_DEVICE, SDK_ERR_TOO_LARGE = range(6)
+NOALLOC_SCRATCH_FLOATS = 4 * 1024 * 1024
 
 TORCH_TO_SDK = {
     torch.float32: DTYPE_F32,
@@ -40,6 +41,7 @@ SIGNATURES = {
     "sdk_topk_attn_bwd": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _i32, _f64, _i32,
                           _i32, _i32, _p],
     "sdk_finalize_grad": [_p, _p, _i64, _f64, _i32, _p],
+    "sdk_topk_attn_bwd_noalloc": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _i32, _f64, _i32, _p],
     "sdk_affinity": [_p, _p, _p, _i64, _i64, _i32, _i64, _i64, _i32, _p],
     "sdk_topk_select": [_p, _p, _p, _i64, _i64, _i64, _i32, _i32, _p],
     "sdk_topk_aggregate": [_p, _p, _p, _p, _i64, _i32, _i64, _i32, _i64, _i64, _i64, _i32, _i32, _i32, _p],

@@ -52,6 +52,8 @@ int check_device() {
 }
 }  // namespace
 
+int record_cuda_error(cudaError_t err) { return record(err); }
+
 // Device address of this library's status word on the current device, looked
 // up once per device with that device current.
 unsigned int* device_status_ptr() {
@@ -84,6 +86,7 @@ const char* sdk_status_string(int status) {
     case SDK_ERR_UNSUPPORTED: return "unsupported by this build's kernels";
     case SDK_ERR_CUDA: return "CUDA error";
     case SDK_ERR_NO_DEVICE: return "no sm_100 CUDA device is current";
+    case SDK_ERR_TOO_LARGE: return "request exceeds the fixed scratch capacity of the no-allocation entry point";
     default: return "unknown status";
   }
 }

@@ -5,6 +5,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "../../include/sparsedict_b200.h"
+
 namespace sdk {
 
 constexpr size_t kMaxDynamicSmem = 227 * 1024;
@@ -54,6 +56,10 @@ struct BwdLaunch {
   unsigned int* status;
   cudaStream_t stream;
 };
+
+// Records a CUDA error for sdk_last_cuda_error(); returns SDK_ERR_CUDA (or
+// SDK_OK for cudaSuccess).  Defined in capi.cu.
+int record_cuda_error(cudaError_t err);
 
 // CUDA-core fused forward (fwd_generic.cu).
 int fwd_generic(const FwdLaunch& L);
