@@ -133,6 +133,183 @@ __global__ void __launch_bounds__(NT) sparse_bwd(BwdArgs<typename AccOf<T>::type
   }
 }
 
+// ------------------------------------------------ d = dv = 64 fast path ---
+// bf16/fp16 rows of 64 features (128 bytes), k <= 64.  A warp owns one query
+// row; lane L owns slots L and L+32:
+//   pass 1  each lane reads its slots' key and value rows with 16-byte loads
+//           and forms s, P = exp(s - lse) and G = dout·v against q and dout
+//           broadcast from shared memory;
+//   dq      each lane keeps its key rows in registers and adds dS·k into a
+//           64-wide partial; the 32 partials are summed through a padded
+//           shared-memory transpose (lane L finishes features 2L, 2L+1);
+//   scatter lanes span the 64 features of one key row (two per lane) so each
+//           warp-wide vector reduction covers a whole 256-byte fp32 row.
+constexpr int F64W = 4;  // warps per block
+
+__device__ __forceinline__ void red_add2(float* p, float a, float b) {
+  asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(p), "f"(a), "f"(b) : "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int h = 0; h < 8; ++h) f[h] = to_acc(e[h]);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(F64W * kWarp) sparse_bwd_d64(BwdArgs<float> a) {
+  __shared__ __align__(16) float sq[F64W][64];
+  __shared__ __align__(16) float sdo[F64W][64];
+  __shared__ float part[F64W][kWarp][65];
+  __shared__ float swk[F64W][64], swv[F64W][64];
+  __shared__ int skey[F64W][64];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const T* __restrict__ q = static_cast<const T*>(a.q);
+  const T* __restrict__ dout = static_cast<const T*>(a.dout);
+
+  for (int64_t r = (int64_t)blockIdx.x * F64W + warp; r < a.rows; r += (int64_t)gridDim.x * F64W) {
+    const int64_t slice = slice_of_row(a.geo, r);
+    const int64_t pr = a.row_index ? (int64_t)a.row_index[r] : r;
+    const T* __restrict__ kmat = static_cast<const T*>(a.k) + slice * a.m * 64;
+    const T* __restrict__ vmat = static_cast<const T*>(a.v) + slice * a.m * 64;
+    sq[warp][2 * lane] = to_acc(q[pr * 64 + 2 * lane]);
+    sq[warp][2 * lane + 1] = to_acc(q[pr * 64 + 2 * lane + 1]);
+    sdo[warp][2 * lane] = to_acc(dout[pr * 64 + 2 * lane]);
+    sdo[warp][2 * lane + 1] = to_acc(dout[pr * 64 + 2 * lane + 1]);
+    __syncwarp();
+    const float l = a.lse[r];
+
+    uint4 kr[2][8];
+    float p[2], g[2];
+    int key[2];
+#pragma unroll
+    for (int sj = 0; sj < 2; ++sj) {
+      const int j = lane + 32 * sj;
+      p[sj] = 0.f;
+      g[sj] = 0.f;
+      key[sj] = -1;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) kr[sj][c] = make_uint4(0, 0, 0, 0);
+      if (j < a.topk) {
+        int kk = a.top_idx[r * a.topk + j];
+        if (kk < 0 || kk >= a.m) {
+          raise_device_status(a.status, kStatusIndexOutOfRange);
+        } else {
+          key[sj] = kk;
+          const uint4* krow = reinterpret_cast<const uint4*>(kmat + (int64_t)kk * 64);
+          const uint4* vrow = reinterpret_cast<const uint4*>(vmat + (int64_t)kk * 64);
+          uint4 vr[8];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            kr[sj][c] = __ldg(krow + c);
+            vr[c] = __ldg(vrow + c);
+          }
+          float s = 0.f, gg = 0.f;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            float kf[8], vf[8];
+            unpack8<T>(kr[sj][c], kf);
+            unpack8<T>(vr[c], vf);
+            const float4 q0 = *reinterpret_cast<const float4*>(&sq[warp][8 * c]);
+            const float4 q1 = *reinterpret_cast<const float4*>(&sq[warp][8 * c + 4]);
+            const float4 d0 = *reinterpret_cast<const float4*>(&sdo[warp][8 * c]);
+            const float4 d1 = *reinterpret_cast<const float4*>(&sdo[warp][8 * c + 4]);
+            s = fmaf(q0.x, kf[0], s); s = fmaf(q0.y, kf[1], s); s = fmaf(q0.z, kf[2], s); s = fmaf(q0.w, kf[3], s);
+            s = fmaf(q1.x, kf[4], s); s = fmaf(q1.y, kf[5], s); s = fmaf(q1.z, kf[6], s); s = fmaf(q1.w, kf[7], s);
+            gg = fmaf(d0.x, vf[0], gg); gg = fmaf(d0.y, vf[1], gg); gg = fmaf(d0.z, vf[2], gg); gg = fmaf(d0.w, vf[3], gg);
+            gg = fmaf(d1.x, vf[4], gg); gg = fmaf(d1.y, vf[5], gg); gg = fmaf(d1.z, vf[6], gg); gg = fmaf(d1.w, vf[7], gg);
+          }
+          p[sj] = expf(s * a.scale - l);
+          g[sj] = gg;
+        }
+      }
+    }
+    float part_sum = p[0] * g[0] + p[1] * g[1];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) part_sum += __shfl_xor_sync(0xffffffffu, part_sum, o);
+    const float delta = part_sum;
+    const float ds0 = p[0] * (g[0] - delta), ds1 = p[1] * (g[1] - delta);
+
+    float dqp[64];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      float k0[8], k1[8];
+      unpack8<T>(kr[0][c], k0);
+      unpack8<T>(kr[1][c], k1);
+#pragma unroll
+      for (int h = 0; h < 8; ++h) dqp[8 * c + h] = fmaf(ds0, k0[h], ds1 * k1[h]);
+    }
+#pragma unroll
+    for (int f = 0; f < 64; ++f) part[warp][lane][f] = dqp[f];
+#pragma unroll
+    for (int sj = 0; sj < 2; ++sj) {
+      const int j = lane + 32 * sj;
+      if (j < 64) {
+        skey[warp][j] = key[sj];
+        swk[warp][j] = (sj ? ds1 : ds0) * a.scale;
+        swv[warp][j] = p[sj];
+      }
+    }
+    __syncwarp();
+    float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll 8
+    for (int i = 0; i < kWarp; ++i) {
+      acc0 += part[warp][i][2 * lane];
+      acc1 += part[warp][i][2 * lane + 1];
+    }
+    T* dqr = static_cast<T*>(a.dq) + pr * 64;
+    dqr[2 * lane] = cvt_out<T>(acc0 * a.scale);
+    dqr[2 * lane + 1] = cvt_out<T>(acc1 * a.scale);
+
+    const float q0 = sq[warp][2 * lane], q1 = sq[warp][2 * lane + 1];
+    const float o0 = sdo[warp][2 * lane], o1 = sdo[warp][2 * lane + 1];
+    float* dkm = a.dk_acc + slice * a.m * 64;
+    float* dvm = a.dv_acc + slice * a.m * 64;
+    for (int j = 0; j < a.topk; ++j) {
+      const int kk = skey[warp][j];
+      if (kk < 0) continue;
+      const float wk = swk[warp][j], wv = swv[warp][j];
+      red_add2(dkm + (int64_t)kk * 64 + 2 * lane, wk * q0, wk * q1);
+      red_add2(dvm + (int64_t)kk * 64 + 2 * lane, wv * o0, wv * o1);
+    }
+    __syncwarp();
+  }
+}
+
+template <typename T>
+int launch_d64(const BwdLaunch& L) {
+  BwdArgs<float> a;
+  a.q = L.q; a.k = L.k; a.v = L.v; a.dout = L.dout; a.top_idx = L.top_idx;
+  a.lse = static_cast<const float*>(L.lse);
+  a.dq = L.dq;
+  a.dk_acc = static_cast<float*>(L.dk_acc);
+  a.dv_acc = static_cast<float*>(L.dv_acc);
+  a.geo = SliceGeometry{L.row_offsets, L.slices, L.n};
+  a.row_index = L.row_index;
+  a.rows = L.row_offsets ? L.n : L.slices * L.n;
+  a.m = L.m; a.d = L.d; a.dv = L.dv; a.topk = L.topk;
+  a.scale = (float)L.scale;
+  a.root = (float)(1.0 / L.scale);
+  a.grid = 0.f;
+  a.status = L.status;
+  if (a.rows <= 0) return SDK_OK;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (a.rows + F64W - 1) / F64W;
+  const int64_t cap = (int64_t)sms * 8;
+  sparse_bwd_d64<T><<<(unsigned)(want < cap ? want : cap), F64W * kWarp, 0, L.stream>>>(a);
+  return cudaPeekAtLastError() == cudaSuccess ? SDK_OK : SDK_ERR_CUDA;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+bool d64_supported(const BwdLaunch& L) {
+  return (L.dtype == SDK_DTYPE_BF16 || L.dtype == SDK_DTYPE_F16) && L.d == 64 && L.dv == 64 && L.topk <= 64 &&
+         L.score_grid == 0 && aligned16(L.k) && aligned16(L.v) && aligned16(L.dk_acc) && aligned16(L.dv_acc);
+}
+
 template <typename T>
 int launch(const BwdLaunch& L) {
   using Acc = typename AccOf<T>::type;
@@ -187,6 +364,7 @@ int launch_finalize(const void* acc, void* out, int64_t count, double mult, cuda
 }  // namespace
 
 int bwd_sparse(const BwdLaunch& L) {
+  if (d64_supported(L)) return L.dtype == SDK_DTYPE_BF16 ? launch_d64<__nv_bfloat16>(L) : launch_d64<__half>(L);
   switch (L.dtype) {
     case SDK_DTYPE_F32: return launch<float>(L);
     case SDK_DTYPE_F64: return launch<double>(L);
