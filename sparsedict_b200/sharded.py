@@ -11,14 +11,17 @@ queries, a rank's dK/dV partials are zero outside its own slices.  The
 prescribed all-reduce therefore adds zeros for the other ranks' slices; two
 cheaper collectives give the same replicated result or keep it sharded:
 
-* ``reduce="allreduce"``  NCCL all-reduce(SUM) of the full fp32 accumulators
+* ``reduce="allreduce"``  all-reduce(SUM) of the full fp32 accumulators
                           (the prescribed exchange, the headline number);
 * ``reduce="allgather"``  all-gather of each rank's owned slices;
 * ``reduce="none"``       no collective: each rank keeps the gradients of its
                           own slices (sharded).
 
-The collective runs in buckets of slices on a side stream, so bucket ``j``
-reduces while the backward of bucket ``j+1`` runs.
+On CUDA the collective runs in buckets of slices on a side stream, so bucket
+``j`` reduces while the backward of bucket ``j+1`` runs.  Every rank issues
+the same collectives in the same order.  The compute backend is pluggable
+(``kernels``): the default calls the native library; tests substitute a CPU
+implementation to exercise the partition and exchange logic on ``gloo``.
 """
 
 from __future__ import annotations
@@ -28,8 +31,6 @@ from dataclasses import dataclass
 
 import torch
 import torch.distributed as dist
-
-from . import _ops
 
 
 @dataclass
@@ -41,6 +42,8 @@ class ShardPlan:
     rank: int
 
     def __post_init__(self):
+        if self.world < 1 or not 0 <= self.rank < self.world:
+            raise ValueError(f"rank {self.rank} outside a world of {self.world}")
         if self.slices % self.world:
             raise ValueError(f"{self.slices} slices do not split evenly over {self.world} ranks")
 
@@ -57,6 +60,29 @@ class ShardPlan:
         return self.begin + self.per_rank
 
 
+class NativeKernels:
+    """The CUDA path: fused forward, sparse backward, accumulator conversion."""
+
+    def __init__(self):
+        from . import _ops
+
+        self._ops = _ops
+
+    def acc_dtype(self, dtype):
+        return self._ops.acc_dtype(dtype)
+
+    def forward(self, q, k, v, topk, scale):
+        out, idx, lse, _ = self._ops.topk_attn_fwd(q, k, v, topk, scale)
+        return out, idx, lse
+
+    def backward(self, q, k, v, dout, idx, lse, scale, dk_acc, dv_acc, accumulate, dq):
+        self._ops.topk_attn_bwd(q, k, v, dout, idx, lse, scale, dk_acc=dk_acc, dv_acc=dv_acc,
+                                accumulate=accumulate, dq=dq)
+
+    def finalize(self, acc, dtype):
+        return self._ops.finalize_grad(acc, dtype)
+
+
 class ShardedTopKAttention:
     """Reusable buffers and streams for repeated sharded fwd+bwd steps.
 
@@ -66,23 +92,40 @@ class ShardedTopKAttention:
 
     def __init__(self, plan: ShardPlan, m: int, d: int, dv: int, topk: int, dtype: torch.dtype,
                  device: torch.device, *, temperature: float = 1.0, group=None, reduce: str = "allreduce",
-                 buckets: int = 4):
+                 buckets: int = 4, kernels=None):
         if reduce not in ("allreduce", "allgather", "none"):
             raise ValueError(f"unknown reduce mode {reduce!r}")
         self.plan, self.m, self.d, self.dv, self.topk = plan, m, d, dv, topk
-        self.dtype, self.device, self.group, self.reduce = dtype, device, group, reduce
+        self.dtype, self.device, self.group, self.reduce = dtype, torch.device(device), group, reduce
+        self.kernels = kernels if kernels is not None else NativeKernels()
         self.scale = 1.0 / (temperature * math.sqrt(d))
-        acc = _ops.acc_dtype(dtype)
+        acc = self.kernels.acc_dtype(dtype)
         full = plan.slices if reduce != "none" else plan.per_rank
-        self.dk_acc = torch.zeros((full, m, d), device=device, dtype=acc)
-        self.dv_acc = torch.zeros((full, m, dv), device=device, dtype=acc)
+        self.dk_acc = torch.zeros((full, m, d), device=self.device, dtype=acc)
+        self.dv_acc = torch.zeros((full, m, dv), device=self.device, dtype=acc)
         self.buckets = max(1, min(buckets, plan.per_rank)) if plan.world > 1 else 1
-        self.comm_stream = torch.cuda.Stream(device=device) if plan.world > 1 and reduce != "none" else None
+        on_cuda = self.device.type == "cuda"
+        self.comm_stream = (torch.cuda.Stream(device=self.device)
+                            if on_cuda and plan.world > 1 and reduce != "none" else None)
 
     def _bucket_ranges(self):
         per = self.plan.per_rank
         edges = [round(i * per / self.buckets) for i in range(self.buckets + 1)]
         return [(edges[i], edges[i + 1]) for i in range(self.buckets) if edges[i + 1] > edges[i]]
+
+    def _allreduce_bucket(self, lo, hi):
+        # bucket j of every rank, in rank order: the same calls on all ranks
+        for r in range(self.plan.world):
+            s0 = r * self.plan.per_rank
+            dist.all_reduce(self.dk_acc[s0 + lo: s0 + hi], group=self.group)
+            dist.all_reduce(self.dv_acc[s0 + lo: s0 + hi], group=self.group)
+
+    def _allgather(self):
+        b0, b1 = self.plan.begin, self.plan.end
+        own_k = self.dk_acc[b0:b1].clone()
+        own_v = self.dv_acc[b0:b1].clone()
+        dist.all_gather_into_tensor(self.dk_acc, own_k, group=self.group)
+        dist.all_gather_into_tensor(self.dv_acc, own_v, group=self.group)
 
     def step(self, q_rows, keys, values, dout_rows, fwd_timer=None):
         """Forward and backward of this rank's rows.
@@ -92,49 +135,48 @@ class ShardedTopKAttention:
         ``fwd_timer`` (optional) is a pair of CUDA events recorded around the
         forward kernel.
         """
-        plan = self.plan
+        plan, kern = self.plan, self.kernels
         b0, b1 = plan.begin, plan.end
         k_loc, v_loc = keys[b0:b1], values[b0:b1]
         if fwd_timer is not None:
             fwd_timer[0].record()
-        out, idx, lse, _ = _ops.topk_attn_fwd(q_rows, k_loc, v_loc, self.topk, self.scale)
+        out, idx, lse = kern.forward(q_rows, k_loc, v_loc, self.topk, self.scale)
         if fwd_timer is not None:
             fwd_timer[1].record()
+        exchange = plan.world > 1 and self.reduce != "none"
         local = 0 if self.reduce == "none" else b0
-        if self.reduce == "allreduce" and plan.world > 1:
+        accumulate = self.reduce == "allreduce" and plan.world > 1
+        if accumulate:
             self.dk_acc.zero_()
             self.dv_acc.zero_()
-        main = torch.cuda.current_stream(self.device)
+        main = torch.cuda.current_stream(self.device) if self.comm_stream is not None else None
         dq = torch.empty_like(q_rows)
-        work = []
+        idx3 = idx.view(plan.per_rank, -1, self.topk)
+        lse2 = lse.view(plan.per_rank, -1)
+        pending = []
         for lo, hi in self._bucket_ranges():
-            _ops.topk_attn_bwd(
-                q_rows[lo:hi], k_loc[lo:hi], v_loc[lo:hi], dout_rows[lo:hi], idx.view(plan.per_rank, -1, self.topk)[lo:hi],
-                lse.view(plan.per_rank, -1)[lo:hi], self.scale,
-                dk_acc=self.dk_acc[local + lo: local + hi], dv_acc=self.dv_acc[local + lo: local + hi],
-                accumulate=(self.reduce == "allreduce" and plan.world > 1), dq=dq[lo:hi],
-            )
-            if self.comm_stream is not None and self.reduce == "allreduce":
-                ev = torch.cuda.Event()
-                ev.record(main)
-                work.append((lo, hi, ev))
-        if self.comm_stream is not None:
+            kern.backward(q_rows[lo:hi], k_loc[lo:hi], v_loc[lo:hi], dout_rows[lo:hi], idx3[lo:hi], lse2[lo:hi],
+                          self.scale, self.dk_acc[local + lo: local + hi], self.dv_acc[local + lo: local + hi],
+                          accumulate, dq[lo:hi])
+            if exchange and self.reduce == "allreduce":
+                if self.comm_stream is not None:
+                    ev = torch.cuda.Event()
+                    ev.record(main)
+                    pending.append((lo, hi, ev))
+                else:
+                    self._allreduce_bucket(lo, hi)
+        if exchange and self.comm_stream is not None:
             with torch.cuda.stream(self.comm_stream):
                 if self.reduce == "allreduce":
-                    for lo, hi, ev in work:
+                    for lo, hi, ev in pending:
                         self.comm_stream.wait_event(ev)
-                        # the same slice range of every rank: bucket j of all ranks
-                        for r in range(plan.world):
-                            s0 = r * plan.per_rank
-                            dist.all_reduce(self.dk_acc[s0 + lo: s0 + hi], group=self.group)
-                            dist.all_reduce(self.dv_acc[s0 + lo: s0 + hi], group=self.group)
-                else:  # allgather of owned slices
+                        self._allreduce_bucket(lo, hi)
+                else:
                     self.comm_stream.wait_stream(main)
-                    own_k = self.dk_acc[b0:b1].clone()
-                    own_v = self.dv_acc[b0:b1].clone()
-                    dist.all_gather_into_tensor(self.dk_acc, own_k, group=self.group)
-                    dist.all_gather_into_tensor(self.dv_acc, own_v, group=self.group)
+                    self._allgather()
             main.wait_stream(self.comm_stream)
-        dk = _ops.finalize_grad(self.dk_acc, self.dtype)
-        dv = _ops.finalize_grad(self.dv_acc, self.dtype)
+        elif exchange and self.reduce == "allgather":
+            self._allgather()
+        dk = kern.finalize(self.dk_acc, self.dtype)
+        dv = kern.finalize(self.dv_acc, self.dtype)
         return out, dq, dk, dv

@@ -438,3 +438,24 @@ def test_full_size_bf16_sampled_rows(b, h, n, m, d, k):
         o, idx, _, _ = oracle.topk_attention_forward(qs, ks, vs, k, 1 / math.sqrt(d))
         got = out.reshape(b * h, n, d)[s, rows].float().cpu().numpy()
         np.testing.assert_allclose(got, o[0], rtol=2e-2, atol=2e-2)
+
+
+def test_routed_bf16_backward_vs_oracle():
+    torch.manual_seed(4)
+    n, d, e, m, k = 2048, 64, 4, 512, 16
+    q = torch.randn(n, d)
+    atoms = torch.randn(e, m, d) / 8
+    logits = torch.randn(n, e)
+    do = torch.randn(n, d)
+    qd = q.to(DEV, torch.bfloat16).requires_grad_(True)
+    ad = atoms.to(DEV, torch.bfloat16).requires_grad_(True)
+    out = routed_dictionary_attention(qd, ad, logits.to(DEV), k, 1.0)
+    dq, da = torch.autograd.grad((out.float() * do.to(DEV)).sum(), (qd, ad))
+    qr, ar = qd.detach().float().cpu().numpy(), ad.detach().float().cpu().numpy()
+    experts = oracle.moe_route_top1(logits.numpy())
+    o, idx, _ = oracle.moe_topk_attention_forward(qr, ar, experts, k, 1.0)
+    np.testing.assert_allclose(out.detach().float().cpu().numpy(), o, rtol=2e-2, atol=2e-2)
+    gq, ga = oracle.moe_topk_attention_backward(qr, ar, experts, idx, do.numpy(), 1.0)
+    for got, exp in ((dq, gq), (da, ga)):
+        got = got.float().cpu().numpy()
+        assert np.abs(got - exp).max() <= 2e-2 * max(1.0, np.abs(exp).max())
