@@ -196,7 +196,7 @@ def run_native_arm(args):
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
         group = dist.group.WORLD
 
-    c = CFG
+    c = dict(CFG, B=args.batch, H=args.heads)
     slices = c["B"] * c["H"]
     plan = ShardPlan(slices, world, rank)
     gen = torch.Generator(device=dev).manual_seed(1234)
@@ -281,13 +281,16 @@ def run_native_arm(args):
     fwd_flops_per_launch = flops_tc / world
     achieved = fwd_flops_per_launch / (fwd_ms / 1000.0) / 1e12
     peak_tc = peaks["bf16_tflops_sustained"]
-    traffic = load_traffic().get("fused_fwd_cfg4")
+    # ncu-measured DRAM bytes of one headline forward launch (profiles/traffic.json)
+    traffic = load_traffic().get("fused_fwd_cfg4") if (c["B"], c["H"], world) == (CFG["B"], CFG["H"], 1) else None
     t_roof = max(flops_tc / world / (peak_tc * 1e12), bytes_fb / world / (peaks["hbm_gbs"] * 1e9))
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, **CFG, "parallelism": f"rows{world}", "reduce": args.reduce,
+        "config": {"workload": WORKLOAD if (args.batch, args.heads) == (CFG["B"], CFG["H"]) else
+                   f"sharded bf16 fwd+bwd, B={args.batch} H={args.heads} N=M=16384 d=64 k=64",
+                   **c, "parallelism": f"rows{world}", "reduce": args.reduce,
                    "l2": "inputs larger than L2 (268 MB per tensor)"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tc, "unit": "TFLOP/s",
                      "frac": achieved / peak_tc, "traffic": traffic, "kernel": "fused forward",
@@ -324,6 +327,8 @@ def main():
     ap.add_argument("--impl", choices=["native", "reference"], default="native")
     ap.add_argument("--reduce", choices=["allreduce", "allgather", "none"], default="allreduce")
     ap.add_argument("--buckets", type=int, default=4)
+    ap.add_argument("--batch", type=int, default=CFG["B"], help="B (default: the headline 16)")
+    ap.add_argument("--heads", type=int, default=CFG["H"], help="H (default: the headline 8)")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--ref-rows", type=int, default=256)
     ap.add_argument("--skip-e2e", action="store_true")
