@@ -154,17 +154,17 @@ __device__ void compact_list(float* cv, uint16_t* ci, int r, int& cnt, float& ta
       }
     t = t + 4 > 12 ? 12 : t + 4;
   }
-  int w = 0;
+  uint32_t w = 0;
+  const uint32_t cvb = smem_addr(cv) + 4u * r, cib = smem_addr(ci) + 2u * r;
   for (int s = 0; s < cnt; ++s) {
     const float x = cv[s * TQ + r];
-    const uint16_t i = ci[s * TQ + r];
-    if (!(x < pivot)) {
-      cv[w * TQ + r] = x;
-      ci[w * TQ + r] = i;
-      ++w;
-    }
+    const uint32_t i = ci[s * TQ + r];
+    const uint32_t keep = (uint32_t)!(x < pivot);
+    st_shared_f32_if(cvb + w * (4u * TQ), x, keep);
+    st_shared_u16_if(cib + w * (2u * TQ), i, keep);
+    w += keep;
   }
-  cnt = w;
+  cnt = (int)w;
   tau = pivot;
 }
 
@@ -190,20 +190,18 @@ __device__ void trim_to_topk(float* cv, uint16_t* ci, int r, int& cnt, float& ta
 }
 
 // Append every key of a 32-key chunk whose score passes !(x <= tau) to the
-// row's list.  Branch-free: each key's slot is the running count, and the
-// store is predicated on the test.
+// row's list.  Branch-free: each key's slot is the running count and the
+// stores are predicated instructions, so lanes never diverge per key.
 __device__ __forceinline__ void append_chunk(const uint32_t* v, int valid, float tau, int key0, float* cv,
                                              uint16_t* ci, int r, int& cnt) {
   uint32_t slot = (uint32_t)cnt;
+  const uint32_t cvb = smem_addr(cv) + 4u * r, cib = smem_addr(ci) + 2u * r;
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
     const float x = __uint_as_float(v[i]);
     const uint32_t take = (uint32_t)(i < valid && !(x <= tau));
-    const uint32_t off = slot * TQ + r;
-    if (take) {
-      cv[off] = x;
-      ci[off] = (uint16_t)(key0 + i);
-    }
+    st_shared_f32_if(cvb + slot * (4u * TQ), x, take);
+    st_shared_u16_if(cib + slot * (2u * TQ), (uint32_t)(key0 + i), take);
     slot += take;
   }
   cnt = (int)slot;

@@ -174,6 +174,23 @@ __host__ __device__ constexpr uint32_t instr_desc_f16(bool bf16, int m, int n) {
          ((uint32_t)(m >> 4) << 24);
 }
 
+// Shared-memory stores executed only when `p` is nonzero, as predicated
+// instructions rather than branches (no divergence per element).
+__device__ __forceinline__ void st_shared_f32_if(uint32_t addr, float v, uint32_t p) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.shared.f32 [%0], %1;\n\t}" ::"r"(addr), "f"(v),
+      "r"(p)
+      : "memory");
+}
+
+__device__ __forceinline__ void st_shared_u16_if(uint32_t addr, uint32_t v, uint32_t p) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\t.reg .b16 h;\n\tcvt.u16.u32 h, %1;\n\tsetp.ne.b32 q, %2, 0;\n\t"
+      "@q st.shared.u16 [%0], h;\n\t}" ::"r"(addr),
+      "r"(v), "r"(p)
+      : "memory");
+}
+
 // Three-input maximum that propagates NaN (a NaN score ranks above all).
 __device__ __forceinline__ float max3_nan(float a, float b, float c) {
   float r;
