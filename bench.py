@@ -296,7 +296,8 @@ def run_native_arm(args):
                      "frac": achieved / peak_tc, "traffic": traffic, "kernel": "fused forward",
                      "fwd_ms": fwd_ms, "peak_source": f"{peaks['source']} bf16_tflops_sustained",
                      "step_frac_combined": t_roof / (ms_per_step / 1000.0)},
-        "gpu_launches": 4 * args.steps,
+        # this library's kernels per step: forward, one backward per bucket, two finalizes
+        "gpu_launches": (1 + len(runner._bucket_ranges()) + 2) * args.steps,
     }
     if e2e is not None:
         line["e2e"] = e2e

@@ -459,3 +459,30 @@ def test_routed_bf16_backward_vs_oracle():
     for got, exp in ((dq, gq), (da, ga)):
         got = got.float().cpu().numpy()
         assert np.abs(got - exp).max() <= 2e-2 * max(1.0, np.abs(exp).max())
+
+
+@pytest.mark.parametrize("topk", [1, 128])
+def test_tie_stress_full_configuration_sampled_rows_bit_exact(topk):
+    # B=4, H=4, N=M=8192, d=128, fp32; Q and K on a 1/8 grid clamped to [-4, 4] so every
+    # dot product is exact; scores rounded to the 1/64 grid before selection (many exact
+    # ties); the lower key index must win every tie.
+    from sparsedict_b200 import _ops
+
+    bh, n, m, d = 16, 8192, 8192, 128
+    gen = torch.Generator(device=DEV).manual_seed(55 + topk)
+    q = torch.clamp(torch.round(torch.randn(bh, n, d, device=DEV, generator=gen) * 8) / 8, -4, 4)
+    k = torch.clamp(torch.round(torch.randn(bh, m, d, device=DEV, generator=gen) * 8) / 8, -4, 4)
+    v = torch.randn(bh, m, d, device=DEV, generator=gen)
+    out, idx, _, _ = _ops.topk_attn_fwd(q, k, v, topk, 1 / math.sqrt(d), score_grid=64)
+    rng = np.random.default_rng(topk)
+    for s in rng.choice(bh, 3, replace=False):
+        rows = rng.choice(n, 64, replace=False)
+        qs = q[s, rows].cpu().numpy()[None]
+        ks = k[s].cpu().numpy()[None]
+        scores = oracle.quantize_to_grid(qs, ks, d, 64)
+        _, exp_idx = oracle.topk_order(scores, topk)
+        got = idx.view(bh, n, topk)[s, rows].cpu().numpy()
+        assert np.array_equal(got, exp_idx[0])
+        o, _, _, _ = oracle.topk_attention_forward(qs, ks, v[s].cpu().numpy()[None], topk, 1 / math.sqrt(d),
+                                                   scores=scores)
+        np.testing.assert_allclose(out.view(bh, n, d)[s, rows].cpu().numpy(), o[0], atol=1e-5, rtol=1e-5)
