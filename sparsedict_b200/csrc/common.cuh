@@ -92,6 +92,24 @@ __device__ __forceinline__ int next_pow2_dev(int x) {
   return p;
 }
 
+// Sort the first `count` candidates of one row (padding to a power of two
+// with sentinels) and keep the best min(count, topk).  Sets the row's
+// threshold once topk candidates are held.
+template <typename Acc>
+__device__ int compact_row(Acc* vals, int* idx, int count, int topk, Acc* tau, int lane) {
+  const int P = next_pow2_dev(count);
+  for (int i = count + lane; i < P; i += kWarp) {
+    vals[i] = neg_inf<Acc>();
+    idx[i] = kPadIndex;
+  }
+  __syncwarp();
+  warp_bitonic_sort(vals, idx, P, lane);
+  const int kept = count < topk ? count : topk;
+  if (kept == topk && lane == 0) *tau = vals[topk - 1];
+  __syncwarp();
+  return kept;
+}
+
 // --------------------------------------------------------- device status ---
 // Bits set by kernels when they meet data they refuse to act on (an index
 // outside [0, M) handed to the aggregate op, for example).  Read and cleared

@@ -58,24 +58,6 @@ __device__ __forceinline__ void load4<double>(const double* p, double (&r)[4]) {
   r[0] = a.x; r[1] = a.y; r[2] = b.x; r[3] = b.y;
 }
 
-// Sort the first `count` candidates of one row (padding to a power of two
-// with sentinels) and keep the best min(count, topk).  Sets the row's
-// threshold once topk candidates are held.
-template <typename Acc>
-__device__ int compact_row(Acc* vals, int* idx, int count, int topk, Acc* tau, int lane) {
-  const int P = next_pow2_dev(count);
-  for (int i = count + lane; i < P; i += kWarp) {
-    vals[i] = neg_inf<Acc>();
-    idx[i] = kPadIndex;
-  }
-  __syncwarp();
-  warp_bitonic_sort(vals, idx, P, lane);
-  const int kept = count < topk ? count : topk;
-  if (kept == topk && lane == 0) *tau = vals[topk - 1];
-  __syncwarp();
-  return kept;
-}
-
 template <typename T>
 __global__ void __launch_bounds__(NT) fused_fwd_generic(FwdArgs<typename AccOf<T>::type> a) {
   using Acc = typename AccOf<T>::type;

@@ -1,31 +1,48 @@
 // Fused top-k attention forward on the 5th-generation tensor cores (sm_100a).
 //
-// One CTA owns 128 query rows of one (b, h) slice (d = dv = 64, bf16 or fp16)
-// and streams the slice's keys in tiles of 128:
+// One CTA owns 256 query rows of one (b, h) slice (d = dv = 64, bf16 or fp16)
+// as two 128-row tiles, A and B, and streams the slice's keys in tiles of 128:
 //
-//   warp 0      TMA producer: the Q tile once, then K tiles into a 3-stage
-//               ring of 128-byte-swizzled shared-memory buffers;
-//   warp 1      allocates 256 TMEM columns and issues tcgen05.mma
-//               (M=128, N=128, K=16 x 4) of S = Q·Kᵀ into one of two TMEM
-//               accumulators, committing to the "S full" and "stage free"
-//               mbarriers;
-//   warps 4..7  selection: thread i owns query row i (TMEM lane i), reads
-//               its 128 scores of the tile with tcgen05.ld 32 columns at a
-//               time, keeps every key that beats the row's running
-//               threshold in a shared-memory candidate list and, when the
-//               list could overflow, raises the threshold with a sampled
-//               pivot and compacts the list.  The score row never reaches
-//               global memory.
+//   warp 0       TMA producer: both Q tiles once, then K tiles into a 2-stage
+//                ring of 128-byte-swizzled shared-memory buffers;
+//   warp 1       allocates 512 TMEM columns and issues tcgen05.mma
+//                (M=128, N=128, K=16 x 4) of S_A = Q_A·Kᵀ and S_B = Q_B·Kᵀ
+//                for every K tile, each into one of two TMEM accumulators of
+//                its query tile, committing to "S full" / "stage free"
+//                mbarriers;
+//   warps 4..7   selection for tile A, warps 8..11 for tile B (two selection
+//                warps per SM sub-partition): thread i of a group owns query
+//                row i of its tile (TMEM lane i), reads its 128 scores of the
+//                K tile with tcgen05.ld, and appends every key that beats the
+//                row's running threshold to a slot-major shared-memory list.
 //
-// After the last tile each selection thread trims its list to exactly k
-// keys (lowest-rank-first removal; ties at the k-th score keep the lower
-// key index), writes the indices, the row LSE, and the softmax-weighted
-// sum of the gathered value rows.  The k indices of a row are written in no
-// particular order; the set is the reference's top-k set.
+// A list entry is 4 bytes: the upper 16 bits of the fp32 score's bit pattern
+// (its bf16 truncation, which names the score's bf16 "bucket") and the 16-bit
+// key index.  When a list could overflow it is compacted with a bucket pivot:
+// the highest of 16 sampled buckets that at least k listed keys reach.  Keys
+// below that bucket are dropped and the row's threshold becomes the lowest
+// score of the bucket; both steps are exact (no top-k key is ever dropped).
+// A row whose list cannot be shrunk that way (more than ~100 listed keys
+// share the cut bucket, which needs heavily tied scores) is marked and
+// re-selected exactly at the end, see below.
+//
+// After the last tile the survivors of each row (at most 96) are re-scored
+// exactly: the row's Q values go to registers, the Q/K buffers are released
+// (named barrier of the 256 selection threads), the key indices move there,
+// and each candidate's fp32 score is recomputed from the gathered key row by
+// one fixed FMA order.  The exact cut to k keys uses order-preserving 64-bit
+// keys (score, complemented index), so ties keep the lower key index.  Then
+// the row LSE, the k indices (in no particular order; the set is the
+// reference's top-k set) and the softmax-weighted sum of the gathered value
+// rows are written.
+//
+// Marked rows are re-selected by their warp: lanes score 32 keys at a time
+// with the same FMA order and keep an exact candidate list sorted by a warp
+// bitonic network, as the CUDA-core kernel does.
 //
 // Selection runs on the raw dot products; scale = 1/(T·sqrt(d)) > 0 is
-// applied in the epilogue (for d = 64 the scale is a power of two, so the
-// order is exactly that of the scaled scores).
+// applied in the epilogue (for d = 64 and T a power of two the scale is a
+// power of two, so the order is exactly that of the scaled scores).
 #include <cuda.h>
 
 #include <type_traits>
@@ -39,25 +56,39 @@ namespace {
 
 using namespace sm100;
 
-constexpr int TQ = 128;  // query rows per CTA (TMEM lanes)
-constexpr int TK = 128;  // keys per score tile (MMA N)
-constexpr int D = 64;    // feature width (one 128-byte swizzle row)
-constexpr int KSTAGES = 3;
-constexpr int CAP = 192;  // candidate slots per row
-constexpr int NT = 256;
-constexpr uint32_t TMEM_COLS = 256;
-constexpr uint32_t TILE_BYTES = TK * D * 2;
+constexpr int TQ = 128;         // query rows per tile (TMEM lanes, MMA M)
+constexpr int NTILE = 2;        // query tiles per CTA
+constexpr int RS = TQ * NTILE;  // rows per CTA; row stride of the slot-major lists
+constexpr int TK = 128;         // keys per score tile (MMA N)
+constexpr int D = 64;           // feature width (one 128-byte swizzle row)
+constexpr int KSTAGES = 2;
+constexpr int CAP = 160;        // list slots per row
+constexpr int FINAL_CAP = 96;   // most candidates a row may carry into exact re-scoring
+constexpr int FIX_CAP = 128;    // exact list of a row re-selected by one warp
+constexpr int NT = 384;
+constexpr int NSEL = 8 * kWarp;  // selection threads
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t TILE_BYTES = TK * D * 2;  // a K tile, also a Q tile
 
 constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + TQ * D * 2;
-constexpr int OFF_CV = OFF_K + KSTAGES * (int)TILE_BYTES;
-constexpr int OFF_CI = OFF_CV + CAP * TQ * 4;
-constexpr int OFF_BAR = OFF_CI + CAP * TQ * 2;
-constexpr int NBARS = 1 + 2 * KSTAGES + 4;
+constexpr int OFF_K = OFF_Q + NTILE * (int)TILE_BYTES;
+constexpr int OFF_LIST = OFF_K + KSTAGES * (int)TILE_BYTES;
+constexpr int OFF_BAR = OFF_LIST + CAP * RS * 4;
+constexpr int NBARS = 1 + 2 * KSTAGES + 4 * NTILE;
 constexpr int OFF_MISC = OFF_BAR + NBARS * 8;
 constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
+// The Q/K region once the stream is over: key indices of the re-scored
+// candidates, then one exact re-selection buffer per selection warp.
+constexpr int OFF_STAGE = 0;
+constexpr int OFF_FIX = OFF_STAGE + FINAL_CAP * RS * 2;
+constexpr int FIX_BYTES = FIX_CAP * 8 + 16;
+static_assert(OFF_FIX + 8 * FIX_BYTES <= OFF_LIST, "post-stream buffers exceed the Q/K region");
+static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
+static_assert(OFF_BAR % 8 == 0, "mbarrier alignment");
 
 struct TcArgs {
+  const void* q;
+  const void* k;
   const void* v;
   void* out;
   int32_t* top_idx;
@@ -69,23 +100,38 @@ struct TcArgs {
   unsigned int* status;
 };
 
-// ----------------------------------------------------------- selection ---
-// Candidate list of row r: slots s = 0..cnt-1 at cv[s*TQ + r] / ci[s*TQ + r]
-// (row-fastest, so the 32 lanes of a warp hit 32 distinct banks).
+// ---------------------------------------------------- bucketed list entries ---
+// Order-preserving form of an entry: the high 16 bits order the buckets like
+// their scores (negative scores complemented); the low 16 bits are not used.
+__device__ __forceinline__ uint32_t ord_entry(uint32_t e) {
+  return e ^ ((uint32_t)((int32_t)e >> 31) | 0x80000000u);
+}
 
-// Order-preserving 64-bit rank key: larger key = ranks higher.  The high
-// word maps the float onto an unsigned order (NaN highest, -0 == +0); the
-// low word is the complemented key index, so equal scores rank the lower
-// index higher.
-__device__ __forceinline__ uint64_t rank_key(float x, uint32_t idx) {
-  uint32_t u;
-  if (x != x) {
-    u = 0xffffffffu;
-  } else {
-    u = __float_as_uint(x + 0.0f);
-    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  }
-  return ((uint64_t)u << 32) | (uint64_t)(0xffffffffu - idx);
+// Threshold after a compaction that kept every key of bucket >= p (p is an
+// ordered bucket << 16): a later key x is dropped iff !(x > tau), i.e. iff its
+// ordered score is <= p.  At least k kept keys rank at or above p, and a later
+// key equal to them loses the index tie, so the drop is exact.
+__device__ __forceinline__ float tau_of_bucket(uint32_t p) {
+  if (p >= 0xff800000u) return __int_as_float(0x7f800000);  // only NaN ranks higher
+  if (p < 0x00800000u) return __int_as_float(0x7fc00000);   // at or below -inf: admit all
+  return __uint_as_float((p & 0x80000000u) ? (p & 0x7fffffffu) : ~p);
+}
+
+__device__ __forceinline__ void sort16_desc(uint32_t (&x)[16]) {
+#pragma unroll
+  for (int size = 2; size <= 16; size <<= 1)
+#pragma unroll
+    for (int st = size >> 1; st > 0; st >>= 1)
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int j = i ^ st;
+        if (j > i) {
+          const bool desc = (i & size) == 0;
+          const uint32_t hi = max(x[i], x[j]), lo = min(x[i], x[j]);
+          x[i] = desc ? hi : lo;
+          x[j] = desc ? lo : hi;
+        }
+      }
 }
 
 __device__ __forceinline__ void sort16_desc(float (&x)[16]) {
@@ -105,47 +151,49 @@ __device__ __forceinline__ void sort16_desc(float (&x)[16]) {
       }
 }
 
-// Counts of listed values >= each of four pivots, in one pass.
-__device__ __forceinline__ void count4(const float* cv, int r, int cnt, const float (&p)[4], int (&c)[4]) {
-  c[0] = c[1] = c[2] = c[3] = 0;
-#pragma unroll 4
-  for (int s = 0; s < cnt; ++s) {
-    const float x = cv[s * TQ + r];
+template <typename V>
+__device__ __forceinline__ V pick16(const V (&x)[16], int want) {
+  V v = x[15];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) c[q] += !(x < p[q]);
-  }
+  for (int j = 0; j < 16; ++j)
+    if (j == want) v = x[j];
+  return v;
 }
 
-// Raise the row's threshold to the highest of 16 sampled list values that at
-// least `topk` listed keys meet (keys seen later rank below these on equal
-// scores, so `!(s <= tau)` stays exact) and drop the keys below it.  The
-// search starts near the sample rank expected to keep about
-// topk + slack*cnt/16 keys and tests four candidate pivots per pass.
-__device__ void compact_list(float* cv, uint16_t* ci, int r, int& cnt, float& tau, int topk, int slack) {
-  float smp[16];
+// Shrink row R's list to the keys whose bucket reaches the highest of 16
+// sampled buckets that at least `topk` listed keys reach (four candidate
+// pivots per counting pass, starting near the sample rank expected to keep
+// topk + slack*cnt/16 keys).  Returns false when no sampled pivot qualifies
+// or nothing would be dropped.  Kept out of line: it runs rarely, and one
+// copy keeps the streaming loop small enough for the instruction cache.
+struct Compacted {
+  int cnt;
+  float tau;
+  bool shrank;
+};
+
+__device__ __noinline__ Compacted compact_bucket(const uint32_t* list_c, int R, int cnt, float tau, int topk,
+                                                 int slack) {
+  uint32_t* list = const_cast<uint32_t*>(list_c);
+  uint32_t smp[16];
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const float x = cv[((j * cnt) >> 4) * TQ + r];
-    smp[j] = (x != x) ? __int_as_float(0x7f800000) : x;
-  }
+  for (int j = 0; j < 16; ++j) smp[j] = ord_entry(list[((j * cnt) >> 4) * RS + R]) & 0xffff0000u;
   sort16_desc(smp);
   int t = (16 * topk) / (cnt > 0 ? cnt : 1) + slack - 1;
   t = t < 0 ? 0 : (t > 12 ? 12 : t);
-  float pivot = __int_as_float(0xff800000);
+  uint32_t pivot = 0;
   bool found = false;
   for (int pass = 0; pass < 4 && !found; ++pass) {
-    float p[4];
+    uint32_t p[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int want = t + q;
-      float v = smp[15];
+    for (int q = 0; q < 4; ++q) p[q] = pick16(smp, t + q);
+    int c[4] = {0, 0, 0, 0};
+#pragma unroll 4
+    for (int s = 0; s < cnt; ++s) {
+      const uint32_t o = ord_entry(list[s * RS + R]);
 #pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (j == want) v = smp[j];
-      p[q] = v;
+      for (int q = 0; q < 4; ++q) c[q] += (int)(o >= p[q]);
     }
-    int c[4];
-    count4(cv, r, cnt, p, c);
 #pragma unroll
     for (int q = 3; q >= 0; --q)
       if (c[q] >= topk) {
@@ -154,60 +202,35 @@ __device__ void compact_list(float* cv, uint16_t* ci, int r, int& cnt, float& ta
       }
     t = t + 4 > 12 ? 12 : t + 4;
   }
+  if (!found) return Compacted{cnt, tau, false};
   uint32_t w = 0;
-  const uint32_t cvb = smem_addr(cv) + 4u * r, cib = smem_addr(ci) + 2u * r;
+  const uint32_t base = smem_addr(list) + 4u * R;
   for (int s = 0; s < cnt; ++s) {
-    const float x = cv[s * TQ + r];
-    const uint32_t i = ci[s * TQ + r];
-    const uint32_t keep = (uint32_t)!(x < pivot);
-    st_shared_f32_if(cvb + w * (4u * TQ), x, keep);
-    st_shared_u16_if(cib + w * (2u * TQ), i, keep);
+    const uint32_t e = list[s * RS + R];
+    const uint32_t keep = (uint32_t)(ord_entry(e) >= pivot);
+    st_shared_u32_if(base + w * (4u * RS), e, keep);
     w += keep;
   }
-  cnt = (int)w;
-  tau = pivot;
-}
-
-// Remove lowest-ranked keys until exactly `topk` remain; the survivors are
-// the list's top-k by (score descending, index ascending).
-__device__ void trim_to_topk(float* cv, uint16_t* ci, int r, int& cnt, float& tau, int topk) {
-  while (cnt > topk) {
-    uint64_t worst = ~0ull;
-    int pos = 0;
-#pragma unroll 4
-    for (int s = 0; s < cnt; ++s) {
-      const uint64_t key = rank_key(cv[s * TQ + r], ci[s * TQ + r]);
-      const bool lower = key < worst;
-      worst = lower ? key : worst;
-      pos = lower ? s : pos;
-    }
-    tau = cv[pos * TQ + r];
-    const int last = cnt - 1;
-    cv[pos * TQ + r] = cv[last * TQ + r];
-    ci[pos * TQ + r] = ci[last * TQ + r];
-    cnt = last;
-  }
+  // both thresholds are exact; keep the higher
+  return Compacted{(int)w, fmaxf(tau, tau_of_bucket(pivot)), (int)w < cnt};
 }
 
 // Append every key of a 32-key chunk whose score passes !(x <= tau) to the
 // row's list.  Branch-free: each key's slot is the running count and the
-// stores are predicated instructions, so lanes never diverge per key.
-__device__ __forceinline__ void append_chunk(const uint32_t* v, int valid, float tau, int key0, float* cv,
-                                             uint16_t* ci, int r, int& cnt) {
+// store is a predicated instruction, so lanes never diverge per key.
+__device__ __forceinline__ void append_chunk(const uint32_t* v, int valid, float tau, uint32_t key0,
+                                             uint32_t base, int& cnt) {
   uint32_t slot = (uint32_t)cnt;
-  const uint32_t cvb = smem_addr(cv) + 4u * r, cib = smem_addr(ci) + 2u * r;
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
-    const float x = __uint_as_float(v[i]);
-    const uint32_t take = (uint32_t)(i < valid && !(x <= tau));
-    st_shared_f32_if(cvb + slot * (4u * TQ), x, take);
-    st_shared_u16_if(cib + slot * (2u * TQ), (uint32_t)(key0 + i), take);
+    const uint32_t take = (uint32_t)(i < valid && !(__uint_as_float(v[i]) <= tau));
+    st_shared_u32_if(base + slot * (4u * RS), __byte_perm(key0 + (uint32_t)i, v[i], 0x7610), take);
     slot += take;
   }
   cnt = (int)slot;
 }
 
-__device__ __forceinline__ float chunk_max(const uint32_t (&v)[32]) {
+__device__ __forceinline__ float chunk_max(const uint32_t* v) {
   float a[11];
 #pragma unroll
   for (int g = 0; g < 10; ++g)
@@ -219,29 +242,226 @@ __device__ __forceinline__ float chunk_max(const uint32_t (&v)[32]) {
   return max_nan(max3_nan(b0, b1, b2), b3);
 }
 
+// ------------------------------------------------------- exact re-scoring ---
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& u, float* f) {
+  const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int h = 0; h < 8; ++h) f[h] = to_acc(e[h]);
+}
+
+// The one fp32 score of this kernel's exact stages: four FMA chains (feature
+// f feeds chain f mod 4) summed pairwise.
+__device__ __forceinline__ float dot64_regs(const float (&q)[D], const uint4 (&u)[8], bool bf16) {
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    float f[8];
+    if (bf16)
+      unpack8<__nv_bfloat16>(u[c], f);
+    else
+      unpack8<__half>(u[c], f);
+#pragma unroll
+    for (int h = 0; h < 8; ++h) acc[h & 3] = fmaf(q[c * 8 + h], f[h], acc[h & 3]);
+  }
+  return (acc[0] + acc[1]) + (acc[2] + acc[3]);
+}
+
+template <typename T>
+__device__ __forceinline__ void load_row(const T* row, uint4 (&u)[8]) {
+  const uint4* p = reinterpret_cast<const uint4*>(row);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) u[c] = __ldg(p + c);
+}
+
+// Exact cut on re-scored candidates (fp32 scores in cv, key indices in ci,
+// both slot-major with stride RS).  Raise a pivot as compact_bucket does,
+// with exact scores: keep the keys scoring at least the highest of 16
+// sampled scores that >= topk candidates meet.
+__device__ __noinline__ int compact_exact(float* cv, uint16_t* ci, int R, int cnt, int topk) {
+  float smp[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float x = cv[((j * cnt) >> 4) * RS + R];
+    smp[j] = (x != x) ? __int_as_float(0x7f800000) : x;
+  }
+  sort16_desc(smp);
+  int t = (16 * topk) / (cnt > 0 ? cnt : 1);
+  t = t > 12 ? 12 : t;
+  float pivot = __int_as_float(0xff800000);
+  bool found = false;
+  for (int pass = 0; pass < 4 && !found; ++pass) {
+    float p[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) p[q] = pick16(smp, t + q);
+    int c[4] = {0, 0, 0, 0};
+#pragma unroll 4
+    for (int s = 0; s < cnt; ++s) {
+      const float x = cv[s * RS + R];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) c[q] += !(x < p[q]);
+    }
+#pragma unroll
+    for (int q = 3; q >= 0; --q)
+      if (c[q] >= topk) {
+        pivot = p[q];
+        found = true;
+      }
+    t = t + 4 > 12 ? 12 : t + 4;
+  }
+  if (!found) return cnt;
+  uint32_t w = 0;
+  const uint32_t cvb = smem_addr(cv) + 4u * R, cib = smem_addr(ci) + 2u * R;
+  for (int s = 0; s < cnt; ++s) {
+    const float x = cv[s * RS + R];
+    const uint32_t i = ci[s * RS + R];
+    const uint32_t keep = (uint32_t)!(x < pivot);
+    st_shared_f32_if(cvb + w * (4u * RS), x, keep);
+    st_shared_u16_if(cib + w * (2u * RS), i, keep);
+    w += keep;
+  }
+  return (int)w;
+}
+
+// Order-preserving 64-bit rank key: larger key = ranks higher.  The high
+// word maps the float onto an unsigned order (NaN highest, -0 == +0); the
+// low word is the complemented key index, so equal scores rank the lower
+// index higher.
+__device__ __forceinline__ uint64_t rank_key(float x, uint32_t idx) {
+  uint32_t u;
+  if (x != x) {
+    u = 0xffffffffu;
+  } else {
+    u = __float_as_uint(x + 0.0f);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  }
+  return ((uint64_t)u << 32) | (uint64_t)(0xffffffffu - idx);
+}
+
+// Remove lowest-ranked keys until exactly `topk` remain.
+__device__ __noinline__ int trim_exact(float* cv, uint16_t* ci, int R, int cnt, int topk) {
+  while (cnt > topk) {
+    uint64_t worst = ~0ull;
+    int pos = 0;
+#pragma unroll 4
+    for (int s = 0; s < cnt; ++s) {
+      const uint64_t key = rank_key(cv[s * RS + R], ci[s * RS + R]);
+      const bool lower = key < worst;
+      worst = lower ? key : worst;
+      pos = lower ? s : pos;
+    }
+    const int last = cnt - 1;
+    cv[pos * RS + R] = cv[last * RS + R];
+    ci[pos * RS + R] = ci[last * RS + R];
+    cnt = last;
+  }
+  return cnt;
+}
+
+template <typename T>
+__device__ __forceinline__ void store_out_row(const float (&acc)[D], T* orow_t) {
+  uint4* orow = reinterpret_cast<uint4*>(orow_t);
+#pragma unroll
+  for (int q4 = 0; q4 < D / 8; ++q4) {
+    uint4 u;
+    T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+    for (int h = 0; h < 8; ++h) e[h] = from_acc<T>(acc[q4 * 8 + h]);
+    orow[q4] = u;
+  }
+}
+
+// Exact re-selection of one row by a whole warp (rows whose bucketed list
+// could not be shrunk).  fv/fi hold FIX_CAP entries; ftau is one float.
+template <typename T>
+__device__ __noinline__ void reselect_row(const TcArgs& a, int64_t slice, int64_t gr, float* fv, int* fi, float* ftau,
+                             int lane) {
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  float q[D];
+  {
+    uint4 u[8];
+    load_row(static_cast<const T*>(a.q) + gr * D, u);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) unpack8<T>(u[c], &q[c * 8]);
+  }
+  const T* kbase = static_cast<const T*>(a.k) + slice * a.m * D;
+  if (lane == 0) *ftau = __int_as_float(0x7fc00000);
+  __syncwarp();
+  float tau = __int_as_float(0x7fc00000);
+  int c0 = 0;
+  for (int64_t k0 = 0; k0 < a.m; k0 += kWarp) {
+    const int64_t key = k0 + lane;
+    const bool valid = key < a.m;
+    float s = 0.f;
+    if (valid) {
+      uint4 u[8];
+      load_row(kbase + key * D, u);
+      s = dot64_regs(q, u, kBf16);
+    }
+    const bool pass = valid && !(s <= tau);
+    const unsigned bal = __ballot_sync(0xffffffffu, pass);
+    if (pass) {
+      const int pos = c0 + __popc(bal & ((1u << lane) - 1u));
+      fv[pos] = s;
+      fi[pos] = (int)key;
+    }
+    c0 += __popc(bal);
+    if (c0 > FIX_CAP - kWarp) {
+      __syncwarp();
+      c0 = compact_row(fv, fi, c0, a.topk, ftau, lane);
+      tau = *ftau;
+    }
+  }
+  __syncwarp();
+  c0 = compact_row(fv, fi, c0, a.topk, ftau, lane);  // sorted, c0 == topk (topk <= m)
+  const float mxs = fv[0] * a.scale;
+  float part = 0.f;
+  for (int j = lane; j < c0; j += kWarp) part += expf(fv[j] * a.scale - mxs);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  const float lse = mxs + logf(part);
+  for (int j = lane; j < c0; j += kWarp) {
+    a.top_idx[gr * a.topk + j] = fi[j];
+    if (a.top_scores) a.top_scores[gr * a.topk + j] = fv[j] * a.scale;
+  }
+  if (lane == 0) a.lse[gr] = lse;
+  // lane l accumulates features 2l, 2l+1
+  const T* vbase = static_cast<const T*>(a.v) + slice * a.m * D;
+  float o0 = 0.f, o1 = 0.f;
+  for (int j = 0; j < c0; ++j) {
+    const float p = expf(fv[j] * a.scale - lse);
+    const T* vr = vbase + (int64_t)fi[j] * D + 2 * lane;
+    o0 = fmaf(p, to_acc(vr[0]), o0);
+    o1 = fmaf(p, to_acc(vr[1]), o1);
+  }
+  T* orow = static_cast<T*>(a.out) + gr * D + 2 * lane;
+  orow[0] = from_acc<T>(o0);
+  orow[1] = from_acc<T>(o1);
+  __syncwarp();
+}
+
 template <typename T>
 __global__ void __launch_bounds__(NT, 1)
     fused_fwd_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                  TcArgs a) {
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
   uint8_t* qs = sm + OFF_Q;
   uint8_t* ks = sm + OFF_K;
-  float* cv = reinterpret_cast<float*>(sm + OFF_CV);
-  uint16_t* ci = reinterpret_cast<uint16_t*>(sm + OFF_CI);
+  uint32_t* list = reinterpret_cast<uint32_t*>(sm + OFF_LIST);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* k_empty = bars + 1 + KSTAGES;
-  uint64_t* s_full = bars + 1 + 2 * KSTAGES;
-  uint64_t* s_empty = s_full + 2;
+  uint64_t* s_full = bars + 1 + 2 * KSTAGES;  // [tile][buffer]
+  uint64_t* s_empty = s_full + 2 * NTILE;     // [tile][buffer]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + OFF_MISC + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t slice = blockIdx.x / a.tiles_per_slice;
-  const int64_t local0 = (int64_t)(blockIdx.x % a.tiles_per_slice) * TQ;
-  const int rows = (int)((a.n - local0) < TQ ? (a.n - local0) : TQ);
+  const int64_t local0 = (int64_t)(blockIdx.x % a.tiles_per_slice) * RS;
   const int64_t row0 = slice * a.n + local0;
   const int ntiles = (int)((a.m + TK - 1) / TK);
 
@@ -251,7 +471,7 @@ __global__ void __launch_bounds__(NT, 1)
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < 2 * NTILE; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&s_empty[b], 4 * kWarp);
     }
@@ -270,8 +490,8 @@ __global__ void __launch_bounds__(NT, 1)
   if (warp == 0) {
     if (lane == 0) {
       int issued = 0;
-      mbar_arrive_expect_tx(q_full, TQ * D * 2);
-      tma_load_2d(qs, &tmap_q, 0, (int)row0, q_full);
+      mbar_arrive_expect_tx(q_full, NTILE * TILE_BYTES);
+      for (int g = 0; g < NTILE; ++g) tma_load_2d(qs + g * TILE_BYTES, &tmap_q, 0, (int)(row0 + g * TQ), q_full);
       for (int t = 0; t < ntiles; ++t) {
         const int s = t % KSTAGES;
         const uint32_t ph = (uint32_t)(t / KSTAGES) & 1u;
@@ -295,128 +515,198 @@ __global__ void __launch_bounds__(NT, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = instr_desc_f16(sizeof(T) == 2 && !std::is_same<T, __half>::value, TQ, TK);
+      const uint32_t idesc = instr_desc_f16(kBf16, TQ, TK);
       const uint32_t q_addr = smem_addr(qs);
-      int committed = -1;
+      uint64_t* last_bar = nullptr;  // barrier of the last commit, for the abort path
+      uint32_t last_ph = 0;
       if (mbar_wait(q_full, 0, abort_flag)) {
         for (int t = 0; t < ntiles; ++t) {
           const int s = t % KSTAGES, b = t & 1;
+          const uint32_t ph_s = ((uint32_t)(t >> 1) & 1u);
           if (!mbar_wait(&k_full[s], (uint32_t)(t / KSTAGES) & 1u, abort_flag)) break;
-          if (!mbar_wait(&s_empty[b], ((uint32_t)(t >> 1) & 1u) ^ 1u, abort_flag)) break;
-          tc_fence_after();
           const uint32_t k_addr = smem_addr(ks + s * TILE_BYTES);
+          bool stop = false;
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            mma_f16(tmem + b * TK, smem_desc_k128(q_addr + kk * 32), smem_desc_k128(k_addr + kk * 32), idesc,
-                    kk > 0);
+          for (int g = 0; g < NTILE; ++g) {
+            if (!mbar_wait(&s_empty[2 * g + b], ph_s ^ 1u, abort_flag)) {
+              stop = true;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk)
+              mma_f16(tmem + (uint32_t)((2 * g + b) * TK), smem_desc_k128(q_addr + g * TILE_BYTES + kk * 32),
+                      smem_desc_k128(k_addr + kk * 32), idesc, kk > 0);
+            mma_commit(&s_full[2 * g + b]);
+            last_bar = &s_full[2 * g + b];
+            last_ph = ph_s;
+          }
+          if (stop) break;
           mma_commit(&k_empty[s]);
-          mma_commit(&s_full[b]);
-          committed = t;
         }
       }
-      if (*abort_flag && committed >= 0) {
+      if (*abort_flag && last_bar) {
         // wait for the last MMAs before TMEM is released
-        const int b = committed & 1;
         const uint64_t t0 = global_timer();
-        while (!mbar_try_wait(&s_full[b], (uint32_t)(committed >> 1) & 1u) && global_timer() - t0 < kWaitLimitNs) {
+        while (!mbar_try_wait(last_bar, last_ph) && global_timer() - t0 < kWaitLimitNs) {
         }
       }
     }
   } else if (warp >= 4) {
-    const int r = threadIdx.x - 4 * kWarp;  // row within the tile == TMEM lane
-    const uint32_t lane_base = (uint32_t)((warp - 4) * kWarp) << 16;
+    const int wg = (warp - 4) >> 2, quarter = warp & 3;
+    const int rl = quarter * kWarp + lane;  // row within the query tile == TMEM lane
+    const int R = wg * TQ + rl;              // list column
+    const int64_t tile_left = a.n - local0 - (int64_t)wg * TQ;
+    const int rows = (int)(tile_left < 0 ? 0 : (tile_left < TQ ? tile_left : TQ));
+    const uint32_t tm = tmem + ((uint32_t)(quarter * kWarp) << 16) + (uint32_t)(2 * wg * TK);
+    uint64_t* my_full = s_full + 2 * wg;
+    uint64_t* my_empty = s_empty + 2 * wg;
+    const uint32_t lbase = smem_addr(list) + 4u * R;
     float tau = __int_as_float(0x7fc00000);  // "no threshold yet"
     int cnt = 0;
+    bool dead = false;  // list could not be shrunk: exact re-selection at the end
     bool ok = true;
-    for (int t = 0; t < ntiles && ok; ++t) {
+    for (int t = 0; t < ntiles; ++t) {
       const int b = t & 1;
-      if (!mbar_wait(&s_full[b], (uint32_t)(t >> 1) & 1u, abort_flag)) {
-        ok = false;
-        break;
-      }
+      ok = __all_sync(0xffffffffu, mbar_wait(&my_full[b], (uint32_t)(t >> 1) & 1u, abort_flag));
+      if (!ok) break;
       tc_fence_after();
       const int64_t key_tile = (int64_t)t * TK;
       const int tile_valid = (int)((a.m - key_tile) < TK ? (a.m - key_tile) : TK);
-      // All four 32-column chunks of this tile go to registers at once; the
-      // TMEM buffer is released before any selection work so the next MMA
-      // into it can start.
-      uint32_t v[TK];
-#pragma unroll
-      for (int c = 0; c < TK / 32; ++c)
-        tmem_load_32cols(tmem + lane_base + b * TK + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
-      tmem_wait_load();
-      tc_fence_before();
-      mbar_arrive(&s_empty[b]);
-      float mx[TK / 32];
-#pragma unroll
+      // One 32-column chunk at a time, in a loop that is not unrolled: the
+      // loop body is the whole hot path and stays resident in the
+      // instruction cache next to the other group's warps.  The TMEM buffer
+      // is released once its last chunk is in registers.
+#pragma unroll 1
       for (int c = 0; c < TK / 32; ++c) {
-        if (tile_valid >= TK) {
-          mx[c] = chunk_max(*reinterpret_cast<const uint32_t(*)[32]>(&v[c * 32]));
+        uint32_t v[32];
+        tmem_load_32cols(tm + b * TK + c * 32, v);
+        tmem_wait_load();
+        if (c == TK / 32 - 1) {
+          tc_fence_before();
+          mbar_arrive(&my_empty[b]);
+        }
+        const int valid = tile_valid - c * 32;
+        float mx;
+        if (valid >= 32) {
+          mx = chunk_max(v);
         } else {
-          float m = __int_as_float(0xff800000);
+          mx = __int_as_float(0xff800000);
 #pragma unroll
           for (int i = 0; i < 32; ++i)
-            if (c * 32 + i < tile_valid) m = max_nan(m, __uint_as_float(v[c * 32 + i]));
-          mx[c] = m;
+            if (i < valid) mx = max_nan(mx, __uint_as_float(v[i]));
         }
-      }
+        if (!__any_sync(0xffffffffu, !(mx <= tau))) continue;
+        if (__any_sync(0xffffffffu, mx != mx)) {
+          // one NaN pattern, ranked above every number
 #pragma unroll
-      for (int c = 0; c < TK / 32; ++c) {
-        if (!__any_sync(0xffffffffu, !(mx[c] <= tau))) continue;
-        append_chunk(&v[c * 32], tile_valid - c * 32, tau, (int)(key_tile + c * 32), cv, ci, r, cnt);
+          for (int i = 0; i < 32; ++i) v[i] = ((v[i] & 0x7fffffffu) > 0x7f800000u) ? 0x7fffffffu : v[i];
+        }
+        append_chunk(v, dead ? 0 : valid, tau, (uint32_t)(key_tile + c * 32), lbase, cnt);
         // When one lane's list could overflow, every lane holding well over
         // k keys compacts in the same pass: under SIMT the warp pays for the
         // longest list either way.
-        if (__any_sync(0xffffffffu, cnt > CAP - 32)) {
-          if (cnt > a.topk + 32) {
-            compact_list(cv, ci, r, cnt, tau, a.topk, 2);
-            if (cnt > CAP - 32) trim_to_topk(cv, ci, r, cnt, tau, a.topk);
+        if (__any_sync(0xffffffffu, !dead && cnt > CAP - 32)) {
+          if (!dead && cnt > a.topk + 32) {
+            Compacted r = compact_bucket(list, R, cnt, tau, a.topk, 2);
+            if (r.cnt > CAP - 32) r = compact_bucket(list, R, r.cnt, r.tau, a.topk, 1);
+            cnt = r.cnt;
+            tau = r.tau;
+            dead = cnt > CAP - 32;
           }
         }
       }
     }
-    if (ok && !*abort_flag) {
-      if (cnt > a.topk + 16) compact_list(cv, ci, r, cnt, tau, a.topk, 1);
-      trim_to_topk(cv, ci, r, cnt, tau, a.topk);
-      if (r < rows) {
-        const int64_t gr = row0 + r;
-        float mx = cv[r];
-        for (int j = 1; j < a.topk; ++j) mx = fmaxf(mx, cv[j * TQ + r]);
-        const float mxs = mx * a.scale;
-        float total = 0.f;
-        for (int j = 0; j < a.topk; ++j) total += expf(cv[j * TQ + r] * a.scale - mxs);
-        const float lse = mxs + logf(total);
-        a.lse[gr] = lse;
-        int32_t* idx_row = a.top_idx + gr * a.topk;
-        for (int j = 0; j < a.topk; ++j) {
-          idx_row[j] = ci[j * TQ + r];
-          if (a.top_scores) a.top_scores[gr * a.topk + j] = cv[j * TQ + r] * a.scale;
+    // Shrink to the candidates that go to exact re-scoring.
+    if (ok && !dead) {
+      while (cnt > a.topk + 16) {
+        const Compacted r = compact_bucket(list, R, cnt, tau, a.topk, 1);
+        cnt = r.cnt;
+        tau = r.tau;
+        if (!r.shrank) break;
+      }
+      dead = cnt > FINAL_CAP;
+    }
+    float q[D];
+    if (ok) {
+      const uint8_t* qrow = qs + wg * TILE_BYTES + rl * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 u = *reinterpret_cast<const uint4*>(qrow + ((c ^ (rl & 7)) << 4));
+        unpack8<T>(u, &q[c * 8]);
+      }
+    }
+    // Every MMA has completed (each selection warp saw its last tile) and no
+    // copy is in flight: the Q/K buffers are free after this barrier.
+    __syncwarp();
+    named_bar_sync(1, NSEL);
+    const bool live = __all_sync(0xffffffffu, ok && !*abort_flag);
+    if (live) {
+      uint16_t* stage = reinterpret_cast<uint16_t*>(sm + OFF_STAGE);
+      float* lf = reinterpret_cast<float*>(list);
+      const T* kbase = static_cast<const T*>(a.k) + slice * a.m * D;
+      const int64_t gr = row0 + (int64_t)wg * TQ + rl;
+      if (!dead) {
+        int s = 0;
+        for (; s + 1 < cnt; s += 2) {
+          const uint32_t e0 = list[s * RS + R], e1 = list[(s + 1) * RS + R];
+          uint4 u0[8], u1[8];
+          load_row(kbase + (int64_t)(e0 & 0xffffu) * D, u0);
+          load_row(kbase + (int64_t)(e1 & 0xffffu) * D, u1);
+          stage[s * RS + R] = (uint16_t)(e0 & 0xffffu);
+          stage[(s + 1) * RS + R] = (uint16_t)(e1 & 0xffffu);
+          lf[s * RS + R] = dot64_regs(q, u0, kBf16);
+          lf[(s + 1) * RS + R] = dot64_regs(q, u1, kBf16);
         }
-        float acc[D];
-#pragma unroll
-        for (int f = 0; f < D; ++f) acc[f] = 0.f;
-        const T* vbase = static_cast<const T*>(a.v) + slice * a.m * D;
-#pragma unroll 2
-        for (int j = 0; j < a.topk; ++j) {
-          const float p = expf(cv[j * TQ + r] * a.scale - lse);
-          const uint4* vrow = reinterpret_cast<const uint4*>(vbase + (int64_t)ci[j * TQ + r] * D);
-#pragma unroll
-          for (int q4 = 0; q4 < D / 8; ++q4) {
-            const uint4 u = __ldg(vrow + q4);
-            const T* e = reinterpret_cast<const T*>(&u);
-#pragma unroll
-            for (int h = 0; h < 8; ++h) acc[q4 * 8 + h] = fmaf(p, to_acc(e[h]), acc[q4 * 8 + h]);
+        if (s < cnt) {
+          const uint32_t e0 = list[s * RS + R];
+          uint4 u0[8];
+          load_row(kbase + (int64_t)(e0 & 0xffffu) * D, u0);
+          stage[s * RS + R] = (uint16_t)(e0 & 0xffffu);
+          lf[s * RS + R] = dot64_regs(q, u0, kBf16);
+        }
+        if (cnt > a.topk + 4) cnt = compact_exact(lf, stage, R, cnt, a.topk);
+        cnt = trim_exact(lf, stage, R, cnt, a.topk);
+        if (rl < rows) {
+          float mx = lf[R];
+          for (int j = 1; j < a.topk; ++j) mx = fmaxf(mx, lf[j * RS + R]);
+          const float mxs = mx * a.scale;
+          float total = 0.f;
+          for (int j = 0; j < a.topk; ++j) total += expf(lf[j * RS + R] * a.scale - mxs);
+          const float lse = mxs + logf(total);
+          a.lse[gr] = lse;
+          int32_t* idx_row = a.top_idx + gr * a.topk;
+          for (int j = 0; j < a.topk; ++j) {
+            idx_row[j] = stage[j * RS + R];
+            if (a.top_scores) a.top_scores[gr * a.topk + j] = lf[j * RS + R] * a.scale;
           }
-        }
-        uint4* orow = reinterpret_cast<uint4*>(static_cast<T*>(a.out) + gr * D);
+          float acc[D];
 #pragma unroll
-        for (int q4 = 0; q4 < D / 8; ++q4) {
-          uint4 u;
-          T* e = reinterpret_cast<T*>(&u);
+          for (int f = 0; f < D; ++f) acc[f] = 0.f;
+          const T* vbase = static_cast<const T*>(a.v) + slice * a.m * D;
+#pragma unroll 2
+          for (int j = 0; j < a.topk; ++j) {
+            const float p = expf(lf[j * RS + R] * a.scale - lse);
+            const uint4* vrow = reinterpret_cast<const uint4*>(vbase + (int64_t)stage[j * RS + R] * D);
 #pragma unroll
-          for (int h = 0; h < 8; ++h) e[h] = from_acc<T>(acc[q4 * 8 + h]);
-          orow[q4] = u;
+            for (int q4 = 0; q4 < D / 8; ++q4) {
+              float f[8];
+              unpack8<T>(__ldg(vrow + q4), f);
+#pragma unroll
+              for (int h = 0; h < 8; ++h) acc[q4 * 8 + h] = fmaf(p, f[h], acc[q4 * 8 + h]);
+            }
+          }
+          store_out_row<T>(acc, static_cast<T*>(a.out) + gr * D);
         }
+      }
+      uint8_t* fix = sm + OFF_FIX + (warp - 4) * FIX_BYTES;
+      unsigned pending = __ballot_sync(0xffffffffu, dead && rl < rows);
+      while (pending) {
+        const int l = __ffs(pending) - 1;
+        pending &= pending - 1;
+        reselect_row<T>(a, slice, row0 + (int64_t)wg * TQ + quarter * kWarp + l, reinterpret_cast<float*>(fix),
+                        reinterpret_cast<int*>(fix + FIX_CAP * 4), reinterpret_cast<float*>(fix + FIX_CAP * 8),
+                        lane);
       }
     }
   }
@@ -472,6 +762,8 @@ int launch(const FwdLaunch& L) {
   if (!make_rows_map(&tq, L.q, L.slices * L.n, bf16)) return SDK_ERR_CUDA;
   if (!make_rows_map(&tk, L.k, L.slices * L.m, bf16)) return SDK_ERR_CUDA;
   TcArgs a;
+  a.q = L.q;
+  a.k = L.k;
   a.v = L.v;
   a.out = L.out;
   a.top_idx = L.top_idx;
@@ -479,7 +771,7 @@ int launch(const FwdLaunch& L) {
   a.top_scores = static_cast<float*>(L.top_scores);
   a.n = L.n;
   a.m = L.m;
-  a.tiles_per_slice = (int)((L.n + TQ - 1) / TQ);
+  a.tiles_per_slice = (int)((L.n + RS - 1) / RS);
   a.topk = L.topk;
   a.scale = (float)L.scale;
   a.status = L.status;
@@ -501,7 +793,7 @@ bool fwd_tensorcore_supports(const FwdLaunch& L) {
   if (L.d != D || L.dv != D || L.score_grid != 0) return false;
   if (L.row_offsets || L.row_index) return false;
   if (L.m > 65536 || L.topk > 64 || L.n < 1) return false;
-  if (L.slices * L.n > 0x7fffffff || L.slices * L.m > 0x7fffffff) return false;
+  if (L.slices * L.n > 0x7fffff00 || L.slices * L.m > 0x7fffffff) return false;
   if (!aligned16(L.q) || !aligned16(L.k) || !aligned16(L.v) || !aligned16(L.out)) return false;
   return encode_fn() != nullptr;
 }

@@ -191,6 +191,17 @@ __device__ __forceinline__ void st_shared_u16_if(uint32_t addr, uint32_t v, uint
       : "memory");
 }
 
+__device__ __forceinline__ void st_shared_u32_if(uint32_t addr, uint32_t v, uint32_t p) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.shared.u32 [%0], %1;\n\t}" ::"r"(addr),
+               "r"(v), "r"(p)
+               : "memory");
+}
+
+// Barrier `id` (1..15) over `count` threads (a multiple of 32) of the CTA.
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // Three-input maximum that propagates NaN (a NaN score ranks above all).
 __device__ __forceinline__ float max3_nan(float a, float b, float c) {
   float r;
