@@ -160,6 +160,35 @@ __device__ __forceinline__ V pick16(const V (&x)[16], int want) {
   return v;
 }
 
+// Keep the entries whose ordered score reaches `pivot`, in place and in
+// order.  Entries are read eight at a time ahead of the predicated stores:
+// a store goes to a slot at or below the slot being read, so the batch
+// already holds anything a store could overwrite, and the loads no longer
+// wait on the stores one by one.
+__device__ __forceinline__ int keep_pass(uint32_t* list, int R, int cnt, uint32_t pivot) {
+  uint32_t w = 0;
+  const uint32_t base = smem_addr(list) + 4u * R;
+  int s = 0;
+  for (; s + 8 <= cnt; s += 8) {
+    uint32_t e[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) e[i] = list[(s + i) * RS + R];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t keep = (uint32_t)(ord_entry(e[i]) >= pivot);
+      st_shared_u32_if(base + w * (4u * RS), e[i], keep);
+      w += keep;
+    }
+  }
+  for (; s < cnt; ++s) {
+    const uint32_t e = list[s * RS + R];
+    const uint32_t keep = (uint32_t)(ord_entry(e) >= pivot);
+    st_shared_u32_if(base + w * (4u * RS), e, keep);
+    w += keep;
+  }
+  return (int)w;
+}
+
 // Shrink row R's list to the keys whose bucket reaches the highest of 16
 // sampled buckets that at least `topk` listed keys reach (four candidate
 // pivots per counting pass, starting near the sample rank expected to keep
@@ -203,16 +232,48 @@ __device__ __noinline__ Compacted compact_bucket(const uint32_t* list_c, int R, 
     t = t + 4 > 12 ? 12 : t + 4;
   }
   if (!found) return Compacted{cnt, tau, false};
-  uint32_t w = 0;
-  const uint32_t base = smem_addr(list) + 4u * R;
-  for (int s = 0; s < cnt; ++s) {
-    const uint32_t e = list[s * RS + R];
-    const uint32_t keep = (uint32_t)(ord_entry(e) >= pivot);
-    st_shared_u32_if(base + w * (4u * RS), e, keep);
-    w += keep;
-  }
+  const int w = keep_pass(list, R, cnt, pivot);
   // both thresholds are exact; keep the higher
-  return Compacted{(int)w, fmaxf(tau, tau_of_bucket(pivot)), (int)w < cnt};
+  return Compacted{w, fmaxf(tau, tau_of_bucket(pivot)), w < cnt};
+}
+
+// Exact bucket cut, for lists the sampled pivots cannot shrink: the highest
+// bucket P that at least `topk` listed keys reach, found by narrowing
+// [lowest bucket, highest bucket + 1) with four pivots per counting pass
+// (the range shrinks five-fold per pass), then keep the keys of bucket >= P.
+// What remains is k keys plus the other keys of bucket P; needs cnt >= topk.
+__device__ __noinline__ Compacted compact_bucket_exact(const uint32_t* list_c, int R, int cnt, float tau, int topk) {
+  uint32_t* list = const_cast<uint32_t*>(list_c);
+  uint32_t lo = 0xffffu, hi = 0u;
+  for (int s = 0; s < cnt; ++s) {
+    const uint32_t b = ord_entry(list[s * RS + R]) >> 16;
+    lo = min(lo, b);
+    hi = max(hi, b);
+  }
+  hi += 1u;  // count(>= lo) = cnt >= topk, count(>= hi) = 0 < topk
+  while (hi - lo > 1u) {
+    const uint32_t span = hi - lo;
+    uint32_t p[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) p[q] = (lo + (span * (uint32_t)(q + 1)) / 5u) << 16;
+    int c[4] = {0, 0, 0, 0};
+#pragma unroll 4
+    for (int s = 0; s < cnt; ++s) {
+      const uint32_t o = ord_entry(list[s * RS + R]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) c[q] += (int)(o >= p[q]);
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (c[q] >= topk)
+        lo = max(lo, p[q] >> 16);
+      else
+        hi = min(hi, p[q] >> 16);
+    }
+  }
+  const uint32_t pivot = lo << 16;
+  const int w = keep_pass(list, R, cnt, pivot);
+  return Compacted{w, fmaxf(tau, tau_of_bucket(pivot)), w < cnt};
 }
 
 // Append every key of a 32-key chunk whose score passes !(x <= tau) to the
@@ -312,7 +373,24 @@ __device__ __noinline__ int compact_exact(float* cv, uint16_t* ci, int R, int cn
   if (!found) return cnt;
   uint32_t w = 0;
   const uint32_t cvb = smem_addr(cv) + 4u * R, cib = smem_addr(ci) + 2u * R;
-  for (int s = 0; s < cnt; ++s) {
+  int s = 0;
+  for (; s + 8 <= cnt; s += 8) {  // loads ahead of stores, as in keep_pass
+    float x[8];
+    uint32_t i[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      x[j] = cv[(s + j) * RS + R];
+      i[j] = ci[(s + j) * RS + R];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t keep = (uint32_t)!(x[j] < pivot);
+      st_shared_f32_if(cvb + w * (4u * RS), x[j], keep);
+      st_shared_u16_if(cib + w * (2u * RS), i[j], keep);
+      w += keep;
+    }
+  }
+  for (; s < cnt; ++s) {
     const float x = cv[s * RS + R];
     const uint32_t i = ci[s * RS + R];
     const uint32_t keep = (uint32_t)!(x < pivot);
@@ -373,9 +451,19 @@ __device__ __forceinline__ void store_out_row(const float (&acc)[D], T* orow_t) 
 
 // Exact re-selection of one row by a whole warp (rows whose bucketed list
 // could not be shrunk).  fv/fi hold FIX_CAP entries; ftau is one float.
+struct RowOut {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  int32_t* top_idx;
+  float* lse;
+  float* top_scores;
+};
+
 template <typename T>
-__device__ __noinline__ void reselect_row(const TcArgs& a, int64_t slice, int64_t gr, float* fv, int* fi, float* ftau,
-                             int lane) {
+__device__ __noinline__ void reselect_row(RowOut a, int64_t m, int topk, float scale, int64_t slice, int64_t gr,
+                                          float* fv, int* fi, float* ftau, int lane) {
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   float q[D];
   {
@@ -384,14 +472,14 @@ __device__ __noinline__ void reselect_row(const TcArgs& a, int64_t slice, int64_
 #pragma unroll
     for (int c = 0; c < 8; ++c) unpack8<T>(u[c], &q[c * 8]);
   }
-  const T* kbase = static_cast<const T*>(a.k) + slice * a.m * D;
+  const T* kbase = static_cast<const T*>(a.k) + slice * m * D;
   if (lane == 0) *ftau = __int_as_float(0x7fc00000);
   __syncwarp();
   float tau = __int_as_float(0x7fc00000);
   int c0 = 0;
-  for (int64_t k0 = 0; k0 < a.m; k0 += kWarp) {
+  for (int64_t k0 = 0; k0 < m; k0 += kWarp) {
     const int64_t key = k0 + lane;
-    const bool valid = key < a.m;
+    const bool valid = key < m;
     float s = 0.f;
     if (valid) {
       uint4 u[8];
@@ -408,28 +496,28 @@ __device__ __noinline__ void reselect_row(const TcArgs& a, int64_t slice, int64_
     c0 += __popc(bal);
     if (c0 > FIX_CAP - kWarp) {
       __syncwarp();
-      c0 = compact_row(fv, fi, c0, a.topk, ftau, lane);
+      c0 = compact_row(fv, fi, c0, topk, ftau, lane);
       tau = *ftau;
     }
   }
   __syncwarp();
-  c0 = compact_row(fv, fi, c0, a.topk, ftau, lane);  // sorted, c0 == topk (topk <= m)
-  const float mxs = fv[0] * a.scale;
+  c0 = compact_row(fv, fi, c0, topk, ftau, lane);  // sorted, c0 == topk (topk <= m)
+  const float mxs = fv[0] * scale;
   float part = 0.f;
-  for (int j = lane; j < c0; j += kWarp) part += expf(fv[j] * a.scale - mxs);
+  for (int j = lane; j < c0; j += kWarp) part += expf(fv[j] * scale - mxs);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
   const float lse = mxs + logf(part);
   for (int j = lane; j < c0; j += kWarp) {
-    a.top_idx[gr * a.topk + j] = fi[j];
-    if (a.top_scores) a.top_scores[gr * a.topk + j] = fv[j] * a.scale;
+    a.top_idx[gr * topk + j] = fi[j];
+    if (a.top_scores) a.top_scores[gr * topk + j] = fv[j] * scale;
   }
   if (lane == 0) a.lse[gr] = lse;
   // lane l accumulates features 2l, 2l+1
-  const T* vbase = static_cast<const T*>(a.v) + slice * a.m * D;
+  const T* vbase = static_cast<const T*>(a.v) + slice * m * D;
   float o0 = 0.f, o1 = 0.f;
   for (int j = 0; j < c0; ++j) {
-    const float p = expf(fv[j] * a.scale - lse);
+    const float p = expf(fv[j] * scale - lse);
     const T* vr = vbase + (int64_t)fi[j] * D + 2 * lane;
     o0 = fmaf(p, to_acc(vr[0]), o0);
     o1 = fmaf(p, to_acc(vr[1]), o1);
@@ -609,7 +697,7 @@ __global__ void __launch_bounds__(NT, 1)
         if (__any_sync(0xffffffffu, !dead && cnt > CAP - 32)) {
           if (!dead && cnt > a.topk + 32) {
             Compacted r = compact_bucket(list, R, cnt, tau, a.topk, 2);
-            if (r.cnt > CAP - 32) r = compact_bucket(list, R, r.cnt, r.tau, a.topk, 1);
+            if (r.cnt > CAP - 32) r = compact_bucket_exact(list, R, r.cnt, r.tau, a.topk);
             cnt = r.cnt;
             tau = r.tau;
             dead = cnt > CAP - 32;
@@ -624,6 +712,11 @@ __global__ void __launch_bounds__(NT, 1)
         cnt = r.cnt;
         tau = r.tau;
         if (!r.shrank) break;
+      }
+      if (cnt > a.topk + 16) {
+        const Compacted r = compact_bucket_exact(list, R, cnt, tau, a.topk);
+        cnt = r.cnt;
+        tau = r.tau;
       }
       dead = cnt > FINAL_CAP;
     }
@@ -704,7 +797,8 @@ __global__ void __launch_bounds__(NT, 1)
       while (pending) {
         const int l = __ffs(pending) - 1;
         pending &= pending - 1;
-        reselect_row<T>(a, slice, row0 + (int64_t)wg * TQ + quarter * kWarp + l, reinterpret_cast<float*>(fix),
+        reselect_row<T>(RowOut{a.q, a.k, a.v, a.out, a.top_idx, a.lse, a.top_scores}, a.m, a.topk, a.scale, slice,
+                        row0 + (int64_t)wg * TQ + quarter * kWarp + l, reinterpret_cast<float*>(fix),
                         reinterpret_cast<int*>(fix + FIX_CAP * 4), reinterpret_cast<float*>(fix + FIX_CAP * 8),
                         lane);
       }
