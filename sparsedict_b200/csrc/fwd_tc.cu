@@ -311,8 +311,8 @@ __device__ __forceinline__ void unpack8(const uint4& u, float* f) {
   for (int h = 0; h < 8; ++h) f[h] = to_acc(e[h]);
 }
 
-// The one fp32 score of this kernel's exact stages: four FMA chains (feature
-// f feeds chain f mod 4) summed pairwise.
+// Exact fp32 score of the re-scoring stage: four FMA chains (feature f feeds
+// chain f mod 4) summed pairwise.
 __device__ __forceinline__ float dot64_regs(const float (&q)[D], const uint4 (&u)[8], bool bf16) {
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -333,6 +333,84 @@ __device__ __forceinline__ void load_row(const T* row, uint4 (&u)[8]) {
   const uint4* p = reinterpret_cast<const uint4*>(row);
 #pragma unroll
   for (int c = 0; c < 8; ++c) u[c] = __ldg(p + c);
+}
+
+// Warp re-selection works on one query row with the whole warp: lane
+// 8*grp + g handles features 8g..8g+7 (16 bytes) of key grp of a group of
+// four, so one 16-byte load instruction reads four whole 128-byte key or
+// value rows.
+template <typename T>
+__device__ __forceinline__ void load_chunk8(const T* p, float (&f)[8]) {
+  unpack8<T>(__ldg(reinterpret_cast<const uint4*>(p)), f);
+}
+
+// Exact fp32 score of the warp re-selection: each lane runs one FMA chain
+// over its 8 features in order, then the 8 lanes of a group add their
+// partial sums by xor-shuffles over 1, 2 and 4, so all 8 lanes hold the same
+// sum.  (A row's scores all come from one of the two exact stages, so each
+// row ranks its keys by one rounding of the dot product.)
+template <typename T>
+__device__ __forceinline__ float group_dot(const float (&qg)[8], const uint4& kc) {
+  float f[8];
+  unpack8<T>(kc, f);
+  float acc = 0.f;
+#pragma unroll
+  for (int h = 0; h < 8; ++h) acc = fmaf(qg[h], f[h], acc);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+  return acc;
+}
+
+// Softmax-weighted sum of one query row's selected value rows, by the whole
+// warp.  score_of(j) / index_of(j) give the raw score and key of selection j.
+// Lane 8*grp + g accumulates features 8g..8g+7 of selections grp, grp+4, ...
+// in that order; the four groups are added by xor-shuffles over 8 and 16 and
+// lanes 0..7 store the 128-byte output row.  Also writes the row's indices
+// (and scaled scores when asked) with consecutive lanes on consecutive
+// entries.
+template <typename T, typename ScoreOf, typename IndexOf>
+__device__ __forceinline__ void write_row(const T* vbase, ScoreOf score_of, IndexOf index_of, int topk, float scale,
+                                          float lse, T* orow, int32_t* idx_row, float* score_row, int lane) {
+  for (int j = lane; j < topk; j += kWarp) {
+    idx_row[j] = (int32_t)index_of(j);
+    if (score_row) score_row[j] = score_of(j) * scale;
+  }
+  const int g = lane & 7, grp = lane >> 3;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int b0 = 0; b0 < topk; b0 += 8) {
+    const int j0 = b0 + grp, j1 = b0 + 4 + grp;
+    const bool v0 = j0 < topk, v1 = j1 < topk;
+    float p0 = 0.f, p1 = 0.f;
+    uint4 c0 = make_uint4(0u, 0u, 0u, 0u), c1 = c0;
+    if (v0) {
+      p0 = expf(score_of(j0) * scale - lse);
+      c0 = __ldg(reinterpret_cast<const uint4*>(vbase + (int64_t)index_of(j0) * D) + g);
+    }
+    if (v1) {
+      p1 = expf(score_of(j1) * scale - lse);
+      c1 = __ldg(reinterpret_cast<const uint4*>(vbase + (int64_t)index_of(j1) * D) + g);
+    }
+    float f[8];
+    unpack8<T>(c0, f);
+#pragma unroll
+    for (int h = 0; h < 8; ++h) acc[h] = fmaf(p0, f[h], acc[h]);
+    unpack8<T>(c1, f);
+#pragma unroll
+    for (int h = 0; h < 8; ++h) acc[h] = fmaf(p1, f[h], acc[h]);
+  }
+#pragma unroll
+  for (int h = 0; h < 8; ++h) {
+    acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 8);
+    acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 16);
+  }
+  if (lane < 8) {
+    uint4 u;
+    T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+    for (int h = 0; h < 8; ++h) e[h] = from_acc<T>(acc[h]);
+    reinterpret_cast<uint4*>(orow)[g] = u;
+  }
 }
 
 // Exact cut on re-scored candidates (fp32 scores in cv, key indices in ci,
@@ -450,7 +528,10 @@ __device__ __forceinline__ void store_out_row(const float (&acc)[D], T* orow_t) 
 }
 
 // Exact re-selection of one row by a whole warp (rows whose bucketed list
-// could not be shrunk).  fv/fi hold FIX_CAP entries; ftau is one float.
+// could not be shrunk).  32 keys per step: eight group dots of four keys,
+// then lane L takes the score of key k0 + L; a lane keeps each key beating
+// the row's threshold in an exact list (fv/fi, FIX_CAP entries) that a warp
+// bitonic sort cuts back to k when it could overflow.  ftau is one float.
 struct RowOut {
   const void* q;
   const void* k;
@@ -464,28 +545,27 @@ struct RowOut {
 template <typename T>
 __device__ __noinline__ void reselect_row(RowOut a, int64_t m, int topk, float scale, int64_t slice, int64_t gr,
                                           float* fv, int* fi, float* ftau, int lane) {
-  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-  float q[D];
-  {
-    uint4 u[8];
-    load_row(static_cast<const T*>(a.q) + gr * D, u);
-#pragma unroll
-    for (int c = 0; c < 8; ++c) unpack8<T>(u[c], &q[c * 8]);
-  }
+  const int g = lane & 7, grp = lane >> 3;
+  float qg[8];
+  load_chunk8<T>(static_cast<const T*>(a.q) + gr * D + 8 * g, qg);
   const T* kbase = static_cast<const T*>(a.k) + slice * m * D;
   if (lane == 0) *ftau = __int_as_float(0x7fc00000);
   __syncwarp();
   float tau = __int_as_float(0x7fc00000);
   int c0 = 0;
   for (int64_t k0 = 0; k0 < m; k0 += kWarp) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t kk = k0 + 4 * i + grp;
+      uint4 kc = make_uint4(0u, 0u, 0u, 0u);
+      if (kk < m) kc = __ldg(reinterpret_cast<const uint4*>(kbase + kk * D) + g);
+      const float d = group_dot<T>(qg, kc);  // score of key k0 + 4i + grp
+      const float x = __shfl_sync(0xffffffffu, d, 8 * (lane & 3));
+      if ((lane >> 2) == i) s = x;
+    }
     const int64_t key = k0 + lane;
     const bool valid = key < m;
-    float s = 0.f;
-    if (valid) {
-      uint4 u[8];
-      load_row(kbase + key * D, u);
-      s = dot64_regs(q, u, kBf16);
-    }
     const bool pass = valid && !(s <= tau);
     const unsigned bal = __ballot_sync(0xffffffffu, pass);
     if (pass) {
@@ -508,23 +588,10 @@ __device__ __noinline__ void reselect_row(RowOut a, int64_t m, int topk, float s
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
   const float lse = mxs + logf(part);
-  for (int j = lane; j < c0; j += kWarp) {
-    a.top_idx[gr * topk + j] = fi[j];
-    if (a.top_scores) a.top_scores[gr * topk + j] = fv[j] * scale;
-  }
   if (lane == 0) a.lse[gr] = lse;
-  // lane l accumulates features 2l, 2l+1
-  const T* vbase = static_cast<const T*>(a.v) + slice * m * D;
-  float o0 = 0.f, o1 = 0.f;
-  for (int j = 0; j < c0; ++j) {
-    const float p = expf(fv[j] * scale - lse);
-    const T* vr = vbase + (int64_t)fi[j] * D + 2 * lane;
-    o0 = fmaf(p, to_acc(vr[0]), o0);
-    o1 = fmaf(p, to_acc(vr[1]), o1);
-  }
-  T* orow = static_cast<T*>(a.out) + gr * D + 2 * lane;
-  orow[0] = from_acc<T>(o0);
-  orow[1] = from_acc<T>(o1);
+  write_row<T>(static_cast<const T*>(a.v) + slice * m * D, [&](int j) { return fv[j]; }, [&](int j) { return fi[j]; },
+               c0, scale, lse, static_cast<T*>(a.out) + gr * D, a.top_idx + gr * topk,
+               a.top_scores ? a.top_scores + gr * topk : nullptr, lane);
   __syncwarp();
 }
 
