@@ -354,6 +354,29 @@ def test_low_precision_forward_backward_vs_oracle(dtype):
         assert np.abs(got - exp).max() <= 2e-2 * max(1.0, np.abs(exp).max())
 
 
+@pytest.mark.parametrize("n,m,k", [(300, 1000, 32), (512, 4096, 64), (100, 129, 1), (257, 2000, 7)])
+def test_bf16_tensor_core_exact_ties_lower_index_wins(n, m, k):
+    # Integer-valued bf16 queries and keys: every score is an exact integer
+    # (no rounding anywhere), most of them tied.  Rows whose bucketed
+    # candidate lists cannot be shrunk go through the exact warp
+    # re-selection; either way the selected set must be the oracle's, with
+    # the lower key index winning every tie.
+    g = torch.Generator().manual_seed(n + m + k)
+    bh, d = 3, 64
+    q, kk = (torch.randint(-2, 3, (bh, x, d), generator=g).to(torch.bfloat16) for x in (n, m))
+    v = torch.randn(bh, m, d, generator=g).to(torch.bfloat16)
+    from sparsedict_b200 import _ops
+
+    out, idx, lse, _ = _ops.topk_attn_fwd(q.to(DEV), kk.to(DEV), v.to(DEV), k, 1 / 8)
+    assert _native.device_status(clear=True) == 0
+    qf, kf, vf = (t.float().numpy() for t in (q, kk, v))
+    o, oi, ol, _ = oracle.topk_attention_forward(qf, kf, vf, k, 1 / 8)
+    got = np.sort(idx.cpu().numpy().reshape(-1, k), axis=1)
+    assert np.array_equal(got, np.sort(oi.reshape(-1, k), axis=1))
+    np.testing.assert_allclose(lse.cpu().numpy().reshape(ol.shape), ol, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(out.float().cpu().numpy(), o, rtol=2e-2, atol=2e-2)
+
+
 # --- tie stress (configuration 5 shape family, reduced size) ----------------------
 
 
