@@ -3,8 +3,10 @@
 // One CTA owns 256 query rows of one (b, h) slice (d = dv = 64, bf16 or fp16)
 // as two 128-row tiles, A and B, and streams the slice's keys in tiles of 128:
 //
-//   warp 0       TMA producer: both Q tiles once, then K tiles into a 2-stage
-//                ring of 128-byte-swizzled shared-memory buffers;
+//   warp 0       TMA producer: both Q tiles once, then each K tile into one
+//                128-byte-swizzled shared-memory buffer (the MMAs of a tile
+//                take a fraction of a microsecond, a tile's selection several,
+//                so one buffer never starves the pipeline);
 //   warp 1       allocates 512 TMEM columns and issues tcgen05.mma
 //                (M=128, N=128, K=16 x 4) of S_A = Q_A·Kᵀ and S_B = Q_B·Kᵀ
 //                for every K tile, each into one of two TMEM accumulators of
@@ -27,10 +29,10 @@
 // re-selected exactly at the end, see below.
 //
 // After the last tile the survivors of each row (at most 96) are re-scored
-// exactly: the row's Q values go to registers, the Q/K buffers are released
-// (named barrier of the 256 selection threads), the key indices move there,
-// and each candidate's fp32 score is recomputed from the gathered key row by
-// one fixed FMA order.  The exact cut to k keys uses order-preserving 64-bit
+// exactly: the row's Q values go to registers, the candidates' key indices
+// move to the row's own unused list slots, and each candidate's fp32 score
+// is recomputed from the gathered key row by one fixed FMA order, replacing
+// its bucketed entry.  The exact cut to k keys uses order-preserving 64-bit
 // keys (score, complemented index), so ties keep the lower key index.  Then
 // the row LSE, the k indices (in no particular order; the set is the
 // reference's top-k set) and the softmax-weighted sum of the gathered value
@@ -61,8 +63,8 @@ constexpr int NTILE = 2;        // query tiles per CTA
 constexpr int RS = TQ * NTILE;  // rows per CTA; row stride of the slot-major lists
 constexpr int TK = 128;         // keys per score tile (MMA N)
 constexpr int D = 64;           // feature width (one 128-byte swizzle row)
-constexpr int KSTAGES = 2;
-constexpr int CAP = 160;        // list slots per row
+constexpr int KSTAGES = 1;
+constexpr int CAP = 176;        // list slots per row
 constexpr int FINAL_CAP = 96;   // most candidates a row may carry into exact re-scoring
 constexpr int FIX_CAP = 128;    // exact list of a row re-selected by one warp
 constexpr int NT = 384;
@@ -77,12 +79,13 @@ constexpr int OFF_BAR = OFF_LIST + CAP * RS * 4;
 constexpr int NBARS = 1 + 2 * KSTAGES + 4 * NTILE;
 constexpr int OFF_MISC = OFF_BAR + NBARS * 8;
 constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
-// The Q/K region once the stream is over: key indices of the re-scored
-// candidates, then one exact re-selection buffer per selection warp.
-constexpr int OFF_STAGE = 0;
-constexpr int OFF_FIX = OFF_STAGE + FINAL_CAP * RS * 2;
+// After the stream: the key indices of a row's re-scored candidates go to
+// the row's own list column above FINAL_CAP (two 16-bit indices per word),
+// and the Q/K region holds one exact re-selection buffer per selection warp.
+constexpr int OFF_FIX = 0;
 constexpr int FIX_BYTES = FIX_CAP * 8 + 16;
 static_assert(OFF_FIX + 8 * FIX_BYTES <= OFF_LIST, "post-stream buffers exceed the Q/K region");
+static_assert(FINAL_CAP + (FINAL_CAP + 1) / 2 <= CAP, "re-scoring indices exceed the list column");
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 static_assert(OFF_BAR % 8 == 0, "mbarrier alignment");
 
@@ -160,6 +163,33 @@ __device__ __forceinline__ V pick16(const V (&x)[16], int want) {
   return v;
 }
 
+// Counts of row R's listed entries whose ordered form reaches each of four
+// pivots.  Eight entries per step and two sets of counters keep several
+// loads and adds in flight (the counters are the only dependency chains).
+__device__ __forceinline__ void count4(const uint32_t* list, int R, int cnt, const uint32_t (&p)[4], int (&c)[4]) {
+  int a[4] = {0, 0, 0, 0}, b[4] = {0, 0, 0, 0};
+  int s = 0;
+  for (; s + 8 <= cnt; s += 8) {
+    uint32_t o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = ord_entry(list[(s + i) * RS + R]);
+#pragma unroll
+    for (int i = 0; i < 8; i += 2)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        a[q] += (int)(o[i] >= p[q]);
+        b[q] += (int)(o[i + 1] >= p[q]);
+      }
+  }
+  for (; s < cnt; ++s) {
+    const uint32_t o = ord_entry(list[s * RS + R]);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) a[q] += (int)(o >= p[q]);
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) c[q] = a[q] + b[q];
+}
+
 // Keep the entries whose ordered score reaches `pivot`, in place and in
 // order.  Entries are read eight at a time ahead of the predicated stores:
 // a store goes to a slot at or below the slot being read, so the batch
@@ -216,13 +246,8 @@ __device__ __noinline__ Compacted compact_bucket(const uint32_t* list_c, int R, 
     uint32_t p[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) p[q] = pick16(smp, t + q);
-    int c[4] = {0, 0, 0, 0};
-#pragma unroll 4
-    for (int s = 0; s < cnt; ++s) {
-      const uint32_t o = ord_entry(list[s * RS + R]);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) c[q] += (int)(o >= p[q]);
-    }
+    int c[4];
+    count4(list, R, cnt, p, c);
 #pragma unroll
     for (int q = 3; q >= 0; --q)
       if (c[q] >= topk) {
@@ -256,13 +281,8 @@ __device__ __noinline__ Compacted compact_bucket_exact(const uint32_t* list_c, i
     uint32_t p[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) p[q] = (lo + (span * (uint32_t)(q + 1)) / 5u) << 16;
-    int c[4] = {0, 0, 0, 0};
-#pragma unroll 4
-    for (int s = 0; s < cnt; ++s) {
-      const uint32_t o = ord_entry(list[s * RS + R]);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) c[q] += (int)(o >= p[q]);
-    }
+    int c[4];
+    count4(list, R, cnt, p, c);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       if (c[q] >= topk)
@@ -413,11 +433,19 @@ __device__ __forceinline__ void write_row(const T* vbase, ScoreOf score_of, Inde
   }
 }
 
+// Key index of re-scored candidate s of a row: `srow` points at the row's
+// list column at slot FINAL_CAP; candidate s sits in slot FINAL_CAP + s/2,
+// half s%2 of the word.
+__device__ __forceinline__ uint32_t stage_byte(int s) { return (uint32_t)((s >> 1) * (4 * RS) + 2 * (s & 1)); }
+__device__ __forceinline__ uint16_t& stage_at(uint16_t* srow, int s) {
+  return *reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(srow) + stage_byte(s));
+}
+
 // Exact cut on re-scored candidates (fp32 scores in cv, key indices in ci,
 // both slot-major with stride RS).  Raise a pivot as compact_bucket does,
 // with exact scores: keep the keys scoring at least the highest of 16
 // sampled scores that >= topk candidates meet.
-__device__ __noinline__ int compact_exact(float* cv, uint16_t* ci, int R, int cnt, int topk) {
+__device__ __noinline__ int compact_exact(float* cv, uint16_t* srow, int R, int cnt, int topk) {
   float smp[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
@@ -450,7 +478,7 @@ __device__ __noinline__ int compact_exact(float* cv, uint16_t* ci, int R, int cn
   }
   if (!found) return cnt;
   uint32_t w = 0;
-  const uint32_t cvb = smem_addr(cv) + 4u * R, cib = smem_addr(ci) + 2u * R;
+  const uint32_t cvb = smem_addr(cv) + 4u * R, cib = smem_addr(srow);
   int s = 0;
   for (; s + 8 <= cnt; s += 8) {  // loads ahead of stores, as in keep_pass
     float x[8];
@@ -458,22 +486,22 @@ __device__ __noinline__ int compact_exact(float* cv, uint16_t* ci, int R, int cn
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       x[j] = cv[(s + j) * RS + R];
-      i[j] = ci[(s + j) * RS + R];
+      i[j] = stage_at(srow, s + j);
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const uint32_t keep = (uint32_t)!(x[j] < pivot);
       st_shared_f32_if(cvb + w * (4u * RS), x[j], keep);
-      st_shared_u16_if(cib + w * (2u * RS), i[j], keep);
+      st_shared_u16_if(cib + stage_byte((int)w), i[j], keep);
       w += keep;
     }
   }
   for (; s < cnt; ++s) {
     const float x = cv[s * RS + R];
-    const uint32_t i = ci[s * RS + R];
+    const uint32_t i = stage_at(srow, s);
     const uint32_t keep = (uint32_t)!(x < pivot);
     st_shared_f32_if(cvb + w * (4u * RS), x, keep);
-    st_shared_u16_if(cib + w * (2u * RS), i, keep);
+    st_shared_u16_if(cib + stage_byte((int)w), i, keep);
     w += keep;
   }
   return (int)w;
@@ -495,20 +523,20 @@ __device__ __forceinline__ uint64_t rank_key(float x, uint32_t idx) {
 }
 
 // Remove lowest-ranked keys until exactly `topk` remain.
-__device__ __noinline__ int trim_exact(float* cv, uint16_t* ci, int R, int cnt, int topk) {
+__device__ __noinline__ int trim_exact(float* cv, uint16_t* srow, int R, int cnt, int topk) {
   while (cnt > topk) {
     uint64_t worst = ~0ull;
     int pos = 0;
 #pragma unroll 4
     for (int s = 0; s < cnt; ++s) {
-      const uint64_t key = rank_key(cv[s * RS + R], ci[s * RS + R]);
+      const uint64_t key = rank_key(cv[s * RS + R], stage_at(srow, s));
       const bool lower = key < worst;
       worst = lower ? key : worst;
       pos = lower ? s : pos;
     }
     const int last = cnt - 1;
     cv[pos * RS + R] = cv[last * RS + R];
-    ci[pos * RS + R] = ci[last * RS + R];
+    stage_at(srow, pos) = stage_at(srow, last);
     cnt = last;
   }
   return cnt;
@@ -802,7 +830,7 @@ __global__ void __launch_bounds__(NT, 1)
     named_bar_sync(1, NSEL);
     const bool live = __all_sync(0xffffffffu, ok && !*abort_flag);
     if (live) {
-      uint16_t* stage = reinterpret_cast<uint16_t*>(sm + OFF_STAGE);
+      uint16_t* srow = reinterpret_cast<uint16_t*>(list + FINAL_CAP * RS + R);
       float* lf = reinterpret_cast<float*>(list);
       const T* kbase = static_cast<const T*>(a.k) + slice * a.m * D;
       const int64_t gr = row0 + (int64_t)wg * TQ + rl;
@@ -813,8 +841,8 @@ __global__ void __launch_bounds__(NT, 1)
           uint4 u0[8], u1[8];
           load_row(kbase + (int64_t)(e0 & 0xffffu) * D, u0);
           load_row(kbase + (int64_t)(e1 & 0xffffu) * D, u1);
-          stage[s * RS + R] = (uint16_t)(e0 & 0xffffu);
-          stage[(s + 1) * RS + R] = (uint16_t)(e1 & 0xffffu);
+          stage_at(srow, s) = (uint16_t)(e0 & 0xffffu);
+          stage_at(srow, s + 1) = (uint16_t)(e1 & 0xffffu);
           lf[s * RS + R] = dot64_regs(q, u0, kBf16);
           lf[(s + 1) * RS + R] = dot64_regs(q, u1, kBf16);
         }
@@ -822,11 +850,11 @@ __global__ void __launch_bounds__(NT, 1)
           const uint32_t e0 = list[s * RS + R];
           uint4 u0[8];
           load_row(kbase + (int64_t)(e0 & 0xffffu) * D, u0);
-          stage[s * RS + R] = (uint16_t)(e0 & 0xffffu);
+          stage_at(srow, s) = (uint16_t)(e0 & 0xffffu);
           lf[s * RS + R] = dot64_regs(q, u0, kBf16);
         }
-        if (cnt > a.topk + 4) cnt = compact_exact(lf, stage, R, cnt, a.topk);
-        cnt = trim_exact(lf, stage, R, cnt, a.topk);
+        if (cnt > a.topk + 4) cnt = compact_exact(lf, srow, R, cnt, a.topk);
+        cnt = trim_exact(lf, srow, R, cnt, a.topk);
         if (rl < rows) {
           float mx = lf[R];
           for (int j = 1; j < a.topk; ++j) mx = fmaxf(mx, lf[j * RS + R]);
@@ -837,7 +865,7 @@ __global__ void __launch_bounds__(NT, 1)
           a.lse[gr] = lse;
           int32_t* idx_row = a.top_idx + gr * a.topk;
           for (int j = 0; j < a.topk; ++j) {
-            idx_row[j] = stage[j * RS + R];
+            idx_row[j] = stage_at(srow, j);
             if (a.top_scores) a.top_scores[gr * a.topk + j] = lf[j * RS + R] * a.scale;
           }
           float acc[D];
@@ -847,7 +875,7 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll 2
           for (int j = 0; j < a.topk; ++j) {
             const float p = expf(lf[j * RS + R] * a.scale - lse);
-            const uint4* vrow = reinterpret_cast<const uint4*>(vbase + (int64_t)stage[j * RS + R] * D);
+            const uint4* vrow = reinterpret_cast<const uint4*>(vbase + (int64_t)stage_at(srow, j) * D);
 #pragma unroll
             for (int q4 = 0; q4 < D / 8; ++q4) {
               float f[8];
