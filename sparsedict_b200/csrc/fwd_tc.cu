@@ -756,19 +756,12 @@ __global__ void __launch_bounds__(NT, 1)
       tc_fence_after();
       const int64_t key_tile = (int64_t)t * TK;
       const int tile_valid = (int)((a.m - key_tile) < TK ? (a.m - key_tile) : TK);
-      // One 32-column chunk at a time, in a loop that is not unrolled: the
-      // loop body is the whole hot path and stays resident in the
-      // instruction cache next to the other group's warps.  The TMEM buffer
-      // is released once its last chunk is in registers.
-#pragma unroll 1
-      for (int c = 0; c < TK / 32; ++c) {
-        uint32_t v[32];
-        tmem_load_32cols(tm + b * TK + c * 32, v);
-        tmem_wait_load();
-        if (c == TK / 32 - 1) {
-          tc_fence_before();
-          mbar_arrive(&my_empty[b]);
-        }
+      // One 32-column chunk at a time; the TMEM load of the next chunk is in
+      // flight while the current one is filtered.  The loop body holds two
+      // chunk steps (two register buffers) so that the hot path stays small
+      // enough for the instruction cache.  The TMEM buffer is released once
+      // its last chunk is in registers.
+      auto chunk_step = [&](uint32_t(&v)[32], int c) {
         const int valid = tile_valid - c * 32;
         float mx;
         if (valid >= 32) {
@@ -779,7 +772,7 @@ __global__ void __launch_bounds__(NT, 1)
           for (int i = 0; i < 32; ++i)
             if (i < valid) mx = max_nan(mx, __uint_as_float(v[i]));
         }
-        if (!__any_sync(0xffffffffu, !(mx <= tau))) continue;
+        if (!__any_sync(0xffffffffu, !(mx <= tau))) return;
         if (__any_sync(0xffffffffu, mx != mx)) {
           // one NaN pattern, ranked above every number
 #pragma unroll
@@ -790,6 +783,9 @@ __global__ void __launch_bounds__(NT, 1)
         // k keys compacts in the same pass: under SIMT the warp pays for the
         // longest list either way.
         if (__any_sync(0xffffffffu, !dead && cnt > CAP - 32)) {
+          // The next chunk's TMEM load may still be writing its registers:
+          // complete it before calling out of line.
+          tmem_wait_load();
           if (!dead && cnt > a.topk + 32) {
             Compacted r = compact_bucket(list, R, cnt, tau, a.topk, 2);
             if (r.cnt > CAP - 32) r = compact_bucket_exact(list, R, r.cnt, r.tau, a.topk);
@@ -798,6 +794,25 @@ __global__ void __launch_bounds__(NT, 1)
             dead = cnt > CAP - 32;
           }
         }
+      };
+      uint32_t va[32], vb[32];
+      tmem_load_32cols(tm + b * TK, va);
+      tmem_wait_load(va);
+#pragma unroll 1
+      for (int cp = 0; cp < TK / 64; ++cp) {
+        const int c0 = 2 * cp;
+        tmem_load_32cols(tm + b * TK + (c0 + 1) * 32, vb);
+        chunk_step(va, c0);
+        tmem_wait_load(vb);
+        const bool last = cp == TK / 64 - 1;
+        if (!last) {
+          tmem_load_32cols(tm + b * TK + (c0 + 2) * 32, va);
+        } else {
+          tc_fence_before();
+          mbar_arrive(&my_empty[b]);
+        }
+        chunk_step(vb, c0 + 1);
+        if (!last) tmem_wait_load(va);
       }
     }
     // Shrink to the candidates that go to exact re-scoring.
