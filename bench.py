@@ -306,7 +306,9 @@ def run_native_arm(args):
     peak_tc = peaks["bf16_tflops_sustained"]
     # ncu-measured DRAM bytes of one headline forward launch (profiles/traffic.json)
     traffic = load_traffic().get("fused_fwd_cfg4") if (c["B"], c["H"], world) == (CFG["B"], CFG["H"], 1) else None
-    t_roof = max(flops_tc / world / (peak_tc * 1e12), bytes_fb / world / (peaks["hbm_gbs"] * 1e9))
+    t_tensor = flops_tc / world / (peak_tc * 1e12)
+    t_hbm = bytes_fb / world / (peaks["hbm_gbs"] * 1e9)
+    t_roof = max(t_tensor, t_hbm)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
@@ -318,7 +320,11 @@ def run_native_arm(args):
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tc, "unit": "TFLOP/s",
                      "frac": achieved / peak_tc, "traffic": traffic, "kernel": "fused forward",
                      "fwd_ms": fwd_ms, "peak_source": f"{peaks['source']} bf16_tflops_sustained",
-                     "step_frac_combined": t_roof / (ms_per_step / 1000.0)},
+                     "step_frac_combined": t_roof / (ms_per_step / 1000.0),
+                     # each whole-step term on its own: affinity flops at the tensor peak,
+                     # compulsory fwd+bwd bytes at the HBM peak
+                     "step_frac_tensor": t_tensor / (ms_per_step / 1000.0),
+                     "step_frac_hbm": t_hbm / (ms_per_step / 1000.0)},
         # this library's kernels per step: forward, one backward per bucket, two finalizes
         "gpu_launches": (1 + len(runner._bucket_ranges()) + 2) * args.steps,
     }
