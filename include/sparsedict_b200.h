@@ -102,6 +102,41 @@ int sdk_topk_attn_bwd(const void* q, const void* k, const void* v, const void* d
                       double scale, int32_t score_grid, int32_t accumulate, int32_t dtype,
                       void* stream);
 
+/*
+ * Forward with an additive score bias per (query row, key segment): the gate
+ * fold of DualDomainMoEDictionary._mixture
+ * (models/modules/dual_domain_moe.py:158-173), which adds log(max(g, tiny))
+ * of token n's gate for expert e to the scores of expert e's atoms (-inf
+ * where g == 0) before the top-k over the flat E*M atom axis.  Same as
+ * sdk_topk_attn_fwd with
+ *   score(r, j) = scale * q_r·k_j + seg_bias[r * segs + j / seg_len]
+ * for logical row r; seg_bias is float (double for SDK_DTYPE_F64) and
+ * seg_len * segs >= m.  Selection, lse and top_scores use the biased scores.
+ * Runs on the CUDA-core kernel.
+ */
+int sdk_topk_attn_fwd_biased(const void* q, const void* k, const void* v, void* out, int32_t* top_idx,
+                             void* lse, void* top_scores, const int32_t* row_offsets,
+                             const int32_t* row_index, int64_t slices, int64_t n, int64_t m, int32_t d,
+                             int32_t dv, int32_t topk, double scale, int32_t score_grid,
+                             const void* seg_bias, int64_t seg_len, int32_t segs, int32_t dtype,
+                             void* stream);
+
+/*
+ * Backward of sdk_topk_attn_fwd_biased (the score bias enters the recomputed
+ * S).  dseg_bias (nullable, rows * segs, accumulator dtype) receives, per row
+ * and segment, the sum of dS over the row's selected keys of that segment —
+ * the gradient of the bias, from which the caller forms the gate gradient
+ * dS_sum / g (models/modules/dual_domain_moe.py:164-166 under autograd).  It is
+ * zeroed with the accumulators unless `accumulate` is nonzero.
+ */
+int sdk_topk_attn_bwd_biased(const void* q, const void* k, const void* v, const void* dout,
+                             const int32_t* top_idx, const void* lse, void* dq, void* dk_acc,
+                             void* dv_acc, const int32_t* row_offsets, const int32_t* row_index,
+                             int64_t slices, int64_t n, int64_t m, int32_t d, int32_t dv,
+                             int32_t topk, double scale, int32_t score_grid, int32_t accumulate,
+                             const void* seg_bias, void* dseg_bias, int64_t seg_len, int32_t segs,
+                             int32_t dtype, void* stream);
+
 /* Capacity, in fp32 elements (16 MiB), of the library-owned scratch array
  * that sdk_topk_attn_bwd_noalloc accumulates dK and dV in. */
 #define SDK_NOALLOC_SCRATCH_FLOATS (4u * 1024u * 1024u)

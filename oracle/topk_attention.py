@@ -25,6 +25,10 @@ It restates, in numpy, the algorithm of the reference's PyTorch path:
 * a dense restatement of the same forward/backward, the way autograd runs
   the reference CPU path (dense ``(N, M)`` scores and score gradients),
   used as the timed CPU baseline.
+* the gate fold of ``DualDomainMoEDictionary._mixture``
+  (``models/modules/dual_domain_moe.py:139-174``): scores plus
+  ``log(max(g, tiny))`` per expert, ``-inf`` where ``g == 0``, top-k over the
+  flat atom axis, and its gradients into queries, keys, values and gates.
 
 Parity of this oracle is pinned against golden vectors produced by running
 the reference's own ``sparse_topk_attention`` (see ``tests/golden``).  The
@@ -52,6 +56,9 @@ __all__ = [
     "moe_route_top1",
     "moe_topk_attention_forward",
     "moe_topk_attention_backward",
+    "gate_bias",
+    "gated_mixture_forward",
+    "gated_mixture_backward",
     "gap_aware_index_mismatches",
 ]
 
@@ -352,6 +359,89 @@ def moe_topk_attention_backward(
         dq[rows] = gq[0]
         ddict[e] = gk[0] + gv[0]
     return dq, ddict
+
+
+def gate_bias(gates: np.ndarray) -> np.ndarray:
+    """Additive score bias of the gate fold: ``log(max(g, tiny))``, ``-inf`` where ``g == 0``.
+
+    ``models/modules/dual_domain_moe.py:163-166`` (``tiny`` of the gates' float
+    type).
+    """
+    tiny = np.finfo(gates.dtype).tiny
+    bias = np.log(np.maximum(gates, tiny))
+    return np.where(gates == 0, -np.inf, bias).astype(gates.dtype)
+
+
+def gated_mixture_forward(
+    queries: np.ndarray,
+    keys: np.ndarray,
+    values: np.ndarray,
+    gates: np.ndarray | None,
+    k: int,
+):
+    """Gated top-k mixture of ``DualDomainMoEDictionary._mixture``.
+
+    ``models/modules/dual_domain_moe.py:139-174``: scores ``q·keys`` (no
+    scale) of ``(B, N, d)`` queries against ``(E, M, d)`` projected atoms, the
+    gate fold (``gate_bias`` per expert), then top-k attention over the flat
+    ``E*M`` atom axis (``models/modules/topk_select.py:106-162``).  Returns
+    ``(out (B, N, C), flat indices int32, lse, top_scores)``.
+    """
+    b, n, d = queries.shape
+    e, m, _ = keys.shape
+    scores = np.einsum("bnd,emd->bnem", queries, keys)
+    if gates is not None:
+        scores = scores + gate_bias(gates)[..., None].astype(scores.dtype)
+    flat = scores.reshape(1, b * n, e * m)
+    out, idx, lse, top = topk_attention_forward(
+        queries.reshape(1, b * n, d), keys.reshape(1, e * m, d), values.reshape(1, e * m, -1), k, 1.0,
+        scores=flat,
+    )
+    return out.reshape(b, n, -1), idx.reshape(b, n, k), lse.reshape(b, n), top.reshape(b, n, k)
+
+
+def gated_mixture_backward(
+    queries: np.ndarray,
+    keys: np.ndarray,
+    values: np.ndarray,
+    gates: np.ndarray | None,
+    indices: np.ndarray,
+    grad_out: np.ndarray,
+):
+    """Gradients of ``gated_mixture_forward`` on its selection, float64.
+
+    Returns ``(dq, dkeys, dvalues, dgates)`` (``dgates`` None without gates).
+    The fold contributes ``dgates[b, n, e] = sum of dS over the selected atoms
+    of expert e / g``, zero where the gate is 0 (masked) or below ``tiny``
+    (the clamp), as autograd through ``clamp_min(tiny).log()`` gives.
+    """
+    b, n, d = queries.shape
+    e, m, _ = keys.shape
+    q = queries.astype(np.float64).reshape(1, b * n, d)
+    kk = keys.astype(np.float64).reshape(1, e * m, d)
+    v = values.astype(np.float64).reshape(1, e * m, -1)
+    idx = indices.astype(np.int64).reshape(1, b * n, -1)
+    do = grad_out.astype(np.float64).reshape(1, b * n, -1)
+    s = np.einsum("bnd,bnkd->bnk", q, _gather_rows(kk, idx))
+    if gates is not None:
+        g = gates.astype(np.float64).reshape(b * n, e)
+        s = s + np.take_along_axis(gate_bias(gates).astype(np.float64).reshape(1, b * n, e), idx // m, axis=-1)
+    p, _ = _softmax_lse(s)
+    gg = np.einsum("bnf,bnkf->bnk", do, _gather_rows(v, idx))
+    ds = p * (gg - np.sum(p * gg, axis=-1, keepdims=True))
+    dq = np.einsum("bnk,bnkd->bnd", ds, _gather_rows(kk, idx))
+    dk = np.zeros_like(kk)
+    dv = np.zeros_like(v)
+    rows = np.broadcast_to(np.zeros((1, 1, 1), dtype=np.int64), idx.shape)
+    np.add.at(dk, (rows, idx), ds[..., None] * q[:, :, None, :])
+    np.add.at(dv, (rows, idx), p[..., None] * do[:, :, None, :])
+    dgates = None
+    if gates is not None:
+        dbias = np.zeros((b * n, e))
+        np.add.at(dbias, (np.repeat(np.arange(b * n), idx.shape[-1]), (idx[0] // m).ravel()), ds[0].ravel())
+        tiny = np.finfo(gates.dtype).tiny
+        dgates = np.where(g > tiny, dbias / np.where(g > tiny, g, 1.0), 0.0).reshape(b, n, e)
+    return dq.reshape(b, n, d), dk.reshape(e, m, d), dv.reshape(e, m, -1), dgates
 
 
 def gap_aware_index_mismatches(

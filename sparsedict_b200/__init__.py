@@ -3,8 +3,10 @@
 Public API (the reference's names and signatures):
     fused_topk_attention, FusedTopKAttentionFunction, hybrid_topk_attention,
     tiled_affinity, tiled_topk, tiled_topk_aggregate
-plus routed dictionary attention (``routed_dictionary_attention``) and the
-row-sharded multi-GPU step (``sparsedict_b200.sharded``).
+plus routed dictionary attention (``routed_dictionary_attention``), the gated
+mixture over a bank of dictionary atoms (``gated_mixture_attention``, the
+``_mixture`` of SparseDict's MoE dictionary) and the row-sharded multi-GPU step
+(``sparsedict_b200.sharded``).
 """
 
 from .kernels.fused_topk_attn import (
@@ -15,9 +17,12 @@ from .kernels.fused_topk_attn import (
     tiled_topk_aggregate,
 )
 from .kernels.hybrid_topk import _hybrid_topk_attention_with_aux, hybrid_topk_attention
+from .mixture import GatedMixtureFunction, gated_mixture_attention
 
 __all__ = [
     "FusedTopKAttentionFunction",
+    "GatedMixtureFunction",
+    "gated_mixture_attention",
     "fused_topk_attention",
     "hybrid_topk_attention",
     "tiled_affinity",

@@ -40,6 +40,10 @@ SIGNATURES = {
     "sdk_topk_attn_fwd": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _i32, _f64, _i32, _i32, _p],
     "sdk_topk_attn_bwd": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _i32, _f64, _i32,
                           _i32, _i32, _p],
+    "sdk_topk_attn_fwd_biased": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _i32, _f64, _i32,
+                                 _p, _i64, _i32, _i32, _p],
+    "sdk_topk_attn_bwd_biased": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _i32, _f64,
+                                 _i32, _i32, _p, _p, _i64, _i32, _i32, _p],
     "sdk_finalize_grad": [_p, _p, _i64, _f64, _i32, _p],
     "sdk_topk_attn_bwd_noalloc": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _i32, _f64, _i32, _p],
     "sdk_affinity": [_p, _p, _p, _i64, _i64, _i32, _i64, _i64, _i32, _p],

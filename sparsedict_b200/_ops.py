@@ -30,11 +30,15 @@ def topk_attn_fwd(
     row_offsets: torch.Tensor | None = None,
     row_index: torch.Tensor | None = None,
     out: torch.Tensor | None = None,
+    seg_bias: torch.Tensor | None = None,
 ):
     """Fused forward over ``q2 [rows or (S, n), d]``, ``k2 [S, m, d]``, ``v2 [S, m, dv]``.
 
     Returns ``(out, top_idx int32 [rows, k], lse [rows], top_scores|None)``
     where ``rows`` is ``S * n`` (uniform slices) or the grouped row count.
+    ``seg_bias [rows, segs]`` (accumulator dtype, optional) adds
+    ``seg_bias[r, j // (m // segs)]`` to the scaled score of row ``r`` and
+    key ``j`` (``m`` must divide into ``segs`` equal segments).
     """
     slices, m, d = k2.shape
     dv = v2.shape[-1]
@@ -51,13 +55,15 @@ def topk_attn_fwd(
     lse = torch.empty((rows,), device=dev, dtype=acc)
     scores = torch.empty((rows, topk), device=dev, dtype=acc) if want_scores else None
     with torch.cuda.device(dev):
-        nat.call(
-            "sdk_topk_attn_fwd",
-            q2.data_ptr(), k2.data_ptr(), v2.data_ptr(), out.data_ptr(), idx.data_ptr(), lse.data_ptr(),
-            nat.ptr(scores), nat.ptr(row_offsets), nat.ptr(row_index),
-            slices, n, m, d, dv, topk, float(scale), int(score_grid), nat.TORCH_TO_SDK[q2.dtype],
-            nat.stream_of(dev),
-        )
+        head = (q2.data_ptr(), k2.data_ptr(), v2.data_ptr(), out.data_ptr(), idx.data_ptr(), lse.data_ptr(),
+                nat.ptr(scores), nat.ptr(row_offsets), nat.ptr(row_index),
+                slices, n, m, d, dv, topk, float(scale), int(score_grid))
+        if seg_bias is None:
+            nat.call("sdk_topk_attn_fwd", *head, nat.TORCH_TO_SDK[q2.dtype], nat.stream_of(dev))
+        else:
+            segs = seg_bias.shape[-1]
+            nat.call("sdk_topk_attn_fwd_biased", *head, seg_bias.data_ptr(), m // segs, segs,
+                     nat.TORCH_TO_SDK[q2.dtype], nat.stream_of(dev))
     return out, idx, lse, scores
 
 
@@ -77,8 +83,14 @@ def topk_attn_bwd(
     row_offsets: torch.Tensor | None = None,
     row_index: torch.Tensor | None = None,
     dq: torch.Tensor | None = None,
+    seg_bias: torch.Tensor | None = None,
+    dseg_bias: torch.Tensor | None = None,
 ):
-    """Sparse backward; returns ``(dq, dk_acc, dv_acc)`` (accumulators in ``acc_dtype``)."""
+    """Sparse backward; returns ``(dq, dk_acc, dv_acc)`` (accumulators in ``acc_dtype``).
+
+    With ``seg_bias`` (as in ``topk_attn_fwd``), ``dseg_bias [rows, segs]``
+    (optional) receives the per-segment sums of dS over each row's selection.
+    """
     slices, m, d = k2.shape
     dv = v2.shape[-1]
     topk = top_idx.shape[-1]
@@ -92,13 +104,15 @@ def topk_attn_bwd(
     if dv_acc is None:
         dv_acc = torch.empty((slices, m, dv), device=dev, dtype=acc)
     with torch.cuda.device(dev):
-        nat.call(
-            "sdk_topk_attn_bwd",
-            q2.data_ptr(), k2.data_ptr(), v2.data_ptr(), dout2.data_ptr(), top_idx.data_ptr(), lse.data_ptr(),
-            dq.data_ptr(), dk_acc.data_ptr(), dv_acc.data_ptr(), nat.ptr(row_offsets), nat.ptr(row_index),
-            slices, n, m, d, dv, topk, float(scale), int(score_grid), int(accumulate), nat.TORCH_TO_SDK[q2.dtype],
-            nat.stream_of(dev),
-        )
+        head = (q2.data_ptr(), k2.data_ptr(), v2.data_ptr(), dout2.data_ptr(), top_idx.data_ptr(), lse.data_ptr(),
+                dq.data_ptr(), dk_acc.data_ptr(), dv_acc.data_ptr(), nat.ptr(row_offsets), nat.ptr(row_index),
+                slices, n, m, d, dv, topk, float(scale), int(score_grid), int(accumulate))
+        if seg_bias is None:
+            nat.call("sdk_topk_attn_bwd", *head, nat.TORCH_TO_SDK[q2.dtype], nat.stream_of(dev))
+        else:
+            segs = seg_bias.shape[-1]
+            nat.call("sdk_topk_attn_bwd_biased", *head, seg_bias.data_ptr(), nat.ptr(dseg_bias), m // segs, segs,
+                     nat.TORCH_TO_SDK[q2.dtype], nat.stream_of(dev))
     return dq, dk_acc, dv_acc
 
 

@@ -40,6 +40,10 @@ template <typename Acc> struct BwdArgs {
   int d, dv, topk;
   Acc scale, root, grid;
   unsigned int* status;
+  const Acc* seg_bias;  // nullable: score bias per (logical row, key segment)
+  Acc* dseg_bias;       // nullable: per (row, segment) sum of dS over the selected keys
+  int64_t seg_len;
+  int segs;
 };
 
 __device__ __forceinline__ int64_t slice_of_row(const SliceGeometry& g, int64_t r) {
@@ -98,6 +102,7 @@ __global__ void __launch_bounds__(NT) sparse_bwd(BwdArgs<typename AccOf<T>::type
         Acc s = 0;
         for (int f = 0; f < a.d; ++f) s = fma(qv[f], to_acc(kr[f]), s);
         s = (a.grid > 0) ? rint_acc((s * a.grid) / a.root) / a.grid : s * a.scale;
+        if (a.seg_bias) s += a.seg_bias[r * a.segs + key / a.seg_len];
         p = exp_acc(s - l);
         for (int f = 0; f < a.dv; ++f) g = fma(dov[f], to_acc(vr[f]), g);
       }
@@ -112,6 +117,12 @@ __global__ void __launch_bounds__(NT) sparse_bwd(BwdArgs<typename AccOf<T>::type
     __syncwarp();
     for (int j = lane; j < a.topk; j += kWarp) dsj[j] = pj[j] * (dsj[j] - delta);
     __syncwarp();
+    if (a.dseg_bias && lane == 0) {
+      // the warp owns row r: one lane adds its dS per segment in selection
+      // order (deterministic, no atomics; the buffer starts at zero)
+      for (int j = 0; j < a.topk; ++j)
+        if (ij[j] >= 0) a.dseg_bias[r * a.segs + ij[j] / a.seg_len] += dsj[j];
+    }
 
     T* dqr = static_cast<T*>(a.dq) + pr * a.d;
     for (int f = lane; f < a.d; f += kWarp) {
@@ -293,6 +304,10 @@ int launch_d64(const BwdLaunch& L) {
   a.root = (float)(1.0 / L.scale);
   a.grid = 0.f;
   a.status = L.status;
+  a.seg_bias = nullptr;
+  a.dseg_bias = nullptr;
+  a.seg_len = 0;
+  a.segs = 0;
   if (a.rows <= 0) return SDK_OK;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -307,7 +322,8 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 
 bool d64_supported(const BwdLaunch& L) {
   return (L.dtype == SDK_DTYPE_BF16 || L.dtype == SDK_DTYPE_F16) && L.d == 64 && L.dv == 64 && L.topk <= 64 &&
-         L.score_grid == 0 && aligned16(L.k) && aligned16(L.v) && aligned16(L.dk_acc) && aligned16(L.dv_acc);
+         L.score_grid == 0 && !L.seg_bias && !L.dseg_bias && aligned16(L.k) && aligned16(L.v) &&
+         aligned16(L.dk_acc) && aligned16(L.dv_acc);
 }
 
 template <typename T>
@@ -327,6 +343,10 @@ int launch(const BwdLaunch& L) {
   a.root = (Acc)(1.0 / L.scale);
   a.grid = (Acc)L.score_grid;
   a.status = L.status;
+  a.seg_bias = static_cast<const Acc*>(L.seg_bias);
+  a.dseg_bias = static_cast<Acc*>(L.dseg_bias);
+  a.seg_len = L.seg_len;
+  a.segs = L.segs;
   const size_t smem = (size_t)WARPS * ((L.d + L.dv + 2 * L.topk) * sizeof(Acc) + L.topk * sizeof(int));
   if (smem > kMaxDynamicSmem) return SDK_ERR_UNSUPPORTED;
   if (a.rows <= 0) return SDK_OK;

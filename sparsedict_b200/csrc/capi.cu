@@ -110,10 +110,14 @@ int sdk_device_status(unsigned int* bits, int32_t clear, void* stream) {
   return record(cudaStreamSynchronize(st));
 }
 
-int sdk_topk_attn_fwd(const void* q, const void* k, const void* v, void* out, int32_t* top_idx, void* lse,
-                      void* top_scores, const int32_t* row_offsets, const int32_t* row_index, int64_t slices,
-                      int64_t n, int64_t m, int32_t d, int32_t dv, int32_t topk, double scale, int32_t score_grid,
-                      int32_t dtype, void* stream) {
+}  // extern "C"
+
+namespace {
+
+int fwd_impl(const void* q, const void* k, const void* v, void* out, int32_t* top_idx, void* lse, void* top_scores,
+             const int32_t* row_offsets, const int32_t* row_index, int64_t slices, int64_t n, int64_t m, int32_t d,
+             int32_t dv, int32_t topk, double scale, int32_t score_grid, const void* seg_bias, int64_t seg_len,
+             int32_t segs, int32_t dtype, void* stream) {
   if (!q || !k || !v || !out || !top_idx || !lse) return SDK_ERR_INVALID_ARGUMENT;
   if (!dtype_ok(dtype) || slices <= 0 || n < 0 || m <= 0 || d <= 0 || dv <= 0) return SDK_ERR_INVALID_ARGUMENT;
   if (topk < 1 || topk > m || m > 0x7ffffffe || !(scale > 0) || score_grid < 0) return SDK_ERR_INVALID_ARGUMENT;
@@ -121,15 +125,18 @@ int sdk_topk_attn_fwd(const void* q, const void* k, const void* v, void* out, in
   if (topk > max_topk_generic(dtype, d)) return SDK_ERR_UNSUPPORTED;
   FwdLaunch L{q, k, v, out, top_idx, lse, top_scores, row_offsets, row_index, slices, n, m, d, dv, topk,
               scale, score_grid, dtype, device_status_ptr(), static_cast<cudaStream_t>(stream)};
+  L.seg_bias = seg_bias;
+  L.seg_len = seg_len;
+  L.segs = segs;
   if (fwd_tensorcore_supports(L)) return finish(fwd_tensorcore(L));
   return finish(fwd_generic(L));
 }
 
-int sdk_topk_attn_bwd(const void* q, const void* k, const void* v, const void* dout, const int32_t* top_idx,
-                      const void* lse, void* dq, void* dk_acc, void* dv_acc, const int32_t* row_offsets,
-                      const int32_t* row_index, int64_t slices, int64_t n, int64_t m, int32_t d, int32_t dv,
-                      int32_t topk, double scale, int32_t score_grid, int32_t accumulate, int32_t dtype,
-                      void* stream) {
+int bwd_impl(const void* q, const void* k, const void* v, const void* dout, const int32_t* top_idx, const void* lse,
+             void* dq, void* dk_acc, void* dv_acc, const int32_t* row_offsets, const int32_t* row_index,
+             int64_t slices, int64_t n, int64_t m, int32_t d, int32_t dv, int32_t topk, double scale,
+             int32_t score_grid, int32_t accumulate, const void* seg_bias, void* dseg_bias, int64_t seg_len,
+             int32_t segs, int32_t dtype, void* stream) {
   if (!q || !k || !v || !dout || !top_idx || !lse || !dq || !dk_acc || !dv_acc) return SDK_ERR_INVALID_ARGUMENT;
   if (!dtype_ok(dtype) || slices <= 0 || n < 0 || m <= 0 || d <= 0 || dv <= 0) return SDK_ERR_INVALID_ARGUMENT;
   if (topk < 1 || topk > m || !(scale > 0) || score_grid < 0) return SDK_ERR_INVALID_ARGUMENT;
@@ -140,10 +147,64 @@ int sdk_topk_attn_bwd(const void* q, const void* k, const void* v, const void* d
     if (int rc = record(cudaMemsetAsync(dk_acc, 0, (size_t)slices * m * d * acc_sz, st))) return rc;
     if (dv_acc != dk_acc)
       if (int rc = record(cudaMemsetAsync(dv_acc, 0, (size_t)slices * m * dv * acc_sz, st))) return rc;
+    if (dseg_bias) {
+      const int64_t rows = row_offsets ? n : slices * n;
+      if (int rc = record(cudaMemsetAsync(dseg_bias, 0, (size_t)rows * segs * acc_sz, st))) return rc;
+    }
   }
   BwdLaunch L{q, k, v, dout, top_idx, lse, dq, dk_acc, dv_acc, row_offsets, row_index, slices, n, m, d, dv, topk,
               scale, score_grid, dtype, device_status_ptr(), st};
+  L.seg_bias = seg_bias;
+  L.dseg_bias = dseg_bias;
+  L.seg_len = seg_len;
+  L.segs = segs;
   return finish(bwd_sparse(L));
+}
+
+bool segments_ok(const void* seg_bias, int64_t seg_len, int32_t segs, int64_t m) {
+  return seg_bias && seg_len >= 1 && segs >= 1 && seg_len * (int64_t)segs >= m;
+}
+
+}  // namespace
+
+extern "C" {
+
+int sdk_topk_attn_fwd(const void* q, const void* k, const void* v, void* out, int32_t* top_idx, void* lse,
+                      void* top_scores, const int32_t* row_offsets, const int32_t* row_index, int64_t slices,
+                      int64_t n, int64_t m, int32_t d, int32_t dv, int32_t topk, double scale, int32_t score_grid,
+                      int32_t dtype, void* stream) {
+  return fwd_impl(q, k, v, out, top_idx, lse, top_scores, row_offsets, row_index, slices, n, m, d, dv, topk, scale,
+                  score_grid, nullptr, 0, 0, dtype, stream);
+}
+
+int sdk_topk_attn_bwd(const void* q, const void* k, const void* v, const void* dout, const int32_t* top_idx,
+                      const void* lse, void* dq, void* dk_acc, void* dv_acc, const int32_t* row_offsets,
+                      const int32_t* row_index, int64_t slices, int64_t n, int64_t m, int32_t d, int32_t dv,
+                      int32_t topk, double scale, int32_t score_grid, int32_t accumulate, int32_t dtype,
+                      void* stream) {
+  return bwd_impl(q, k, v, dout, top_idx, lse, dq, dk_acc, dv_acc, row_offsets, row_index, slices, n, m, d, dv, topk,
+                  scale, score_grid, accumulate, nullptr, nullptr, 0, 0, dtype, stream);
+}
+
+int sdk_topk_attn_fwd_biased(const void* q, const void* k, const void* v, void* out, int32_t* top_idx, void* lse,
+                             void* top_scores, const int32_t* row_offsets, const int32_t* row_index,
+                             int64_t slices, int64_t n, int64_t m, int32_t d, int32_t dv, int32_t topk,
+                             double scale, int32_t score_grid, const void* seg_bias, int64_t seg_len,
+                             int32_t segs, int32_t dtype, void* stream) {
+  if (!segments_ok(seg_bias, seg_len, segs, m)) return SDK_ERR_INVALID_ARGUMENT;
+  return fwd_impl(q, k, v, out, top_idx, lse, top_scores, row_offsets, row_index, slices, n, m, d, dv, topk, scale,
+                  score_grid, seg_bias, seg_len, segs, dtype, stream);
+}
+
+int sdk_topk_attn_bwd_biased(const void* q, const void* k, const void* v, const void* dout, const int32_t* top_idx,
+                             const void* lse, void* dq, void* dk_acc, void* dv_acc, const int32_t* row_offsets,
+                             const int32_t* row_index, int64_t slices, int64_t n, int64_t m, int32_t d, int32_t dv,
+                             int32_t topk, double scale, int32_t score_grid, int32_t accumulate,
+                             const void* seg_bias, void* dseg_bias, int64_t seg_len, int32_t segs, int32_t dtype,
+                             void* stream) {
+  if (!segments_ok(seg_bias, seg_len, segs, m)) return SDK_ERR_INVALID_ARGUMENT;
+  return bwd_impl(q, k, v, dout, top_idx, lse, dq, dk_acc, dv_acc, row_offsets, row_index, slices, n, m, d, dv, topk,
+                  scale, score_grid, accumulate, seg_bias, dseg_bias, seg_len, segs, dtype, stream);
 }
 
 int sdk_finalize_grad(const void* acc, void* out, int64_t count, double multiplier, int32_t dtype, void* stream) {

@@ -42,6 +42,9 @@ template <typename Acc> struct FwdArgs {
   int d, dv, topk, capp;
   Acc scale, root, grid;
   unsigned int* status;
+  const Acc* seg_bias;  // nullable: score bias per (logical row, key segment)
+  int64_t seg_len;
+  int segs;
 };
 
 template <typename Acc>
@@ -134,6 +137,8 @@ __global__ void __launch_bounds__(NT) fused_fwd_generic(FwdArgs<typename AccOf<T
       for (int j = 0; j < 4; ++j) {
         Acc s = acc[i][j];
         s = (a.grid > 0) ? rint_acc((s * a.grid) / a.root) / a.grid : s * a.scale;
+        if (a.seg_bias && 4 * ty + i < rows && 4 * tx + j < kvalid)
+          s += a.seg_bias[(row0 + 4 * ty + i) * a.segs + (kt + 4 * tx + j) / a.seg_len];
         Ss[(4 * ty + i) * SS + 4 * tx + j] = s;
       }
     __syncthreads();
@@ -223,6 +228,9 @@ int launch(const FwdLaunch& L) {
   a.root = (Acc)(1.0 / L.scale);
   a.grid = (Acc)L.score_grid;
   a.status = L.status;
+  a.seg_bias = static_cast<const Acc*>(L.seg_bias);
+  a.seg_len = L.seg_len;
+  a.segs = L.segs;
   const int64_t tiles = L.row_offsets ? (L.n + BQ - 1) / BQ + L.slices : L.slices * ((L.n + BQ - 1) / BQ);
   if (tiles <= 0) return SDK_OK;
   auto kern = fused_fwd_generic<T>;

@@ -995,7 +995,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 bool fwd_tensorcore_supports(const FwdLaunch& L) {
   if (L.dtype != SDK_DTYPE_BF16 && L.dtype != SDK_DTYPE_F16) return false;
   if (L.d != D || L.dv != D || L.score_grid != 0) return false;
-  if (L.row_offsets || L.row_index) return false;
+  if (L.row_offsets || L.row_index || L.seg_bias) return false;
   if (L.m > 65536 || L.topk > 64 || L.n < 1) return false;
   if (L.slices * L.n > 0x7fffff00 || L.slices * L.m > 0x7fffffff) return false;
   if (!aligned16(L.q) || !aligned16(L.k) || !aligned16(L.v) || !aligned16(L.out)) return false;

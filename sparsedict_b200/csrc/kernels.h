@@ -34,6 +34,12 @@ struct FwdLaunch {
   int dtype;
   unsigned int* status;
   cudaStream_t stream;
+  // Optional additive score bias per (logical query row, key segment):
+  // score(r, j) += seg_bias[r * segs + j / seg_len], after the scale.  In the
+  // accumulator type (double for fp64 inputs, float otherwise).
+  const void* seg_bias = nullptr;
+  int64_t seg_len = 0;
+  int segs = 0;
 };
 
 struct BwdLaunch {
@@ -55,6 +61,13 @@ struct BwdLaunch {
   int dtype;
   unsigned int* status;
   cudaStream_t stream;
+  // Optional score bias as in FwdLaunch; dseg_bias (nullable, zeroed by the
+  // caller, rows * segs) receives the sum of dS over each row's selected keys
+  // of each segment.
+  const void* seg_bias = nullptr;
+  void* dseg_bias = nullptr;
+  int64_t seg_len = 0;
+  int segs = 0;
 };
 
 // Records a CUDA error for sdk_last_cuda_error(); returns SDK_ERR_CUDA (or

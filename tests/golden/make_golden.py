@@ -191,6 +191,33 @@ def main() -> None:
                         dq=gq[0], datoms=ga).items():
         out[f"moe_{name}"] = _np(t)
 
+    # gated mixture (models/modules/dual_domain_moe.py:139-174) with soft gates:
+    # separate key and value projections of the atoms, gates from top-2 softmax
+    # routing for half of the tokens (zeros elsewhere) and dense softmax gates
+    # for the rest, gradients into queries, keys, values and gates.
+    torch.manual_seed(5)
+    b, n, dk, c, e, m, kk = 2, 48, 16, 12, 4, 40, 9
+    qm = torch.randn(b, n, dk)
+    keys = torch.randn(e, m, dk) / math.sqrt(dk)
+    values = torch.randn(e, m, c)
+    logits = torch.randn(b, n, e)
+    top_l, top_e = logits.topk(2, dim=-1)
+    sparse_g = torch.zeros_like(logits).scatter(-1, top_e, torch.softmax(top_l, -1))
+    dense_g = torch.softmax(logits, -1)
+    gates = torch.where((torch.arange(n) % 2 == 0).view(1, n, 1), sparse_g, dense_g)
+    dom = torch.randn(b, n, c)
+    qg, kg, vg, gg = (t.clone().requires_grad_(True) for t in (qm, keys, values, gates))
+    scores = torch.einsum("bnk,emk->bnem", qg, kg)
+    tiny = torch.finfo(scores.dtype).tiny
+    scores = scores + gg.clamp_min(tiny).log().unsqueeze(-1)
+    scores = scores.masked_fill(gg.unsqueeze(-1) == 0, float("-inf"))
+    scores = scores.reshape(b, n, e * m)
+    res = sparse_topk_attention(scores, vg.reshape(e * m, c), kk)
+    gq, gkeys, gvalues, ggates = torch.autograd.grad((res.output * dom).sum(), (qg, kg, vg, gg))
+    for name, t in dict(q=qm, keys=keys, values=values, gates=gates, do=dom, out=res.output,
+                        flat_idx=res.indices, dq=gq, dkeys=gkeys, dvalues=gvalues, dgates=ggates).items():
+        out[f"mix_{name}"] = _np(t)
+
     path = HERE / "reference_vectors.npz"
     np.savez_compressed(path, **out)
     print(f"wrote {path} ({path.stat().st_size / 1024:.0f} KiB, {len(out)} arrays)")

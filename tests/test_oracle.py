@@ -212,3 +212,23 @@ def test_unordered_set_comparison():
     assert oracle.gap_aware_index_mismatches(np.array([[2, 0]]), np.array([[0, 1]]), scores, 1e-4, ordered=False) == 0
     assert oracle.gap_aware_index_mismatches(np.array([[3, 0]]), np.array([[0, 1]]), scores, 1e-4, ordered=False) == 1
     assert oracle.gap_aware_index_mismatches(np.array([[1, 0]]), np.array([[0, 1]]), scores, 1e-4, ordered=True) == 1
+
+
+def test_gated_mixture_matches_reference_mixture(golden):
+    # DualDomainMoEDictionary._mixture with soft gates (top-2 and dense
+    # softmax rows, exact zeros), separate key and value projections
+    g = {k[4:]: v for k, v in golden.items() if k.startswith("mix_")}
+    out, idx, _, _ = oracle.gated_mixture_forward(g["q"], g["keys"], g["values"], g["gates"], 9)
+    assert np.array_equal(idx, g["flat_idx"])
+    np.testing.assert_allclose(out, g["out"], atol=1e-5, rtol=0)
+    dq, dk, dv, dg = oracle.gated_mixture_backward(g["q"], g["keys"], g["values"], g["gates"], idx, g["do"])
+    for got, name in ((dq, "dq"), (dk, "dkeys"), (dv, "dvalues"), (dg, "dgates")):
+        np.testing.assert_allclose(got, g[name], atol=1e-5, rtol=1e-4)
+
+
+def test_gate_bias_masks_zero_gates_and_clamps_tiny():
+    gates = np.array([[0.0, 1e-45, 0.25, 1.0]], dtype=np.float32)
+    bias = oracle.gate_bias(gates)
+    assert bias[0, 0] == -np.inf
+    assert bias[0, 1] == np.float32(np.log(np.finfo(np.float32).tiny))
+    np.testing.assert_allclose(bias[0, 2:], np.log([0.25, 1.0]), rtol=1e-6)

@@ -509,3 +509,72 @@ def test_tie_stress_full_configuration_sampled_rows_bit_exact(topk):
         o, _, _, _ = oracle.topk_attention_forward(qs, ks, v[s].cpu().numpy()[None], topk, 1 / math.sqrt(d),
                                                    scores=scores)
         np.testing.assert_allclose(out.view(bh, n, d)[s, rows].cpu().numpy(), o[0], atol=1e-5, rtol=1e-5)
+
+
+# --- gated mixture (DualDomainMoEDictionary._mixture) -----------------------------
+
+
+def test_gated_mixture_matches_reference_fp32(golden):
+    from sparsedict_b200 import _ops, gated_mixture_attention
+
+    g = {k[4:]: v for k, v in golden.items() if k.startswith("mix_")}
+    q, keys, values, gates = (_t(g[n]).requires_grad_(True) for n in ("q", "keys", "values", "gates"))
+    out = gated_mixture_attention(q, keys, values, 9, gates)
+    np.testing.assert_allclose(out.detach().cpu().numpy(), g["out"], atol=1e-5, rtol=0)
+    grads = torch.autograd.grad((out * _t(g["do"])).sum(), (q, keys, values, gates))
+    for got, name in zip(grads, ("dq", "dkeys", "dvalues", "dgates")):
+        np.testing.assert_allclose(got.cpu().numpy(), g[name], atol=1e-4, rtol=1e-3)
+    # the selection itself: the biased forward picks the reference's flat indices
+    b, n, dk = g["q"].shape
+    e, m, _ = g["keys"].shape
+    bias = torch.where(gates == 0, torch.full_like(gates, float("-inf")),
+                       gates.clamp_min(torch.finfo(torch.float32).tiny).log()).detach().reshape(b * n, e)
+    _, idx, _, _ = _ops.topk_attn_fwd(q.detach().reshape(1, b * n, dk), keys.detach().reshape(1, e * m, dk),
+                                      values.detach().reshape(1, e * m, -1), 9, 1.0, seg_bias=bias.contiguous())
+    assert np.array_equal(idx.cpu().numpy().reshape(b, n, 9), g["flat_idx"])
+
+
+def test_gated_mixture_bf16_vs_oracle():
+    from sparsedict_b200 import gated_mixture_attention
+
+    gen = torch.Generator().manual_seed(17)
+    b, n, dk, c, e, m, k = 2, 300, 64, 64, 8, 256, 16
+    q = torch.randn(b, n, dk, generator=gen).to(torch.bfloat16)
+    keys = (torch.randn(e, m, dk, generator=gen) / 8).to(torch.bfloat16)
+    values = torch.randn(e, m, c, generator=gen).to(torch.bfloat16)
+    logits = torch.randn(b, n, e, generator=gen)
+    top_l, top_e = logits.topk(2, dim=-1)
+    gates = torch.zeros_like(logits).scatter(-1, top_e, torch.softmax(top_l, -1)).to(torch.bfloat16)
+    do = torch.randn(b, n, c, generator=gen).to(torch.bfloat16)
+    qd, kd, vd, gd = (t.to(DEV).requires_grad_(True) for t in (q, keys, values, gates))
+    out = gated_mixture_attention(qd, kd, vd, k, gd)
+    grads = torch.autograd.grad((out.float() * do.to(DEV).float()).sum(), (qd, kd, vd, gd))
+    qf, kf, vf, gf, dof = (t.float().numpy() for t in (q, keys, values, gates, do))
+    o, idx, _, _ = oracle.gated_mixture_forward(qf, kf, vf, gf, k)
+    np.testing.assert_allclose(out.float().detach().cpu().numpy(), o, rtol=2e-2, atol=2e-2)
+    ref = oracle.gated_mixture_backward(qf, kf, vf, gf, idx, dof)
+    for got, exp in zip(grads, ref):
+        got = got.float().cpu().numpy()
+        assert np.abs(got - exp).max() <= 2e-2 * max(1.0, np.abs(exp).max())
+
+
+def test_gated_mixture_without_gates_is_flat_top_k():
+    from sparsedict_b200 import _ops, gated_mixture_attention
+
+    torch.manual_seed(3)
+    q, keys, values = torch.randn(2, 50, 16, device=DEV), torch.randn(3, 40, 16, device=DEV), torch.randn(3, 40, 8, device=DEV)
+    out = gated_mixture_attention(q, keys, values, 5)
+    flat, _, _, _ = _ops.topk_attn_fwd(q.reshape(1, 100, 16), keys.reshape(1, 120, 16), values.reshape(1, 120, 8), 5, 1.0)
+    assert torch.equal(out.reshape(1, 100, 8), flat)
+
+
+def test_gated_mixture_gradcheck_fp64():
+    from sparsedict_b200 import gated_mixture_attention
+
+    torch.manual_seed(9)
+    q = torch.randn(1, 6, 5, dtype=torch.float64, device=DEV, requires_grad=True)
+    keys = torch.randn(3, 7, 5, dtype=torch.float64, device=DEV, requires_grad=True)
+    values = torch.randn(3, 7, 4, dtype=torch.float64, device=DEV, requires_grad=True)
+    gates = (torch.rand(1, 6, 3, dtype=torch.float64, device=DEV) + 0.1).requires_grad_(True)
+    torch.autograd.gradcheck(lambda *a: gated_mixture_attention(a[0], a[1], a[2], 4, a[3]), (q, keys, values, gates),
+                             eps=1e-6, atol=1e-4, nondet_tol=1e-7)

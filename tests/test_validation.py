@@ -123,3 +123,23 @@ def test_tiled_topk_aggregate_rejects_non_matrix_inputs():
 def test_tiled_topk_aggregate_requires_cuda():
     with pytest.raises(ValueError, match="requires CUDA"):
         tiled_topk_aggregate(torch.rand(2, 3), torch.zeros(2, 3, dtype=torch.int64), torch.rand(5, 6))
+
+
+@pytest.mark.parametrize(
+    ("q", "keys", "values", "gates", "k", "error", "message"),
+    [
+        (torch.rand(2, 3, 4), torch.rand(2, 5, 4), torch.rand(2, 5, 6), torch.rand(2, 3, 3), 2, ValueError,
+         r"expected gates of shape \(2, 3, 2\)"),
+        (torch.rand(2, 3, 4), torch.rand(2, 5, 3), torch.rand(2, 5, 6), None, 2, ValueError, "feature sizes must match"),
+        (torch.rand(3, 4), torch.rand(2, 5, 4), torch.rand(2, 5, 6), None, 2, ValueError, "expected queries"),
+        (torch.rand(2, 3, 4), torch.rand(2, 5, 4), torch.rand(2, 4, 6), None, 2, ValueError, "values must be"),
+        (torch.rand(2, 3, 4), torch.rand(2, 5, 4), torch.rand(2, 5, 6), None, 11, ValueError, "top_k must be"),
+        (torch.rand(2, 3, 4), torch.rand(2, 5, 4), torch.rand(2, 5, 6), None, 2, ValueError, "one CUDA device"),
+        ([1.0], torch.rand(2, 5, 4), torch.rand(2, 5, 6), None, 2, TypeError, "queries must be a torch.Tensor"),
+    ],
+)
+def test_gated_mixture_rejects_invalid_arguments(q, keys, values, gates, k, error, message):
+    from sparsedict_b200 import gated_mixture_attention
+
+    with pytest.raises(error, match=message):
+        gated_mixture_attention(q, keys, values, k, gates)
