@@ -186,7 +186,8 @@ int sdk_affinity(const void* q, const void* k, float* scores, int64_t n, int64_t
 /*
  * Stage 2 alone: per-row top-k of scores[rows, m] (row stride in elements),
  * writing values (input dtype) and int64 indices.  Replaces tiled_topk
- * (kernels/fused_topk_attn.py:290-336); dtype F32 or F16.
+ * (kernels/fused_topk_attn.py:290-336, F32 or F16 there) and the torch.topk of
+ * models/modules/topk_select.py:94-103 (any float dtype: F32, F16, BF16, F64).
  */
 int sdk_topk_select(const void* scores, void* top_values, int64_t* top_idx, int64_t rows, int64_t m,
                     int64_t row_stride, int32_t topk, int32_t dtype, void* stream);

@@ -6,7 +6,8 @@ Public API (the reference's names and signatures):
 plus routed dictionary attention (``routed_dictionary_attention``), the gated
 mixture over a bank of dictionary atoms (``gated_mixture_attention``, the
 ``_mixture`` of SparseDict's MoE dictionary) and the row-sharded multi-GPU step
-(``sparsedict_b200.sharded``).
+(``sparsedict_b200.sharded``); the selection operators of SparseDict's
+``topk_select`` module over given scores live in ``sparsedict_b200.selection``.
 """
 
 from .kernels.fused_topk_attn import (

@@ -226,7 +226,7 @@ int sdk_topk_select(const void* scores, void* top_values, int64_t* top_idx, int6
                     int64_t row_stride, int32_t topk, int32_t dtype, void* stream) {
   if (!scores || !top_values || !top_idx || rows <= 0 || m <= 0 || row_stride < m) return SDK_ERR_INVALID_ARGUMENT;
   if (topk < 1 || topk > m || m > 0x7ffffffe) return SDK_ERR_INVALID_ARGUMENT;
-  if (dtype != SDK_DTYPE_F32 && dtype != SDK_DTYPE_F16) return SDK_ERR_INVALID_ARGUMENT;
+  if (!dtype_ok(dtype)) return SDK_ERR_INVALID_ARGUMENT;
   if (int rc = check_device()) return rc;
   return finish(topk_select(scores, top_values, top_idx, rows, m, row_stride, topk, dtype,
                             static_cast<cudaStream_t>(stream)));

@@ -59,21 +59,24 @@ __global__ void __launch_bounds__(A_NT) affinity_kernel(const T* __restrict__ q,
 // One warp per row streams the row 32 keys at a time, keeps keys that beat
 // the running k-th best in a shared-memory list and re-ranks the list with a
 // warp bitonic sort when it could overflow.
+// Comparisons run in the accumulator type (double for fp64 scores, float
+// otherwise), which holds every input value exactly.
 template <typename T>
 __global__ void select_kernel(const T* __restrict__ s, T* __restrict__ vals_out, int64_t* __restrict__ idx_out,
                               int64_t rows, int64_t m, int64_t stride, int topk, int capp) {
+  using Acc = typename AccOf<T>::type;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
-  float* cv = reinterpret_cast<float*>(smem_raw) + warp * capp;
-  int* ci = reinterpret_cast<int*>(reinterpret_cast<float*>(smem_raw) + warps * capp) + warp * capp;
+  Acc* cv = reinterpret_cast<Acc*>(smem_raw) + warp * capp;
+  int* ci = reinterpret_cast<int*>(reinterpret_cast<Acc*>(smem_raw) + warps * capp) + warp * capp;
   for (int64_t r = (int64_t)blockIdx.x * warps + warp; r < rows; r += (int64_t)gridDim.x * warps) {
     const T* row = s + r * stride;
-    float tau = quiet_nan<float>();
+    Acc tau = quiet_nan<Acc>();
     int cnt = 0;
     for (int64_t c0 = 0; c0 < m; c0 += kWarp) {
       const int64_t c = c0 + lane;
       const bool ok = c < m;
-      const float x = ok ? to_acc(row[c]) : 0.f;
+      const Acc x = ok ? to_acc(row[c]) : Acc(0);
       const bool pass = ok && !(x <= tau);
       const unsigned b = __ballot_sync(0xffffffffu, pass);
       if (pass) {
@@ -85,7 +88,7 @@ __global__ void select_kernel(const T* __restrict__ s, T* __restrict__ vals_out,
       __syncwarp();
       if (cnt > capp - kWarp) {
         const int P = next_pow2_dev(cnt);
-        for (int i = cnt + lane; i < P; i += kWarp) { cv[i] = neg_inf<float>(); ci[i] = kPadIndex; }
+        for (int i = cnt + lane; i < P; i += kWarp) { cv[i] = neg_inf<Acc>(); ci[i] = kPadIndex; }
         __syncwarp();
         warp_bitonic_sort(cv, ci, P, lane);
         cnt = topk;
@@ -93,11 +96,11 @@ __global__ void select_kernel(const T* __restrict__ s, T* __restrict__ vals_out,
       }
     }
     const int P = next_pow2_dev(cnt);
-    for (int i = cnt + lane; i < P; i += kWarp) { cv[i] = neg_inf<float>(); ci[i] = kPadIndex; }
+    for (int i = cnt + lane; i < P; i += kWarp) { cv[i] = neg_inf<Acc>(); ci[i] = kPadIndex; }
     __syncwarp();
     warp_bitonic_sort(cv, ci, P, lane);
     for (int j = lane; j < topk; j += kWarp) {
-      vals_out[r * topk + j] = from_acc<T>(cv[j]);
+      vals_out[r * topk + j] = cvt_out<T>(cv[j]);
       idx_out[r * topk + j] = ci[j];
     }
     __syncwarp();
@@ -222,31 +225,36 @@ int affinity(const void* q, const void* k, float* scores, int64_t n, int64_t m, 
   return cudaPeekAtLastError() == cudaSuccess ? SDK_OK : SDK_ERR_CUDA;
 }
 
-int topk_select(const void* scores, void* top_values, int64_t* top_idx, int64_t rows, int64_t m, int64_t stride,
-                int topk, int dtype, cudaStream_t stream) {
+template <typename T>
+int launch_select(const void* scores, void* top_values, int64_t* top_idx, int64_t rows, int64_t m, int64_t stride,
+                  int topk, cudaStream_t stream) {
+  using Acc = typename AccOf<T>::type;
   const int capp = next_pow2_host(topk + kWarp);
+  const size_t per_warp = (size_t)capp * (sizeof(Acc) + sizeof(int));
   int warps = 4;
-  while (warps > 1 && (size_t)warps * capp * 8 > kMaxDynamicSmem) warps >>= 1;
-  const size_t smem = (size_t)warps * capp * 8;
+  while (warps > 1 && warps * per_warp > kMaxDynamicSmem) warps >>= 1;
+  const size_t smem = warps * per_warp;
   if (smem > kMaxDynamicSmem) return SDK_ERR_UNSUPPORTED;
   const int64_t want = (rows + warps - 1) / warps;
   const unsigned grid = (unsigned)(want < 148 * 64 ? want : 148 * 64);
-  if (dtype == SDK_DTYPE_F32) {
-    auto kern = select_kernel<float>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return SDK_ERR_CUDA;
-    kern<<<grid, warps * kWarp, smem, stream>>>(static_cast<const float*>(scores), static_cast<float*>(top_values),
-                                                top_idx, rows, m, stride, topk, capp);
-  } else if (dtype == SDK_DTYPE_F16) {
-    auto kern = select_kernel<__half>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return SDK_ERR_CUDA;
-    kern<<<grid, warps * kWarp, smem, stream>>>(static_cast<const __half*>(scores), static_cast<__half*>(top_values),
-                                                top_idx, rows, m, stride, topk, capp);
-  } else {
-    return SDK_ERR_INVALID_ARGUMENT;
-  }
+  auto kern = select_kernel<T>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return SDK_ERR_CUDA;
+  kern<<<grid, warps * kWarp, smem, stream>>>(static_cast<const T*>(scores), static_cast<T*>(top_values), top_idx,
+                                              rows, m, stride, topk, capp);
   return cudaPeekAtLastError() == cudaSuccess ? SDK_OK : SDK_ERR_CUDA;
+}
+
+int topk_select(const void* scores, void* top_values, int64_t* top_idx, int64_t rows, int64_t m, int64_t stride,
+                int topk, int dtype, cudaStream_t stream) {
+  switch (dtype) {
+    case SDK_DTYPE_F32: return launch_select<float>(scores, top_values, top_idx, rows, m, stride, topk, stream);
+    case SDK_DTYPE_F16: return launch_select<__half>(scores, top_values, top_idx, rows, m, stride, topk, stream);
+    case SDK_DTYPE_BF16:
+      return launch_select<__nv_bfloat16>(scores, top_values, top_idx, rows, m, stride, topk, stream);
+    case SDK_DTYPE_F64: return launch_select<double>(scores, top_values, top_idx, rows, m, stride, topk, stream);
+    default: return SDK_ERR_INVALID_ARGUMENT;
+  }
 }
 
 int topk_aggregate(const void* ts, const void* ti, const void* v, float* out, int64_t rows, int topk, int64_t m,

@@ -578,3 +578,69 @@ def test_gated_mixture_gradcheck_fp64():
     gates = (torch.rand(1, 6, 3, dtype=torch.float64, device=DEV) + 0.1).requires_grad_(True)
     torch.autograd.gradcheck(lambda *a: gated_mixture_attention(a[0], a[1], a[2], 4, a[3]), (q, keys, values, gates),
                              eps=1e-6, atol=1e-4, nondet_tol=1e-7)
+
+
+# --- selection operators of models/modules/topk_select.py ------------------------
+
+
+def test_hard_topk_mask_known_answer(golden):
+    from sparsedict_b200 import selection
+
+    masked, idx = selection.hard_topk_mask(_t(golden["known_scores"]), 2)
+    assert np.array_equal(idx.cpu().numpy(), golden["known_indices"])
+    assert torch.isinf(masked).sum().item() == 4
+
+
+@pytest.mark.parametrize("mode", ["hard", "ste"])
+def test_sparse_topk_attention_configuration_1(golden, mode):
+    from sparsedict_b200 import selection
+
+    g = {k[5:]: v for k, v in golden.items() if k.startswith("cfg1_")}
+    q, k, v = (_t(g[n]).requires_grad_(True) for n in "qkv")
+    scores = (q @ k.transpose(-2, -1)) / math.sqrt(32)
+    res = selection.sparse_topk_attention(scores, v, 8, selection=mode)
+    np.testing.assert_allclose(res.output.detach().cpu().numpy(), g["out"], atol=1e-5, rtol=0)
+    _assert_indices(res.indices.cpu().numpy().reshape(-1, 8), _flat(g["idx"]).reshape(-1, 8),
+                    _oracle_scores64(g["q"], g["k"], 1 / math.sqrt(32)).reshape(-1, 128))
+    assert res.weights.shape == scores.shape and res.masked_scores.shape == scores.shape
+    grads = torch.autograd.grad((res.output * _t(g["do"])).sum(), (q, k, v))
+    for got, name in zip(grads, ("dq", "dk", "dv")):
+        np.testing.assert_allclose(got.cpu().numpy(), g[name], atol=1e-4, rtol=1e-3)
+
+
+def test_straight_through_and_gumbel_samples_vs_oracle():
+    from sparsedict_b200 import selection
+
+    gen = torch.Generator(device=DEV).manual_seed(5)
+    scores = torch.randn(40, 300, device=DEV, generator=gen).requires_grad_(True)
+    vals, idx = selection.straight_through_topk(scores, 7)
+    ov, oi = oracle.topk_order(scores.detach().cpu().numpy(), 7)
+    assert np.array_equal(idx.cpu().numpy(), oi)
+    np.testing.assert_array_equal(vals.detach().cpu().numpy(), ov)
+    w = torch.randn(40, 7, device=DEV)
+    (grad,) = torch.autograd.grad((vals * w).sum(), scores)
+    expected = torch.zeros(40, 300, device=DEV).scatter(-1, idx, w)
+    assert torch.equal(grad, expected)
+    g1 = torch.Generator(device=DEV).manual_seed(123)
+    sv, si = selection.gumbel_perturbed_topk(scores.detach(), 7, sigma=0.5, num_samples=3, generator=g1)
+    g2 = torch.Generator(device=DEV).manual_seed(123)
+    eps = torch.finfo(torch.float32).eps
+    for s in range(3):
+        u = torch.rand(scores.shape, dtype=torch.float32, device=DEV, generator=g2).clamp(min=eps, max=1 - eps)
+        pert = scores.detach() + 0.5 * (-torch.log(-torch.log(u)))
+        pv, pi = oracle.topk_order(pert.cpu().numpy(), 7)
+        assert np.array_equal(si[s].cpu().numpy(), pi)
+        np.testing.assert_array_equal(sv[s].cpu().numpy(), pv)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float64])
+def test_straight_through_topk_all_float_dtypes(dtype):
+    from sparsedict_b200 import selection
+
+    gen = torch.Generator(device=DEV).manual_seed(8)
+    scores = torch.randn(33, 500, device=DEV, generator=gen).to(dtype)
+    vals, idx = selection.straight_through_topk(scores, 19)
+    assert vals.dtype == dtype
+    ov, oi = oracle.topk_order(scores.double().cpu().numpy(), 19)
+    assert np.array_equal(idx.cpu().numpy(), oi)
+    np.testing.assert_array_equal(vals.double().cpu().numpy(), ov)

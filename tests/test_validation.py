@@ -143,3 +143,19 @@ def test_gated_mixture_rejects_invalid_arguments(q, keys, values, gates, k, erro
 
     with pytest.raises(error, match=message):
         gated_mixture_attention(q, keys, values, k, gates)
+
+
+def test_selection_operators_check_arguments():
+    # messages of models/modules/topk_select.py:94-173 (SparseDict)
+    from sparsedict_b200 import selection
+
+    with pytest.raises(ValueError, match="selection must be 'hard' or 'ste'"):
+        selection.sparse_topk_attention(torch.rand(3, 5), torch.rand(5, 2), 2, selection="soft")
+    with pytest.raises(ValueError, match="expected scores with query and atom dimensions"):
+        selection.straight_through_topk(torch.rand(5), 2)
+    with pytest.raises(ValueError, match="floating-point dtype"):
+        selection.hard_topk_mask(torch.ones(3, 5, dtype=torch.int64), 2)
+    with pytest.raises(ValueError, match=r"k must be between 1 and 5; got 6"):
+        selection.straight_through_topk(torch.rand(3, 5), 6)
+    with pytest.raises(ValueError, match="CUDA"):
+        selection.gumbel_perturbed_topk(torch.rand(3, 5), 2)
