@@ -325,8 +325,10 @@ def run_native_arm(args):
                      # compulsory fwd+bwd bytes at the HBM peak
                      "step_frac_tensor": t_tensor / (ms_per_step / 1000.0),
                      "step_frac_hbm": t_hbm / (ms_per_step / 1000.0)},
-        # this library's kernels per step: forward, one backward per bucket, two finalizes
-        "gpu_launches": (1 + len(runner._bucket_ranges()) + 2) * args.steps,
+        # this library's kernels per step: forward, one backward per bucket, and two
+        # conversions per bucket (bucket-major all-reduce) or two in all
+        "gpu_launches": (1 + len(runner._bucket_ranges()) * (3 if runner._bucket_major else 1)
+                         + (0 if runner._bucket_major else 2)) * args.steps,
     }
     if e2e is not None:
         line["e2e"] = e2e

@@ -116,11 +116,14 @@ def topk_attn_bwd(
     return dq, dk_acc, dv_acc
 
 
-def finalize_grad(acc: torch.Tensor, dtype: torch.dtype, multiplier: float = 1.0) -> torch.Tensor:
-    """Accumulator -> ``dtype`` (returns ``acc`` itself when no conversion is needed)."""
-    if acc.dtype == dtype and multiplier == 1.0:
+def finalize_grad(acc: torch.Tensor, dtype: torch.dtype, multiplier: float = 1.0,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """Accumulator -> ``dtype`` (returns ``acc`` itself when no conversion is needed
+    and no ``out`` is given; ``out`` is a contiguous tensor of ``acc``'s shape)."""
+    if out is None and acc.dtype == dtype and multiplier == 1.0:
         return acc
-    out = torch.empty(acc.shape, device=acc.device, dtype=dtype)
+    if out is None:
+        out = torch.empty(acc.shape, device=acc.device, dtype=dtype)
     with torch.cuda.device(acc.device):
         nat.call("sdk_finalize_grad", acc.data_ptr(), out.data_ptr(), acc.numel(), float(multiplier),
                  nat.TORCH_TO_SDK[dtype], nat.stream_of(acc.device))

@@ -18,8 +18,17 @@ cheaper collectives give the same replicated result or keep it sharded:
                           own slices (sharded).
 
 On CUDA the collective runs in buckets of slices on a side stream, so bucket
-``j`` reduces while the backward of bucket ``j+1`` runs.  Every rank issues
-the same collectives in the same order.  The compute backend is pluggable
+``j`` reduces while the backward of bucket ``j+1`` runs.  For the all-reduce
+the fp32 accumulators are laid out bucket-major, ``[bucket][rank][slice]``:
+a rank's slices of one bucket stay contiguous for the kernel, and bucket
+``j`` of every rank forms one contiguous block that a single all-reduce call
+covers (two calls per bucket, not two per rank per bucket).  Each rank
+converts its own part of a bucket to the output dtype in a staging block whose
+other ranks' parts are zero, and the staging block is what is all-reduced:
+every element has exactly one nonzero term, so the sum in the output dtype is
+bit-identical to converting the fp32 sum, at half the bytes for bf16.  A last
+copy puts dK/dV back in slice order.  Every rank issues the same
+collectives in the same order.  The compute backend is pluggable
 (``kernels``): the default calls the native library; tests substitute a CPU
 implementation to exercise the partition and exchange logic on ``gloo``.
 """
@@ -79,8 +88,8 @@ class NativeKernels:
         self._ops.topk_attn_bwd(q, k, v, dout, idx, lse, scale, dk_acc=dk_acc, dv_acc=dv_acc,
                                 accumulate=accumulate, dq=dq)
 
-    def finalize(self, acc, dtype):
-        return self._ops.finalize_grad(acc, dtype)
+    def finalize(self, acc, dtype, out=None):
+        return self._ops.finalize_grad(acc, dtype, out=out)
 
 
 class ShardedTopKAttention:
@@ -104,6 +113,9 @@ class ShardedTopKAttention:
         self.dk_acc = torch.zeros((full, m, d), device=self.device, dtype=acc)
         self.dv_acc = torch.zeros((full, m, dv), device=self.device, dtype=acc)
         self.buckets = max(1, min(buckets, plan.per_rank)) if plan.world > 1 else 1
+        if self._bucket_major:
+            self.stage_k = torch.zeros((full, m, d), device=self.device, dtype=dtype)
+            self.stage_v = torch.zeros((full, m, dv), device=self.device, dtype=dtype)
         on_cuda = self.device.type == "cuda"
         self.comm_stream = (torch.cuda.Stream(device=self.device)
                             if on_cuda and plan.world > 1 and reduce != "none" else None)
@@ -113,12 +125,33 @@ class ShardedTopKAttention:
         edges = [round(i * per / self.buckets) for i in range(self.buckets + 1)]
         return [(edges[i], edges[i + 1]) for i in range(self.buckets) if edges[i + 1] > edges[i]]
 
+    @property
+    def _bucket_major(self) -> bool:
+        return self.reduce == "allreduce" and self.plan.world > 1
+
+    def _acc_range(self, lo, hi, rank):
+        """Accumulator rows of ``rank``'s local slices ``[lo, hi)``."""
+        if self._bucket_major:
+            # bucket [lo, hi) of all ranks starts at world*lo; rank r's part follows r blocks of hi-lo
+            a0 = self.plan.world * lo + rank * (hi - lo)
+            return a0, a0 + (hi - lo)
+        local = 0 if self.reduce == "none" else rank * self.plan.per_rank
+        return local + lo, local + hi
+
     def _allreduce_bucket(self, lo, hi):
-        # bucket j of every rank, in rank order: the same calls on all ranks
-        for r in range(self.plan.world):
-            s0 = r * self.plan.per_rank
-            dist.all_reduce(self.dk_acc[s0 + lo: s0 + hi], group=self.group)
-            dist.all_reduce(self.dv_acc[s0 + lo: s0 + hi], group=self.group)
+        # bucket j of every rank is one contiguous block: the same calls on all ranks
+        w = self.plan.world
+        dist.all_reduce(self.stage_k[w * lo: w * hi], group=self.group)
+        dist.all_reduce(self.stage_v[w * lo: w * hi], group=self.group)
+
+    def _slice_order(self, stage):
+        out = torch.empty_like(stage)
+        per = self.plan.per_rank
+        for lo, hi in self._bucket_ranges():
+            for r in range(self.plan.world):
+                a0, a1 = self._acc_range(lo, hi, r)
+                out[r * per + lo: r * per + hi].copy_(stage[a0:a1])
+        return out
 
     def _allgather(self):
         b0, b1 = self.plan.begin, self.plan.end
@@ -144,20 +177,22 @@ class ShardedTopKAttention:
         if fwd_timer is not None:
             fwd_timer[1].record()
         exchange = plan.world > 1 and self.reduce != "none"
-        local = 0 if self.reduce == "none" else b0
-        accumulate = self.reduce == "allreduce" and plan.world > 1
-        if accumulate:
-            self.dk_acc.zero_()
-            self.dv_acc.zero_()
+        if self._bucket_major:
+            # the other ranks' parts of each staging block must be zero for the sum
+            self.stage_k.zero_()
+            self.stage_v.zero_()
         main = torch.cuda.current_stream(self.device) if self.comm_stream is not None else None
         dq = torch.empty_like(q_rows)
         idx3 = idx.view(plan.per_rank, -1, self.topk)
         lse2 = lse.view(plan.per_rank, -1)
         pending = []
         for lo, hi in self._bucket_ranges():
+            a0, a1 = self._acc_range(lo, hi, plan.rank)
             kern.backward(q_rows[lo:hi], k_loc[lo:hi], v_loc[lo:hi], dout_rows[lo:hi], idx3[lo:hi], lse2[lo:hi],
-                          self.scale, self.dk_acc[local + lo: local + hi], self.dv_acc[local + lo: local + hi],
-                          accumulate, dq[lo:hi])
+                          self.scale, self.dk_acc[a0:a1], self.dv_acc[a0:a1], False, dq[lo:hi])
+            if self._bucket_major:
+                kern.finalize(self.dk_acc[a0:a1], self.dtype, out=self.stage_k[a0:a1])
+                kern.finalize(self.dv_acc[a0:a1], self.dtype, out=self.stage_v[a0:a1])
             if exchange and self.reduce == "allreduce":
                 if self.comm_stream is not None:
                     ev = torch.cuda.Event()
@@ -177,6 +212,8 @@ class ShardedTopKAttention:
             main.wait_stream(self.comm_stream)
         elif exchange and self.reduce == "allgather":
             self._allgather()
+        if self._bucket_major:
+            return out, dq, self._slice_order(self.stage_k), self._slice_order(self.stage_v)
         dk = kern.finalize(self.dk_acc, self.dtype)
         dv = kern.finalize(self.dv_acc, self.dtype)
         return out, dq, dk, dv
