@@ -17,7 +17,7 @@ import torch
 
 import _sharded_workers as W
 import oracle
-from sparsedict_b200.sharded import ShardPlan
+from sparsedict_b200.sharded import ShardedTopKAttention, ShardPlan
 
 
 def _free_port():
@@ -80,3 +80,27 @@ def test_failed_rank_makes_peer_collective_fail_not_hang():
     assert res[1][0] == "error" and "injected" in res[1][2]
     assert res[0][0] == "error", "the surviving rank should see its collective fail"
     assert elapsed < 55
+
+
+@pytest.mark.parametrize("slices,world,buckets", [(16, 2, 4), (40, 8, 2), (15, 3, 2), (128, 8, 4), (7, 7, 3)])
+def test_bucket_major_layout_is_a_bijection(slices, world, buckets):
+    # every (rank, local slice) maps to its own accumulator row, bucket j of all
+    # ranks is one contiguous block, and each rank's part of it is contiguous
+    class _Kernels:
+        def acc_dtype(self, dtype):
+            return torch.float32
+
+    seen = {}
+    for rank in range(world):
+        runner = ShardedTopKAttention(ShardPlan(slices, world, rank), 4, 2, 2, 1, torch.float32, "cpu",
+                                      reduce="allreduce", buckets=buckets, kernels=_Kernels())
+        assert runner._bucket_major == (world > 1)
+        for lo, hi in runner._bucket_ranges():
+            a0, a1 = runner._acc_range(lo, hi, rank)
+            assert a1 - a0 == hi - lo
+            if world > 1:
+                assert world * lo <= a0 and a1 <= world * hi
+            for i, row in enumerate(range(a0, a1)):
+                assert row not in seen
+                seen[row] = (rank, lo + i)
+    assert sorted(seen) == list(range(slices))
