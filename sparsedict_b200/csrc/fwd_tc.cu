@@ -786,7 +786,7 @@ __global__ void __launch_bounds__(NT, 1)
           // The next chunk's TMEM load may still be writing its registers:
           // complete it before calling out of line.
           tmem_wait_load();
-          if (!dead && cnt > a.topk + 32) {
+          if (!dead && cnt > a.topk + 16) {
             Compacted r = compact_bucket(list, R, cnt, tau, a.topk, 2);
             if (r.cnt > CAP - 32) r = compact_bucket_exact(list, R, r.cnt, r.tau, a.topk);
             cnt = r.cnt;
