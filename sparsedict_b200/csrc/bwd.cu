@@ -12,9 +12,8 @@
 //   dk_j += scale * dS_ij q_i,  dv_j += P_ij dout_i    (scatter into the
 //                                                       accumulators with
 //                                                       vector reductions)
-// The per-row recomputation reads the k selected key/value rows once each
-// (lane j holds slot j), the dq contraction re-reads the key rows coalesced
-// across features.
+// The generic kernel below serves every dtype and width; bf16/fp16 rows of
+// 64 features take the grouped fast path further down.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -146,19 +145,27 @@ __global__ void __launch_bounds__(NT) sparse_bwd(BwdArgs<typename AccOf<T>::type
 
 // ------------------------------------------------ d = dv = 64 fast path ---
 // bf16/fp16 rows of 64 features (128 bytes), k <= 64.  A warp owns one query
-// row; lane L owns slots L and L+32:
-//   pass 1  each lane reads its slots' key and value rows with 16-byte loads
-//           and forms s, P = exp(s - lse) and G = dout·v against q and dout
-//           broadcast from shared memory;
-//   dq      each lane keeps its key rows in registers and adds dS·k into a
-//           64-wide partial; the 32 partials are summed through a padded
-//           shared-memory transpose (lane L finishes features 2L, 2L+1);
-//   scatter lanes span the 64 features of one key row (two per lane) so each
-//           warp-wide vector reduction covers a whole 256-byte fp32 row.
-constexpr int F64W = 4;  // warps per block
+// row.  Its lanes form four groups of eight: group g takes slots g, g+4, g+8,
+// ... and lane l of a group features 8l..8l+7, so each key or value row is one
+// coalesced 128-byte access by eight lanes (four rows per load instruction).
+//   pass 1  per slot: q·k and dout·v as 8-feature partials, summed over the
+//           group by three butterfly steps (every lane of the group holds the
+//           same sums); P = exp(s·scale - lse); P, G and the key go to shared
+//           memory; delta = sum of P·G over the row;
+//   pass 2  per slot: dS = P (G - delta); the key row is read again (an L1/L2
+//           hit) for dq += dS·k; dK[key] += scale·dS·q and dV[key] += P·dout
+//           are two 16-byte vector reductions per lane each, lane l taking
+//           features 4l..4l+3 and 32+4l..32+4l+3 so that each reduction
+//           instruction covers four rows' 128-byte halves.  (Whole-warp
+//           8-byte reductions of one 256-byte row per instruction touch half
+//           the L2 sectors but measured 7 % slower: twice the instructions.)
+//   dq      the four groups' partials are summed by two butterfly steps and
+//           group 0 writes the row once (no atomics).
+constexpr int G8W = 8;  // warps per block
 
-__device__ __forceinline__ void red_add2(float* p, float a, float b) {
-  asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(p), "f"(a), "f"(b) : "memory");
+__device__ __forceinline__ void red_add4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
 }
 
 template <typename T>
@@ -169,120 +176,121 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(F64W * kWarp) sparse_bwd_d64(BwdArgs<float> a) {
-  __shared__ __align__(16) float sq[F64W][64];
-  __shared__ __align__(16) float sdo[F64W][64];
-  __shared__ float part[F64W][kWarp][65];
-  __shared__ float swk[F64W][64], swv[F64W][64];
-  __shared__ int skey[F64W][64];
+__device__ __forceinline__ void unpack4(const uint2& u, float* f) {
+  const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int h = 0; h < 4; ++h) f[h] = to_acc(e[h]);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(G8W * kWarp, 4) sparse_bwd_d64(BwdArgs<float> a) {
+  __shared__ float sp[G8W][64], sg[G8W][64];
+  __shared__ int skey[G8W][64];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int grp = lane >> 3, l8 = lane & 7;
   const T* __restrict__ q = static_cast<const T*>(a.q);
   const T* __restrict__ dout = static_cast<const T*>(a.dout);
 
-  for (int64_t r = (int64_t)blockIdx.x * F64W + warp; r < a.rows; r += (int64_t)gridDim.x * F64W) {
+  for (int64_t r = (int64_t)blockIdx.x * G8W + warp; r < a.rows; r += (int64_t)gridDim.x * G8W) {
     const int64_t slice = slice_of_row(a.geo, r);
     const int64_t pr = a.row_index ? (int64_t)a.row_index[r] : r;
-    const T* __restrict__ kmat = static_cast<const T*>(a.k) + slice * a.m * 64;
-    const T* __restrict__ vmat = static_cast<const T*>(a.v) + slice * a.m * 64;
-    sq[warp][2 * lane] = to_acc(q[pr * 64 + 2 * lane]);
-    sq[warp][2 * lane + 1] = to_acc(q[pr * 64 + 2 * lane + 1]);
-    sdo[warp][2 * lane] = to_acc(dout[pr * 64 + 2 * lane]);
-    sdo[warp][2 * lane + 1] = to_acc(dout[pr * 64 + 2 * lane + 1]);
-    __syncwarp();
+    const uint4* __restrict__ kmat =
+        reinterpret_cast<const uint4*>(static_cast<const T*>(a.k) + slice * a.m * 64) + l8;
+    const uint4* __restrict__ vmat =
+        reinterpret_cast<const uint4*>(static_cast<const T*>(a.v) + slice * a.m * 64) + l8;
+    float qf[8], df[8];
+    unpack8<T>(__ldg(reinterpret_cast<const uint4*>(q + pr * 64) + l8), qf);
+    unpack8<T>(__ldg(reinterpret_cast<const uint4*>(dout + pr * 64) + l8), df);
     const float l = a.lse[r];
+    int i0 = -1, i1 = -1;  // slots lane and lane + 32
+    if (lane < a.topk) i0 = a.top_idx[r * a.topk + lane];
+    if (lane + 32 < a.topk) i1 = a.top_idx[r * a.topk + lane + 32];
+    if ((lane < a.topk && (i0 < 0 || i0 >= a.m)) || (lane + 32 < a.topk && (i1 < 0 || i1 >= a.m))) {
+      raise_device_status(a.status, kStatusIndexOutOfRange);
+      if (i0 >= a.m) i0 = -1;
+      if (i1 >= a.m) i1 = -1;
+    }
 
-    uint4 kr[2][8];
-    float p[2], g[2];
-    int key[2];
+    float part = 0.f;
+#pragma unroll 4
+    for (int it = 0; it < 16; ++it) {
+      const int j = 4 * it + grp;
+      const int key = __shfl_sync(0xffffffffu, it < 8 ? i0 : i1, j & 31);
+      float s = 0.f, g = 0.f;
+      if (key >= 0) {
+        float kf[8], vf[8];
+        unpack8<T>(__ldg(kmat + (int64_t)key * 8), kf);
+        unpack8<T>(__ldg(vmat + (int64_t)key * 8), vf);
 #pragma unroll
-    for (int sj = 0; sj < 2; ++sj) {
-      const int j = lane + 32 * sj;
-      p[sj] = 0.f;
-      g[sj] = 0.f;
-      key[sj] = -1;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) kr[sj][c] = make_uint4(0, 0, 0, 0);
-      if (j < a.topk) {
-        int kk = a.top_idx[r * a.topk + j];
-        if (kk < 0 || kk >= a.m) {
-          raise_device_status(a.status, kStatusIndexOutOfRange);
-        } else {
-          key[sj] = kk;
-          const uint4* krow = reinterpret_cast<const uint4*>(kmat + (int64_t)kk * 64);
-          const uint4* vrow = reinterpret_cast<const uint4*>(vmat + (int64_t)kk * 64);
-          uint4 vr[8];
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            kr[sj][c] = __ldg(krow + c);
-            vr[c] = __ldg(vrow + c);
-          }
-          float s = 0.f, gg = 0.f;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            float kf[8], vf[8];
-            unpack8<T>(kr[sj][c], kf);
-            unpack8<T>(vr[c], vf);
-            const float4 q0 = *reinterpret_cast<const float4*>(&sq[warp][8 * c]);
-            const float4 q1 = *reinterpret_cast<const float4*>(&sq[warp][8 * c + 4]);
-            const float4 d0 = *reinterpret_cast<const float4*>(&sdo[warp][8 * c]);
-            const float4 d1 = *reinterpret_cast<const float4*>(&sdo[warp][8 * c + 4]);
-            s = fmaf(q0.x, kf[0], s); s = fmaf(q0.y, kf[1], s); s = fmaf(q0.z, kf[2], s); s = fmaf(q0.w, kf[3], s);
-            s = fmaf(q1.x, kf[4], s); s = fmaf(q1.y, kf[5], s); s = fmaf(q1.z, kf[6], s); s = fmaf(q1.w, kf[7], s);
-            gg = fmaf(d0.x, vf[0], gg); gg = fmaf(d0.y, vf[1], gg); gg = fmaf(d0.z, vf[2], gg); gg = fmaf(d0.w, vf[3], gg);
-            gg = fmaf(d1.x, vf[4], gg); gg = fmaf(d1.y, vf[5], gg); gg = fmaf(d1.z, vf[6], gg); gg = fmaf(d1.w, vf[7], gg);
-          }
-          p[sj] = expf(s * a.scale - l);
-          g[sj] = gg;
+        for (int h = 0; h < 8; ++h) {
+          s = fmaf(qf[h], kf[h], s);
+          g = fmaf(df[h], vf[h], g);
         }
       }
-    }
-    float part_sum = p[0] * g[0] + p[1] * g[1];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) part_sum += __shfl_xor_sync(0xffffffffu, part_sum, o);
-    const float delta = part_sum;
-    const float ds0 = p[0] * (g[0] - delta), ds1 = p[1] * (g[1] - delta);
-
-    float dqp[64];
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      float k0[8], k1[8];
-      unpack8<T>(kr[0][c], k0);
-      unpack8<T>(kr[1][c], k1);
-#pragma unroll
-      for (int h = 0; h < 8; ++h) dqp[8 * c + h] = fmaf(ds0, k0[h], ds1 * k1[h]);
-    }
-#pragma unroll
-    for (int f = 0; f < 64; ++f) part[warp][lane][f] = dqp[f];
-#pragma unroll
-    for (int sj = 0; sj < 2; ++sj) {
-      const int j = lane + 32 * sj;
-      if (j < 64) {
-        skey[warp][j] = key[sj];
-        swk[warp][j] = (sj ? ds1 : ds0) * a.scale;
-        swv[warp][j] = p[sj];
+      for (int o = 1; o < 8; o <<= 1) {
+        s += __shfl_xor_sync(0xffffffffu, s, o);
+        g += __shfl_xor_sync(0xffffffffu, g, o);
       }
+      const float p = key >= 0 ? expf(s * a.scale - l) : 0.f;
+      if (l8 == 0) {
+        sp[warp][j] = p;
+        sg[warp][j] = g;
+        skey[warp][j] = key;
+      }
+      part = fmaf(p, g, part);
     }
+    part += __shfl_xor_sync(0xffffffffu, part, 8);
+    part += __shfl_xor_sync(0xffffffffu, part, 16);
+    const float delta = part;
     __syncwarp();
-    float acc0 = 0.f, acc1 = 0.f;
-#pragma unroll 8
-    for (int i = 0; i < kWarp; ++i) {
-      acc0 += part[warp][i][2 * lane];
-      acc1 += part[warp][i][2 * lane + 1];
-    }
-    T* dqr = static_cast<T*>(a.dq) + pr * 64;
-    dqr[2 * lane] = cvt_out<T>(acc0 * a.scale);
-    dqr[2 * lane + 1] = cvt_out<T>(acc1 * a.scale);
 
-    const float q0 = sq[warp][2 * lane], q1 = sq[warp][2 * lane + 1];
-    const float o0 = sdo[warp][2 * lane], o1 = sdo[warp][2 * lane + 1];
-    float* dkm = a.dk_acc + slice * a.m * 64;
-    float* dvm = a.dv_acc + slice * a.m * 64;
-    for (int j = 0; j < a.topk; ++j) {
-      const int kk = skey[warp][j];
-      if (kk < 0) continue;
-      const float wk = swk[warp][j], wv = swv[warp][j];
-      red_add2(dkm + (int64_t)kk * 64 + 2 * lane, wk * q0, wk * q1);
-      red_add2(dvm + (int64_t)kk * 64 + 2 * lane, wv * o0, wv * o1);
+    // q and dout again, features 4·l8..4·l8+3 and 32+4·l8..32+4·l8+3 (the
+    // reduction layout)
+    float qb[8], db[8];
+    {
+      const uint2* q2 = reinterpret_cast<const uint2*>(q + pr * 64);
+      const uint2* d2 = reinterpret_cast<const uint2*>(dout + pr * 64);
+      unpack4<T>(__ldg(q2 + l8), qb);
+      unpack4<T>(__ldg(q2 + 8 + l8), qb + 4);
+      unpack4<T>(__ldg(d2 + l8), db);
+      unpack4<T>(__ldg(d2 + 8 + l8), db + 4);
+    }
+    float dq[8];
+#pragma unroll
+    for (int h = 0; h < 8; ++h) dq[h] = 0.f;
+    float* dkm = a.dk_acc + slice * a.m * 64 + 4 * l8;
+    float* dvm = a.dv_acc + slice * a.m * 64 + 4 * l8;
+#pragma unroll 4
+    for (int it = 0; it < 16; ++it) {
+      const int j = 4 * it + grp;
+      const int key = skey[warp][j];
+      if (key < 0) continue;
+      const float p = sp[warp][j];
+      const float ds = p * (sg[warp][j] - delta);
+      float kf[8];
+      unpack8<T>(__ldg(kmat + (int64_t)key * 8), kf);
+#pragma unroll
+      for (int h = 0; h < 8; ++h) dq[h] = fmaf(ds, kf[h], dq[h]);
+      const float wk = ds * a.scale;
+      float* dk = dkm + (int64_t)key * 64;
+      float* dv = dvm + (int64_t)key * 64;
+      red_add4(dk, wk * qb[0], wk * qb[1], wk * qb[2], wk * qb[3]);
+      red_add4(dk + 32, wk * qb[4], wk * qb[5], wk * qb[6], wk * qb[7]);
+      red_add4(dv, p * db[0], p * db[1], p * db[2], p * db[3]);
+      red_add4(dv + 32, p * db[4], p * db[5], p * db[6], p * db[7]);
+    }
+#pragma unroll
+    for (int h = 0; h < 8; ++h) {
+      dq[h] += __shfl_xor_sync(0xffffffffu, dq[h], 8);
+      dq[h] += __shfl_xor_sync(0xffffffffu, dq[h], 16);
+    }
+    if (grp == 0) {
+      uint4 o;
+      T* e = reinterpret_cast<T*>(&o);
+#pragma unroll
+      for (int h = 0; h < 8; ++h) e[h] = cvt_out<T>(dq[h] * a.scale);
+      reinterpret_cast<uint4*>(static_cast<T*>(a.dq) + pr * 64)[l8] = o;
     }
     __syncwarp();
   }
@@ -312,18 +320,17 @@ int launch_d64(const BwdLaunch& L) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t want = (a.rows + F64W - 1) / F64W;
-  const int64_t cap = (int64_t)sms * 8;
-  sparse_bwd_d64<T><<<(unsigned)(want < cap ? want : cap), F64W * kWarp, 0, L.stream>>>(a);
+  const int64_t want = (a.rows + G8W - 1) / G8W;
+  const int64_t cap = (int64_t)sms * 4;
+  sparse_bwd_d64<T><<<(unsigned)(want < cap ? want : cap), G8W * kWarp, 0, L.stream>>>(a);
   return cudaPeekAtLastError() == cudaSuccess ? SDK_OK : SDK_ERR_CUDA;
 }
-
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 bool d64_supported(const BwdLaunch& L) {
   return (L.dtype == SDK_DTYPE_BF16 || L.dtype == SDK_DTYPE_F16) && L.d == 64 && L.dv == 64 && L.topk <= 64 &&
-         L.score_grid == 0 && !L.seg_bias && !L.dseg_bias && aligned16(L.k) && aligned16(L.v) &&
-         aligned16(L.dk_acc) && aligned16(L.dv_acc);
+         L.score_grid == 0 && !L.seg_bias && !L.dseg_bias && aligned16(L.q) && aligned16(L.k) &&
+         aligned16(L.v) && aligned16(L.dout) && aligned16(L.dq) && aligned16(L.dk_acc) && aligned16(L.dv_acc);
 }
 
 template <typename T>
