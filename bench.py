@@ -318,16 +318,17 @@ def run_native_arm(args):
                    **c, "parallelism": f"rows{world}", "reduce": args.reduce,
                    "l2": "inputs larger than L2 (268 MB per tensor)"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tc, "unit": "TFLOP/s",
-                     "frac": achieved / peak_tc, "traffic": traffic, "kernel": "fused forward",
+                     "frac": achieved / peak_tc, "traffic": traffic, "kernel": "forward (stream + finish kernels)",
                      "fwd_ms": fwd_ms, "peak_source": f"{peaks['source']} bf16_tflops_sustained",
                      "step_frac_combined": t_roof / (ms_per_step / 1000.0),
                      # each whole-step term on its own: affinity flops at the tensor peak,
                      # compulsory fwd+bwd bytes at the HBM peak
                      "step_frac_tensor": t_tensor / (ms_per_step / 1000.0),
                      "step_frac_hbm": t_hbm / (ms_per_step / 1000.0)},
-        # this library's kernels per step: forward, one backward per bucket, and two
-        # conversions per bucket (bucket-major all-reduce) or two in all
-        "gpu_launches": (1 + len(runner._bucket_ranges()) * (3 if runner._bucket_major else 1)
+        # this library's kernels per step: the forward (stream + finish kernels), one
+        # backward per bucket, and two conversions per bucket (bucket-major all-reduce)
+        # or two in all
+        "gpu_launches": (2 + len(runner._bucket_ranges()) * (3 if runner._bucket_major else 1)
                          + (0 if runner._bucket_major else 2)) * args.steps,
     }
     if e2e is not None:

@@ -28,25 +28,35 @@
 // share the cut bucket, which needs heavily tied scores) is marked and
 // re-selected exactly at the end, see below.
 //
-// After the last tile the survivors of each row (at most 96) are re-scored
-// exactly: the row's Q values go to registers, the candidates' key indices
-// move to the row's own unused list slots, and each candidate's fp32 score
-// is recomputed from the gathered key row by one fixed FMA order, replacing
-// its bucketed entry.  The exact cut to k keys uses order-preserving 64-bit
-// keys (score, complemented index), so ties keep the lower key index.  Then
-// the row LSE, the k indices (in no particular order; the set is the
-// reference's top-k set) and the softmax-weighted sum of the gathered value
-// rows are written.
+// After the last tile each selection thread writes its row's list (at most
+// 176 entries, four per 16-byte store) and count to a candidate buffer in
+// HBM, and the CTA ends: the SM is free for the next CTA's stream while the
+// exact work runs elsewhere.  A second kernel, one warp per query row at high
+// occupancy, finishes every row:
+//
+//   bucket cut   the k-th largest bucket of the row's entries, by 8-bit radix
+//                digits over a shared histogram (from the highest bit in
+//                which the row's buckets differ); entries of lower buckets
+//                cannot be in the top k and are dropped;
+//   re-score     each survivor's fp32 score is recomputed from the gathered
+//                key row (eight lanes per 128-byte row, one fixed summation
+//                order);
+//   exact cut    the k best by order-preserving keys (score, then lower key
+//                index on ties), by the same radix select;
+//   epilogue     row LSE, the k indices (in list order; the set is the
+//                reference's top-k set) and the softmax-weighted sum of the
+//                gathered value rows.
 //
 // Marked rows are re-selected by their warp: lanes score 32 keys at a time
-// with the same FMA order and keep an exact candidate list sorted by a warp
-// bitonic network, as the CUDA-core kernel does.
+// with the same summation order and keep an exact candidate list sorted by a
+// warp bitonic network, as the CUDA-core kernel does.
 //
 // Selection runs on the raw dot products; scale = 1/(T·sqrt(d)) > 0 is
 // applied in the epilogue (for d = 64 and T a power of two the scale is a
 // power of two, so the order is exactly that of the scaled scores).
 #include <cuda.h>
 
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -64,11 +74,9 @@ constexpr int RS = TQ * NTILE;  // rows per CTA; row stride of the slot-major li
 constexpr int TK = 128;         // keys per score tile (MMA N)
 constexpr int D = 64;           // feature width (one 128-byte swizzle row)
 constexpr int KSTAGES = 1;
-constexpr int CAP = 176;        // list slots per row
-constexpr int FINAL_CAP = 96;   // most candidates a row may carry into exact re-scoring
+constexpr int CAP = 176;        // list slots per row (and candidate buffer entries per row)
 constexpr int FIX_CAP = 128;    // exact list of a row re-selected by one warp
 constexpr int NT = 384;
-constexpr int NSEL = 8 * kWarp;  // selection threads
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t TILE_BYTES = TK * D * 2;  // a K tile, also a Q tile
 
@@ -79,27 +87,19 @@ constexpr int OFF_BAR = OFF_LIST + CAP * RS * 4;
 constexpr int NBARS = 1 + 2 * KSTAGES + 4 * NTILE;
 constexpr int OFF_MISC = OFF_BAR + NBARS * 8;
 constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
-// After the stream: the key indices of a row's re-scored candidates go to
-// the row's own list column above FINAL_CAP (two 16-bit indices per word),
-// and the Q/K region holds one exact re-selection buffer per selection warp.
-constexpr int OFF_FIX = 0;
-constexpr int FIX_BYTES = FIX_CAP * 8 + 16;
-static_assert(OFF_FIX + 8 * FIX_BYTES <= OFF_LIST, "post-stream buffers exceed the Q/K region");
-static_assert(FINAL_CAP + (FINAL_CAP + 1) / 2 <= CAP, "re-scoring indices exceed the list column");
+static_assert(CAP % 4 == 0, "lists are written four entries per store");
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 static_assert(OFF_BAR % 8 == 0, "mbarrier alignment");
 
+// Count word of a row in the candidate buffer: the number of entries, or
+constexpr int32_t kCandDead = -1;     // list could not be shrunk: re-select exactly
+constexpr int32_t kCandAborted = -2;  // a pipeline wait timed out: nothing to finish
+
 struct TcArgs {
-  const void* q;
-  const void* k;
-  const void* v;
-  void* out;
-  int32_t* top_idx;
-  float* lse;
-  float* top_scores;
+  uint32_t* cand;   // [rows][CAP] list entries of each query row
+  int32_t* cand_n;  // [rows] entry count, kCandDead or kCandAborted
   int64_t n, m;
   int tiles_per_slice, topk;
-  float scale;
   unsigned int* status;
 };
 
@@ -131,23 +131,6 @@ __device__ __forceinline__ void sort16_desc(uint32_t (&x)[16]) {
         if (j > i) {
           const bool desc = (i & size) == 0;
           const uint32_t hi = max(x[i], x[j]), lo = min(x[i], x[j]);
-          x[i] = desc ? hi : lo;
-          x[j] = desc ? lo : hi;
-        }
-      }
-}
-
-__device__ __forceinline__ void sort16_desc(float (&x)[16]) {
-#pragma unroll
-  for (int size = 2; size <= 16; size <<= 1)
-#pragma unroll
-    for (int st = size >> 1; st > 0; st >>= 1)
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int j = i ^ st;
-        if (j > i) {
-          const bool desc = (i & size) == 0;
-          const float hi = fmaxf(x[i], x[j]), lo = fminf(x[i], x[j]);
           x[i] = desc ? hi : lo;
           x[j] = desc ? lo : hi;
         }
@@ -331,51 +314,48 @@ __device__ __forceinline__ void unpack8(const uint4& u, float* f) {
   for (int h = 0; h < 8; ++h) f[h] = to_acc(e[h]);
 }
 
-// Exact fp32 score of the re-scoring stage: four FMA chains (feature f feeds
-// chain f mod 4) summed pairwise.
-__device__ __forceinline__ float dot64_regs(const float (&q)[D], const uint4 (&u)[8], bool bf16) {
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    float f[8];
-    if (bf16)
-      unpack8<__nv_bfloat16>(u[c], f);
-    else
-      unpack8<__half>(u[c], f);
-#pragma unroll
-    for (int h = 0; h < 8; ++h) acc[h & 3] = fmaf(q[c * 8 + h], f[h], acc[h & 3]);
-  }
-  return (acc[0] + acc[1]) + (acc[2] + acc[3]);
-}
-
-template <typename T>
-__device__ __forceinline__ void load_row(const T* row, uint4 (&u)[8]) {
-  const uint4* p = reinterpret_cast<const uint4*>(row);
-#pragma unroll
-  for (int c = 0; c < 8; ++c) u[c] = __ldg(p + c);
-}
-
-// Warp re-selection works on one query row with the whole warp: lane
+// Exact-score stages work on one query row with the whole warp: lane
 // 8*grp + g handles features 8g..8g+7 (16 bytes) of key grp of a group of
 // four, so one 16-byte load instruction reads four whole 128-byte key or
 // value rows.
+//
+// dot8: one fp32 FMA chain over 8 features in order, both operands 16-bit.
+// The mixed-precision FMA widens them exactly and the product of two 16-bit
+// floats is exact in fp32, so each step equals fmaf of the widened values.
 template <typename T>
-__device__ __forceinline__ void load_chunk8(const T* p, float (&f)[8]) {
-  unpack8<T>(__ldg(reinterpret_cast<const uint4*>(p)), f);
+__device__ __forceinline__ float dot8(const uint4& a, const uint4& b) {
+  float acc = 0.f;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    asm("{\n .reg .b16 a0, a1, a2, a3, a4, a5, a6, a7, b0, b1, b2, b3, b4, b5, b6, b7;\n"
+        " mov.b32 {a0, a1}, %1;\n mov.b32 {a2, a3}, %2;\n mov.b32 {a4, a5}, %3;\n mov.b32 {a6, a7}, %4;\n"
+        " mov.b32 {b0, b1}, %5;\n mov.b32 {b2, b3}, %6;\n mov.b32 {b4, b5}, %7;\n mov.b32 {b6, b7}, %8;\n"
+        " fma.rn.f32.bf16 %0, a0, b0, %0;\n fma.rn.f32.bf16 %0, a1, b1, %0;\n"
+        " fma.rn.f32.bf16 %0, a2, b2, %0;\n fma.rn.f32.bf16 %0, a3, b3, %0;\n"
+        " fma.rn.f32.bf16 %0, a4, b4, %0;\n fma.rn.f32.bf16 %0, a5, b5, %0;\n"
+        " fma.rn.f32.bf16 %0, a6, b6, %0;\n fma.rn.f32.bf16 %0, a7, b7, %0;\n}"
+        : "+f"(acc)
+        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w));
+  } else {
+    asm("{\n .reg .b16 a0, a1, a2, a3, a4, a5, a6, a7, b0, b1, b2, b3, b4, b5, b6, b7;\n"
+        " mov.b32 {a0, a1}, %1;\n mov.b32 {a2, a3}, %2;\n mov.b32 {a4, a5}, %3;\n mov.b32 {a6, a7}, %4;\n"
+        " mov.b32 {b0, b1}, %5;\n mov.b32 {b2, b3}, %6;\n mov.b32 {b4, b5}, %7;\n mov.b32 {b6, b7}, %8;\n"
+        " fma.rn.f32.f16 %0, a0, b0, %0;\n fma.rn.f32.f16 %0, a1, b1, %0;\n"
+        " fma.rn.f32.f16 %0, a2, b2, %0;\n fma.rn.f32.f16 %0, a3, b3, %0;\n"
+        " fma.rn.f32.f16 %0, a4, b4, %0;\n fma.rn.f32.f16 %0, a5, b5, %0;\n"
+        " fma.rn.f32.f16 %0, a6, b6, %0;\n fma.rn.f32.f16 %0, a7, b7, %0;\n}"
+        : "+f"(acc)
+        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w));
+  }
+  return acc;
 }
 
-// Exact fp32 score of the warp re-selection: each lane runs one FMA chain
-// over its 8 features in order, then the 8 lanes of a group add their
-// partial sums by xor-shuffles over 1, 2 and 4, so all 8 lanes hold the same
-// sum.  (A row's scores all come from one of the two exact stages, so each
-// row ranks its keys by one rounding of the dot product.)
+// Exact fp32 score: dot8 over the lane's 8 features, then the 8 lanes of a
+// group add their partial sums by xor-shuffles over 1, 2 and 4, so all 8
+// lanes hold the same sum.  Every exact score (finish kernel and warp
+// re-selection) is this one rounding of the dot product.
 template <typename T>
-__device__ __forceinline__ float group_dot(const float (&qg)[8], const uint4& kc) {
-  float f[8];
-  unpack8<T>(kc, f);
-  float acc = 0.f;
-#pragma unroll
-  for (int h = 0; h < 8; ++h) acc = fmaf(qg[h], f[h], acc);
+__device__ __forceinline__ float group_dot(const uint4& qg, const uint4& kc) {
+  float acc = dot8<T>(qg, kc);
   acc += __shfl_xor_sync(0xffffffffu, acc, 1);
   acc += __shfl_xor_sync(0xffffffffu, acc, 2);
   acc += __shfl_xor_sync(0xffffffffu, acc, 4);
@@ -433,80 +413,6 @@ __device__ __forceinline__ void write_row(const T* vbase, ScoreOf score_of, Inde
   }
 }
 
-// Key index of re-scored candidate s of a row: `srow` points at the row's
-// list column at slot FINAL_CAP; candidate s sits in slot FINAL_CAP + s/2,
-// half s%2 of the word.
-__device__ __forceinline__ uint32_t stage_byte(int s) { return (uint32_t)((s >> 1) * (4 * RS) + 2 * (s & 1)); }
-__device__ __forceinline__ uint16_t& stage_at(uint16_t* srow, int s) {
-  return *reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(srow) + stage_byte(s));
-}
-
-// Exact cut on re-scored candidates (fp32 scores in cv, key indices in ci,
-// both slot-major with stride RS).  Raise a pivot as compact_bucket does,
-// with exact scores: keep the keys scoring at least the highest of 16
-// sampled scores that >= topk candidates meet.
-__device__ __noinline__ int compact_exact(float* cv, uint16_t* srow, int R, int cnt, int topk) {
-  float smp[16];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const float x = cv[((j * cnt) >> 4) * RS + R];
-    smp[j] = (x != x) ? __int_as_float(0x7f800000) : x;
-  }
-  sort16_desc(smp);
-  int t = (16 * topk) / (cnt > 0 ? cnt : 1);
-  t = t > 12 ? 12 : t;
-  float pivot = __int_as_float(0xff800000);
-  bool found = false;
-  for (int pass = 0; pass < 4 && !found; ++pass) {
-    float p[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) p[q] = pick16(smp, t + q);
-    int c[4] = {0, 0, 0, 0};
-#pragma unroll 4
-    for (int s = 0; s < cnt; ++s) {
-      const float x = cv[s * RS + R];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) c[q] += !(x < p[q]);
-    }
-#pragma unroll
-    for (int q = 3; q >= 0; --q)
-      if (c[q] >= topk) {
-        pivot = p[q];
-        found = true;
-      }
-    t = t + 4 > 12 ? 12 : t + 4;
-  }
-  if (!found) return cnt;
-  uint32_t w = 0;
-  const uint32_t cvb = smem_addr(cv) + 4u * R, cib = smem_addr(srow);
-  int s = 0;
-  for (; s + 8 <= cnt; s += 8) {  // loads ahead of stores, as in keep_pass
-    float x[8];
-    uint32_t i[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      x[j] = cv[(s + j) * RS + R];
-      i[j] = stage_at(srow, s + j);
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint32_t keep = (uint32_t)!(x[j] < pivot);
-      st_shared_f32_if(cvb + w * (4u * RS), x[j], keep);
-      st_shared_u16_if(cib + stage_byte((int)w), i[j], keep);
-      w += keep;
-    }
-  }
-  for (; s < cnt; ++s) {
-    const float x = cv[s * RS + R];
-    const uint32_t i = stage_at(srow, s);
-    const uint32_t keep = (uint32_t)!(x < pivot);
-    st_shared_f32_if(cvb + w * (4u * RS), x, keep);
-    st_shared_u16_if(cib + stage_byte((int)w), i, keep);
-    w += keep;
-  }
-  return (int)w;
-}
-
 // Order-preserving 64-bit rank key: larger key = ranks higher.  The high
 // word maps the float onto an unsigned order (NaN highest, -0 == +0); the
 // low word is the complemented key index, so equal scores rank the lower
@@ -520,39 +426,6 @@ __device__ __forceinline__ uint64_t rank_key(float x, uint32_t idx) {
     u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
   }
   return ((uint64_t)u << 32) | (uint64_t)(0xffffffffu - idx);
-}
-
-// Remove lowest-ranked keys until exactly `topk` remain.
-__device__ __noinline__ int trim_exact(float* cv, uint16_t* srow, int R, int cnt, int topk) {
-  while (cnt > topk) {
-    uint64_t worst = ~0ull;
-    int pos = 0;
-#pragma unroll 4
-    for (int s = 0; s < cnt; ++s) {
-      const uint64_t key = rank_key(cv[s * RS + R], stage_at(srow, s));
-      const bool lower = key < worst;
-      worst = lower ? key : worst;
-      pos = lower ? s : pos;
-    }
-    const int last = cnt - 1;
-    cv[pos * RS + R] = cv[last * RS + R];
-    stage_at(srow, pos) = stage_at(srow, last);
-    cnt = last;
-  }
-  return cnt;
-}
-
-template <typename T>
-__device__ __forceinline__ void store_out_row(const float (&acc)[D], T* orow_t) {
-  uint4* orow = reinterpret_cast<uint4*>(orow_t);
-#pragma unroll
-  for (int q4 = 0; q4 < D / 8; ++q4) {
-    uint4 u;
-    T* e = reinterpret_cast<T*>(&u);
-#pragma unroll
-    for (int h = 0; h < 8; ++h) e[h] = from_acc<T>(acc[q4 * 8 + h]);
-    orow[q4] = u;
-  }
 }
 
 // Exact re-selection of one row by a whole warp (rows whose bucketed list
@@ -574,8 +447,7 @@ template <typename T>
 __device__ __noinline__ void reselect_row(RowOut a, int64_t m, int topk, float scale, int64_t slice, int64_t gr,
                                           float* fv, int* fi, float* ftau, int lane) {
   const int g = lane & 7, grp = lane >> 3;
-  float qg[8];
-  load_chunk8<T>(static_cast<const T*>(a.q) + gr * D + 8 * g, qg);
+  const uint4 qg = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(a.q) + gr * D) + g);
   const T* kbase = static_cast<const T*>(a.k) + slice * m * D;
   if (lane == 0) *ftau = __int_as_float(0x7fc00000);
   __syncwarp();
@@ -815,102 +687,20 @@ __global__ void __launch_bounds__(NT, 1)
         if (!last) tmem_wait_load(va);
       }
     }
-    // Shrink to the candidates that go to exact re-scoring.
-    if (ok && !dead) {
-      while (cnt > a.topk + 16) {
-        const Compacted r = compact_bucket(list, R, cnt, tau, a.topk, 1);
-        cnt = r.cnt;
-        tau = r.tau;
-        if (!r.shrank) break;
-      }
-      if (cnt > a.topk + 16) {
-        const Compacted r = compact_bucket_exact(list, R, cnt, tau, a.topk);
-        cnt = r.cnt;
-        tau = r.tau;
-      }
-      dead = cnt > FINAL_CAP;
-    }
-    float q[D];
-    if (ok) {
-      const uint8_t* qrow = qs + wg * TILE_BYTES + rl * 128;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint4 u = *reinterpret_cast<const uint4*>(qrow + ((c ^ (rl & 7)) << 4));
-        unpack8<T>(u, &q[c * 8]);
-      }
-    }
-    // Every MMA has completed (each selection warp saw its last tile) and no
-    // copy is in flight: the Q/K buffers are free after this barrier.
-    __syncwarp();
-    named_bar_sync(1, NSEL);
-    const bool live = __all_sync(0xffffffffu, ok && !*abort_flag);
-    if (live) {
-      uint16_t* srow = reinterpret_cast<uint16_t*>(list + FINAL_CAP * RS + R);
-      float* lf = reinterpret_cast<float*>(list);
-      const T* kbase = static_cast<const T*>(a.k) + slice * a.m * D;
+    // Hand the row to the finish kernel: its entry count (or kCandDead) and
+    // the entries, four per 16-byte store (slots past the count are unused).
+    if (rl < rows) {
       const int64_t gr = row0 + (int64_t)wg * TQ + rl;
-      if (!dead) {
-        int s = 0;
-        for (; s + 1 < cnt; s += 2) {
-          const uint32_t e0 = list[s * RS + R], e1 = list[(s + 1) * RS + R];
-          uint4 u0[8], u1[8];
-          load_row(kbase + (int64_t)(e0 & 0xffffu) * D, u0);
-          load_row(kbase + (int64_t)(e1 & 0xffffu) * D, u1);
-          stage_at(srow, s) = (uint16_t)(e0 & 0xffffu);
-          stage_at(srow, s + 1) = (uint16_t)(e1 & 0xffffu);
-          lf[s * RS + R] = dot64_regs(q, u0, kBf16);
-          lf[(s + 1) * RS + R] = dot64_regs(q, u1, kBf16);
-        }
-        if (s < cnt) {
-          const uint32_t e0 = list[s * RS + R];
-          uint4 u0[8];
-          load_row(kbase + (int64_t)(e0 & 0xffffu) * D, u0);
-          stage_at(srow, s) = (uint16_t)(e0 & 0xffffu);
-          lf[s * RS + R] = dot64_regs(q, u0, kBf16);
-        }
-        if (cnt > a.topk + 4) cnt = compact_exact(lf, srow, R, cnt, a.topk);
-        cnt = trim_exact(lf, srow, R, cnt, a.topk);
-        if (rl < rows) {
-          float mx = lf[R];
-          for (int j = 1; j < a.topk; ++j) mx = fmaxf(mx, lf[j * RS + R]);
-          const float mxs = mx * a.scale;
-          float total = 0.f;
-          for (int j = 0; j < a.topk; ++j) total += expf(lf[j * RS + R] * a.scale - mxs);
-          const float lse = mxs + logf(total);
-          a.lse[gr] = lse;
-          int32_t* idx_row = a.top_idx + gr * a.topk;
-          for (int j = 0; j < a.topk; ++j) {
-            idx_row[j] = stage_at(srow, j);
-            if (a.top_scores) a.top_scores[gr * a.topk + j] = lf[j * RS + R] * a.scale;
-          }
-          float acc[D];
-#pragma unroll
-          for (int f = 0; f < D; ++f) acc[f] = 0.f;
-          const T* vbase = static_cast<const T*>(a.v) + slice * a.m * D;
-#pragma unroll 2
-          for (int j = 0; j < a.topk; ++j) {
-            const float p = expf(lf[j * RS + R] * a.scale - lse);
-            const uint4* vrow = reinterpret_cast<const uint4*>(vbase + (int64_t)stage_at(srow, j) * D);
-#pragma unroll
-            for (int q4 = 0; q4 < D / 8; ++q4) {
-              float f[8];
-              unpack8<T>(__ldg(vrow + q4), f);
-#pragma unroll
-              for (int h = 0; h < 8; ++h) acc[q4 * 8 + h] = fmaf(p, f[h], acc[q4 * 8 + h]);
-            }
-          }
-          store_out_row<T>(acc, static_cast<T*>(a.out) + gr * D);
-        }
-      }
-      uint8_t* fix = sm + OFF_FIX + (warp - 4) * FIX_BYTES;
-      unsigned pending = __ballot_sync(0xffffffffu, dead && rl < rows);
-      while (pending) {
-        const int l = __ffs(pending) - 1;
-        pending &= pending - 1;
-        reselect_row<T>(RowOut{a.q, a.k, a.v, a.out, a.top_idx, a.lse, a.top_scores}, a.m, a.topk, a.scale, slice,
-                        row0 + (int64_t)wg * TQ + quarter * kWarp + l, reinterpret_cast<float*>(fix),
-                        reinterpret_cast<int*>(fix + FIX_CAP * 4), reinterpret_cast<float*>(fix + FIX_CAP * 8),
-                        lane);
+      if (!ok) {
+        a.cand_n[gr] = kCandAborted;
+      } else if (dead) {
+        a.cand_n[gr] = kCandDead;
+      } else {
+        uint4* dst = reinterpret_cast<uint4*>(a.cand + gr * CAP);
+        for (int s = 0; s < cnt; s += 4)
+          dst[s >> 2] = make_uint4(list[s * RS + R], list[(s + 1) * RS + R], list[(s + 2) * RS + R],
+                                   list[(s + 3) * RS + R]);
+        a.cand_n[gr] = cnt;
       }
     }
   }
@@ -921,6 +711,312 @@ __global__ void __launch_bounds__(NT, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------ finish ---
+// One warp per query row (see the file comment).  Each warp keeps its row's
+// survivors (key, exact score) and a 256-bin histogram in shared memory; the
+// exact re-selection of marked rows reuses the survivor arrays.
+constexpr int FW = 8;                      // warps per finish block
+constexpr int NV = (CAP + kWarp - 1) / kWarp;  // list entries per lane
+constexpr int FUNR = 4;                    // survivors in flight per lane group
+
+struct FinArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  int32_t* top_idx;
+  float* lse;
+  float* top_scores;
+  const uint32_t* cand;
+  const int32_t* cand_n;
+  int64_t rows, n, m;
+  int topk;
+  float scale;
+};
+
+struct __align__(16) FinWarp {
+  float sc[CAP];  // survivors' exact scores, then the selection's
+  int si[CAP];    // their key indices
+  int hist[256];
+};
+static_assert(sizeof(float) * CAP + sizeof(int) * CAP >= FIX_CAP * 8 + 16, "re-selection buffers exceed sc/si");
+
+// The need-th largest (1 <= need <= count) of the warp's values whose `ok`
+// is set, by 8-bit digits starting at the highest bit in which those values
+// differ, one 256-bin shared-memory histogram per digit.  Only the first
+// `nv` slots of each lane (warp-uniform) may be set.  *above receives how
+// many values are strictly larger.
+__device__ __forceinline__ uint32_t warp_kth_largest(const uint32_t (&v)[NV], const bool (&ok)[NV], int nv,
+                                                     int need, int* hist, int lane, int* above) {
+  uint32_t lo = 0xffffffffu, hi = 0u;
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+    if (i < nv && ok[i]) {
+      lo = min(lo, v[i]);
+      hi = max(hi, v[i]);
+    }
+  lo = __reduce_min_sync(0xffffffffu, lo);
+  hi = __reduce_max_sync(0xffffffffu, hi);
+  int gt = 0;
+  uint32_t prefix = lo;
+  if (hi != lo) {
+    const int top = 31 - __clz(hi ^ lo);
+    prefix = lo & ~(uint32_t)((2ull << top) - 1ull);  // the bits above `top`, common to all
+    for (int lowbit = top - 7;; lowbit -= 8) {
+      const int sh = lowbit < 0 ? 0 : lowbit;
+      const uint32_t dmask = (1u << (lowbit + 8 - sh)) - 1u;
+      reinterpret_cast<int4*>(hist)[2 * lane] = make_int4(0, 0, 0, 0);
+      reinterpret_cast<int4*>(hist)[2 * lane + 1] = make_int4(0, 0, 0, 0);
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+        if (i < nv && ok[i] && ((uint64_t)(v[i] ^ prefix) >> (lowbit + 8)) == 0)
+          atomicAdd(&hist[(v[i] >> sh) & dmask], 1);
+      __syncwarp();
+      // lane L holds bins 255-8L down to 248-8L
+      const int4 h0 = reinterpret_cast<const int4*>(hist)[62 - 2 * lane];
+      const int4 h1 = reinterpret_cast<const int4*>(hist)[63 - 2 * lane];
+      const int c[8] = {h1.w, h1.z, h1.y, h1.x, h0.w, h0.z, h0.y, h0.x};
+      int tot = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) tot += c[i];
+      int incl = tot;
+#pragma unroll
+      for (int o = 1; o < kWarp; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      const int excl = incl - tot;
+      const int src = __ffs(__ballot_sync(0xffffffffu, excl < need && need <= incl)) - 1;
+      int dig = -1, before = 0, run = excl;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (dig < 0 && run + c[i] >= need) {
+          dig = 255 - 8 * lane - i;
+          before = run;
+        }
+        run += c[i];
+      }
+      dig = __shfl_sync(0xffffffffu, dig, src);
+      before = __shfl_sync(0xffffffffu, before, src);
+      prefix |= (uint32_t)dig << sh;
+      need -= before;
+      gt += before;
+      __syncwarp();
+      if (lowbit <= 0) break;
+    }
+  }
+  *above = gt;
+  return prefix;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
+  __shared__ FinWarp sw[FW];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane & 7, grp = lane >> 3;
+  const unsigned lt = (1u << lane) - 1u;
+  FinWarp& w = sw[warp];
+  for (int64_t r = (int64_t)blockIdx.x * FW + warp; r < a.rows; r += (int64_t)gridDim.x * FW) {
+    const int cnt = a.cand_n[r];
+    if (cnt == kCandAborted) continue;
+    const int64_t slice = r / a.n;
+    if (cnt < 0) {
+      uint8_t* fix = reinterpret_cast<uint8_t*>(&w);
+      reselect_row<T>(RowOut{a.q, a.k, a.v, a.out, a.top_idx, a.lse, a.top_scores}, a.m, a.topk, a.scale, slice, r,
+                      reinterpret_cast<float*>(fix), reinterpret_cast<int*>(fix + FIX_CAP * 4),
+                      reinterpret_cast<float*>(fix + FIX_CAP * 8), lane);
+      continue;
+    }
+    // bucket cut: keep the entries whose bucket reaches the k-th largest
+    const int nv = (cnt + kWarp - 1) / kWarp;
+    uint32_t e[NV], o[NV];
+    bool ok[NV];
+    const uint32_t* crow = a.cand + r * CAP;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int s = lane + kWarp * i;
+      ok[i] = false;
+      e[i] = 0u;
+      if (i < nv) {
+        ok[i] = s < cnt;
+        e[i] = ok[i] ? crow[s] : 0u;
+      }
+      o[i] = ord_entry(e[i]) >> 16;
+    }
+    int above = 0;
+    const uint32_t tb = cnt > a.topk ? warp_kth_largest(o, ok, nv, a.topk, w.hist, lane, &above) : 0u;
+    int S = 0;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      if (i < nv) {
+        const bool keep = ok[i] && o[i] >= tb;
+        const unsigned b = __ballot_sync(0xffffffffu, keep);
+        if (keep) w.si[S + __popc(b & lt)] = (int)(e[i] & 0xffffu);
+        S += __popc(b);
+      }
+    }
+    __syncwarp();
+    // exact scores: group grp re-scores survivors grp, grp + 4, ...
+    const uint4 qg = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(a.q) + r * D) + g);
+    const T* kbase = static_cast<const T*>(a.k) + slice * a.m * D;
+    for (int s0 = 0; s0 < S; s0 += 4 * FUNR) {
+      uint4 kc[FUNR];
+#pragma unroll
+      for (int u = 0; u < FUNR; ++u) {
+        const int s = s0 + 4 * u + grp;
+        kc[u] = make_uint4(0u, 0u, 0u, 0u);
+        if (s < S) kc[u] = __ldg(reinterpret_cast<const uint4*>(kbase + (int64_t)w.si[s] * D) + g);
+      }
+#pragma unroll
+      for (int u = 0; u < FUNR; ++u) {
+        const int s = s0 + 4 * u + grp;
+        const float d = group_dot<T>(qg, kc[u]);
+        if (g == 0 && s < S) w.sc[s] = d;
+      }
+    }
+    __syncwarp();
+    // exact cut to k: larger score first, lower key index on equal scores
+    int sel = S;
+    if (S > a.topk) {
+      const int sv = (S + kWarp - 1) / kWarp;
+      bool hk[NV];
+      float xs[NV];
+      int ks[NV];
+      uint64_t rk[NV];
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int s = lane + kWarp * i;
+        hk[i] = i < sv && s < S;
+        xs[i] = hk[i] ? w.sc[s] : 0.f;
+        ks[i] = hk[i] ? w.si[s] : 0;
+        rk[i] = hk[i] ? rank_key(xs[i], (uint32_t)ks[i]) : ~0ull;
+      }
+      if (S - a.topk <= 8) {
+        // few extra: drop the lowest-ranked one at a time (rank keys are
+        // distinct, so each round removes exactly one)
+        for (int d = S - a.topk; d > 0; --d) {
+          uint64_t mn = ~0ull;
+#pragma unroll
+          for (int i = 0; i < NV; ++i)
+            if (i < sv) mn = rk[i] < mn ? rk[i] : mn;
+          const uint32_t mh = __reduce_min_sync(0xffffffffu, (uint32_t)(mn >> 32));
+          const uint32_t ml = __reduce_min_sync(0xffffffffu, (uint32_t)(mn >> 32) == mh ? (uint32_t)mn : 0xffffffffu);
+          const uint64_t low = ((uint64_t)mh << 32) | ml;
+#pragma unroll
+          for (int i = 0; i < NV; ++i)
+            if (i < sv && rk[i] == low) {
+              rk[i] = ~0ull;
+              hk[i] = false;
+            }
+        }
+      } else {
+        uint32_t hv[NV], lv[NV];
+        bool lk[NV];
+#pragma unroll
+        for (int i = 0; i < NV; ++i) hv[i] = (uint32_t)(rk[i] >> 32);
+        int gt = 0;
+        const uint32_t ts = warp_kth_largest(hv, hk, sv, a.topk, w.hist, lane, &gt);
+        const int need = a.topk - gt;
+        int eq = 0;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          lk[i] = hk[i] && hv[i] == ts;
+          lv[i] = (uint32_t)rk[i];
+          if (i < sv) eq += __popc(__ballot_sync(0xffffffffu, lk[i]));
+        }
+        uint32_t tl = 0u;  // the kept ties are those whose low word reaches tl
+        if (eq > need) {
+          int unused = 0;
+          tl = warp_kth_largest(lv, lk, sv, need, w.hist, lane, &unused);
+        }
+#pragma unroll
+        for (int i = 0; i < NV; ++i) hk[i] = hk[i] && (hv[i] > ts || (lk[i] && lv[i] >= tl));
+      }
+      __syncwarp();
+      int pos = 0;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        if (i < sv) {
+          const unsigned b = __ballot_sync(0xffffffffu, hk[i]);
+          if (hk[i]) {
+            const int p = pos + __popc(b & lt);
+            w.sc[p] = xs[i];
+            w.si[p] = ks[i];
+          }
+          pos += __popc(b);
+        }
+      }
+      __syncwarp();
+      sel = pos;
+    }
+    // LSE; lane j holds selections j and j + 32 (k <= 64)
+    const bool v0 = lane < sel, v1 = lane + kWarp < sel;
+    const float x0 = v0 ? w.sc[lane] : 0.f, x1 = v1 ? w.sc[lane + kWarp] : 0.f;
+    const int k0 = v0 ? w.si[lane] : 0, k1 = v1 ? w.si[lane + kWarp] : 0;
+    float mx = fmaxf(v0 ? x0 : __int_as_float(0xff800000), v1 ? x1 : __int_as_float(0xff800000));
+#pragma unroll
+    for (int o2 = 16; o2 > 0; o2 >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o2));
+    const float mxs = mx * a.scale;
+    float part = (v0 ? expf(x0 * a.scale - mxs) : 0.f) + (v1 ? expf(x1 * a.scale - mxs) : 0.f);
+#pragma unroll
+    for (int o2 = 16; o2 > 0; o2 >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o2);
+    const float lse = mxs + logf(part);
+    if (lane == 0) a.lse[r] = lse;
+    float* pw = reinterpret_cast<float*>(w.hist);  // softmax weight of each selection
+    int32_t* idx_row = a.top_idx + r * a.topk;
+    if (v0) {
+      pw[lane] = expf(x0 * a.scale - lse);
+      idx_row[lane] = k0;
+      if (a.top_scores) a.top_scores[r * a.topk + lane] = x0 * a.scale;
+    }
+    if (v1) {
+      pw[lane + kWarp] = expf(x1 * a.scale - lse);
+      idx_row[lane + kWarp] = k1;
+      if (a.top_scores) a.top_scores[r * a.topk + lane + kWarp] = x1 * a.scale;
+    }
+    __syncwarp();
+    // softmax-weighted sum of the value rows: group grp takes selections
+    // grp, grp + 4, ... in order; the groups are added by xor-shuffles
+    const T* vbase = static_cast<const T*>(a.v) + slice * a.m * D;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j0 = 0; j0 < sel; j0 += 4 * FUNR) {
+      uint4 vc[FUNR];
+      float pj[FUNR];
+#pragma unroll
+      for (int u = 0; u < FUNR; ++u) {
+        const int j = j0 + 4 * u + grp;
+        vc[u] = make_uint4(0u, 0u, 0u, 0u);
+        pj[u] = 0.f;
+        if (j < sel) {
+          pj[u] = pw[j];
+          vc[u] = __ldg(reinterpret_cast<const uint4*>(vbase + (int64_t)w.si[j] * D) + g);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < FUNR; ++u) {
+        float f[8];
+        unpack8<T>(vc[u], f);
+#pragma unroll
+        for (int h = 0; h < 8; ++h) acc[h] = fmaf(pj[u], f[h], acc[h]);
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < 8; ++h) {
+      acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 8);
+      acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 16);
+    }
+    if (lane < 8) {
+      uint4 u;
+      T* ev = reinterpret_cast<T*>(&u);
+#pragma unroll
+      for (int h = 0; h < 8; ++h) ev[h] = from_acc<T>(acc[h]);
+      reinterpret_cast<uint4*>(static_cast<T*>(a.out) + r * D)[g] = u;
+    }
+    __syncwarp();
   }
 }
 
@@ -959,33 +1055,80 @@ bool make_rows_map(CUtensorMap* map, const void* base, int64_t rows, bool bf16) 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Stream-ordered scratch for the candidate buffer: a memory pool of this
+// library per device that keeps what it has reserved (no release at
+// synchronisation), so repeated calls reuse the same device memory.
+cudaMemPool_t scratch_pool() {
+  static std::mutex mu;
+  static cudaMemPool_t pools[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!pools[dev]) {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t pool = nullptr;
+    if (cudaMemPoolCreate(&pool, &props) != cudaSuccess) return nullptr;
+    uint64_t keep = ~0ull;
+    if (cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep) != cudaSuccess) return nullptr;
+    pools[dev] = pool;
+  }
+  return pools[dev];
+}
+
 template <typename T>
 int launch(const FwdLaunch& L) {
   CUtensorMap tq, tk;
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   if (!make_rows_map(&tq, L.q, L.slices * L.n, bf16)) return SDK_ERR_CUDA;
   if (!make_rows_map(&tk, L.k, L.slices * L.m, bf16)) return SDK_ERR_CUDA;
+  const int64_t rows = L.slices * L.n;
   TcArgs a;
-  a.q = L.q;
-  a.k = L.k;
-  a.v = L.v;
-  a.out = L.out;
-  a.top_idx = L.top_idx;
-  a.lse = static_cast<float*>(L.lse);
-  a.top_scores = static_cast<float*>(L.top_scores);
   a.n = L.n;
   a.m = L.m;
   a.tiles_per_slice = (int)((L.n + RS - 1) / RS);
   a.topk = L.topk;
-  a.scale = (float)L.scale;
   a.status = L.status;
   const int64_t grid = L.slices * a.tiles_per_slice;
   if (grid <= 0) return SDK_OK;
   auto kern = fused_fwd_tc<T>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
     return SDK_ERR_CUDA;
+  cudaMemPool_t pool = scratch_pool();
+  if (!pool) return SDK_ERR_CUDA;
+  void* ws = nullptr;
+  if (cudaMallocFromPoolAsync(&ws, (size_t)rows * (CAP * 4 + 4), pool, L.stream) != cudaSuccess) return SDK_ERR_CUDA;
+  a.cand = static_cast<uint32_t*>(ws);
+  a.cand_n = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + (size_t)rows * CAP * 4);
   kern<<<(unsigned)grid, NT, SMEM_BYTES, L.stream>>>(tq, tk, a);
-  return cudaPeekAtLastError() == cudaSuccess ? SDK_OK : SDK_ERR_CUDA;
+  int rc = cudaPeekAtLastError() == cudaSuccess ? SDK_OK : SDK_ERR_CUDA;
+  if (rc == SDK_OK) {
+    FinArgs f;
+    f.q = L.q;
+    f.k = L.k;
+    f.v = L.v;
+    f.out = L.out;
+    f.top_idx = L.top_idx;
+    f.lse = static_cast<float*>(L.lse);
+    f.top_scores = static_cast<float*>(L.top_scores);
+    f.cand = a.cand;
+    f.cand_n = a.cand_n;
+    f.rows = rows;
+    f.n = L.n;
+    f.m = L.m;
+    f.topk = L.topk;
+    f.scale = (float)L.scale;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t want = (rows + FW - 1) / FW, cap = (int64_t)sms * 8;
+    fwd_tc_finish<T><<<(unsigned)(want < cap ? want : cap), FW * kWarp, 0, L.stream>>>(f);
+    rc = cudaPeekAtLastError() == cudaSuccess ? SDK_OK : SDK_ERR_CUDA;
+  }
+  if (cudaFreeAsync(ws, L.stream) != cudaSuccess) rc = SDK_ERR_CUDA;
+  return rc;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
