@@ -4,8 +4,11 @@
  * Plain pointers and sizes only: every tensor argument is a device pointer to
  * a dense row-major buffer, every size is an element count, `stream` is a
  * cudaStream_t passed as void* (NULL = the legacy default stream).  No call
- * allocates device memory, synchronises the host, or throws: each returns 0
- * (SDK_OK) or one of the status codes below; sdk_status_string() names it.
+ * synchronises the host or throws: each returns 0 (SDK_OK) or one of the
+ * status codes below; sdk_status_string() names it.  No call allocates
+ * device memory except sdk_topk_attn_fwd on the tensor-core path, which takes
+ * stream-ordered scratch from a memory pool of this library (kept for reuse);
+ * sdk_topk_attn_fwd_ws is the same forward on the caller's scratch.
  *
  * Layout conventions (the reference's flattened layout,
  * kernels/fused_topk_attn.py:999-1001):
@@ -82,6 +85,32 @@ int sdk_topk_attn_fwd(const void* q, const void* k, const void* v, void* out, in
                       const int32_t* row_index, int64_t slices, int64_t n, int64_t m, int32_t d,
                       int32_t dv, int32_t topk, double scale, int32_t score_grid, int32_t dtype,
                       void* stream);
+
+/*
+ * Scratch of the forward: the bf16/fp16 tensor-core path (d = dv = 64,
+ * topk <= 64) hands each query row's candidate list (176 four-byte entries and
+ * a count) from its streaming kernel to its finishing kernel.  Returns the
+ * bytes for `rows` query rows (slices*n, or the grouped row count), 0 when the
+ * shape never takes that path.  The reference's wrapper allocates its
+ * intermediate top-k buffers with torch (fused_topk_attn.py:1012-1017);
+ * callers that own their memory allocate this and pass it to
+ * sdk_topk_attn_fwd_ws.
+ */
+size_t sdk_topk_attn_fwd_workspace_size(int64_t rows, int32_t d, int32_t dv, int32_t topk,
+                                        int32_t dtype);
+
+/*
+ * sdk_topk_attn_fwd on caller scratch: `workspace` (16-byte aligned, at least
+ * sdk_topk_attn_fwd_workspace_size bytes) is used instead of the library pool;
+ * SDK_ERR_INVALID_ARGUMENT when it is too small or misaligned.  May be NULL
+ * with workspace_bytes 0 (then as sdk_topk_attn_fwd).  The workspace must not
+ * be reused by another call until this call's launches on `stream` are done.
+ */
+int sdk_topk_attn_fwd_ws(const void* q, const void* k, const void* v, void* out, int32_t* top_idx,
+                         void* lse, void* top_scores, const int32_t* row_offsets,
+                         const int32_t* row_index, int64_t slices, int64_t n, int64_t m, int32_t d,
+                         int32_t dv, int32_t topk, double scale, int32_t score_grid, int32_t dtype,
+                         void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Sparse backward on the saved support (replaces

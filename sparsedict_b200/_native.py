@@ -38,6 +38,9 @@ SIGNATURES = {
     "sdk_max_topk": [_i32, _i32],
     "sdk_device_status": [ctypes.POINTER(ctypes.c_uint), _i32, _p],
     "sdk_topk_attn_fwd": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _i32, _f64, _i32, _i32, _p],
+    "sdk_topk_attn_fwd_workspace_size": [_i64, _i32, _i32, _i32, _i32],
+    "sdk_topk_attn_fwd_ws": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _i32, _f64, _i32, _i32,
+                             _p, ctypes.c_size_t, _p],
     "sdk_topk_attn_bwd": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _i32, _f64, _i32,
                           _i32, _i32, _p],
     "sdk_topk_attn_fwd_biased": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _i32, _f64, _i32,
@@ -51,7 +54,8 @@ SIGNATURES = {
     "sdk_topk_aggregate": [_p, _p, _p, _p, _i64, _i32, _i64, _i32, _i64, _i64, _i64, _i32, _i32, _i32, _p],
     "sdk_route_top1": [_p, _i64, _i32, _p, _p, _p, _p],
 }
-_RESTYPES = {"sdk_status_string": ctypes.c_char_p, "sdk_last_cuda_error": ctypes.c_char_p}
+_RESTYPES = {"sdk_status_string": ctypes.c_char_p, "sdk_last_cuda_error": ctypes.c_char_p,
+             "sdk_topk_attn_fwd_workspace_size": ctypes.c_size_t}
 
 _lock = threading.Lock()
 _lib = None

@@ -59,7 +59,11 @@ def topk_attn_fwd(
                 nat.ptr(scores), nat.ptr(row_offsets), nat.ptr(row_index),
                 slices, n, m, d, dv, topk, float(scale), int(score_grid))
         if seg_bias is None:
-            nat.call("sdk_topk_attn_fwd", *head, nat.TORCH_TO_SDK[q2.dtype], nat.stream_of(dev))
+            # scratch from torch's allocator, like every other buffer of the op
+            code = nat.TORCH_TO_SDK[q2.dtype]
+            nbytes = int(nat.load().sdk_topk_attn_fwd_workspace_size(rows, d, dv, topk, code))
+            ws = torch.empty((nbytes,), device=dev, dtype=torch.uint8) if nbytes else None
+            nat.call("sdk_topk_attn_fwd_ws", *head, code, nat.ptr(ws), nbytes, nat.stream_of(dev))
         else:
             segs = seg_bias.shape[-1]
             nat.call("sdk_topk_attn_fwd_biased", *head, seg_bias.data_ptr(), m // segs, segs,

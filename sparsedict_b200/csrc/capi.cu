@@ -1,7 +1,10 @@
 // extern "C" entry points of libsparsedict_b200.so (declared in
 // include/sparsedict_b200.h).  Each validates its arguments, picks the
 // kernel for the dtype/shape and launches on the caller's stream.  No
-// exceptions cross this boundary and nothing here allocates device memory.
+// exceptions cross this boundary.  The only device memory the library takes
+// itself is the tensor-core forward's stream-ordered scratch when the caller
+// passes no workspace (fwd_tc.cu) and the no-allocation backward's static
+// array (bwd_noalloc.cu).
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -117,7 +120,7 @@ namespace {
 int fwd_impl(const void* q, const void* k, const void* v, void* out, int32_t* top_idx, void* lse, void* top_scores,
              const int32_t* row_offsets, const int32_t* row_index, int64_t slices, int64_t n, int64_t m, int32_t d,
              int32_t dv, int32_t topk, double scale, int32_t score_grid, const void* seg_bias, int64_t seg_len,
-             int32_t segs, int32_t dtype, void* stream) {
+             int32_t segs, int32_t dtype, void* stream, void* workspace = nullptr, size_t workspace_bytes = 0) {
   if (!q || !k || !v || !out || !top_idx || !lse) return SDK_ERR_INVALID_ARGUMENT;
   if (!dtype_ok(dtype) || slices <= 0 || n < 0 || m <= 0 || d <= 0 || dv <= 0) return SDK_ERR_INVALID_ARGUMENT;
   if (topk < 1 || topk > m || m > 0x7ffffffe || !(scale > 0) || score_grid < 0) return SDK_ERR_INVALID_ARGUMENT;
@@ -128,6 +131,8 @@ int fwd_impl(const void* q, const void* k, const void* v, void* out, int32_t* to
   L.seg_bias = seg_bias;
   L.seg_len = seg_len;
   L.segs = segs;
+  L.workspace = workspace;
+  L.workspace_bytes = workspace_bytes;
   if (fwd_tensorcore_supports(L)) return finish(fwd_tensorcore(L));
   return finish(fwd_generic(L));
 }
@@ -175,6 +180,19 @@ int sdk_topk_attn_fwd(const void* q, const void* k, const void* v, void* out, in
                       int32_t dtype, void* stream) {
   return fwd_impl(q, k, v, out, top_idx, lse, top_scores, row_offsets, row_index, slices, n, m, d, dv, topk, scale,
                   score_grid, nullptr, 0, 0, dtype, stream);
+}
+
+size_t sdk_topk_attn_fwd_workspace_size(int64_t rows, int32_t d, int32_t dv, int32_t topk, int32_t dtype) {
+  return fwd_tensorcore_workspace(rows, d, dv, topk, dtype);
+}
+
+int sdk_topk_attn_fwd_ws(const void* q, const void* k, const void* v, void* out, int32_t* top_idx, void* lse,
+                         void* top_scores, const int32_t* row_offsets, const int32_t* row_index, int64_t slices,
+                         int64_t n, int64_t m, int32_t d, int32_t dv, int32_t topk, double scale,
+                         int32_t score_grid, int32_t dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!workspace && workspace_bytes) return SDK_ERR_INVALID_ARGUMENT;
+  return fwd_impl(q, k, v, out, top_idx, lse, top_scores, row_offsets, row_index, slices, n, m, d, dv, topk, scale,
+                  score_grid, nullptr, 0, 0, dtype, stream, workspace, workspace_bytes);
 }
 
 int sdk_topk_attn_bwd(const void* q, const void* k, const void* v, const void* dout, const int32_t* top_idx,

@@ -1055,6 +1055,8 @@ bool make_rows_map(CUtensorMap* map, const void* base, int64_t rows, bool bf16) 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 // Stream-ordered scratch for the candidate buffer: a memory pool of this
 // library per device that keeps what it has reserved (no release at
 // synchronisation), so repeated calls reuse the same device memory.
@@ -1096,10 +1098,16 @@ int launch(const FwdLaunch& L) {
   auto kern = fused_fwd_tc<T>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
     return SDK_ERR_CUDA;
-  cudaMemPool_t pool = scratch_pool();
-  if (!pool) return SDK_ERR_CUDA;
-  void* ws = nullptr;
-  if (cudaMallocFromPoolAsync(&ws, (size_t)rows * (CAP * 4 + 4), pool, L.stream) != cudaSuccess) return SDK_ERR_CUDA;
+  const size_t need = (size_t)rows * (CAP * 4 + 4);
+  void* ws = L.workspace;
+  const bool pooled = ws == nullptr;
+  if (pooled) {
+    cudaMemPool_t pool = scratch_pool();
+    if (!pool) return SDK_ERR_CUDA;
+    if (cudaMallocFromPoolAsync(&ws, need, pool, L.stream) != cudaSuccess) return SDK_ERR_CUDA;
+  } else if (L.workspace_bytes < need || !aligned16(ws)) {
+    return SDK_ERR_INVALID_ARGUMENT;
+  }
   a.cand = static_cast<uint32_t*>(ws);
   a.cand_n = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + (size_t)rows * CAP * 4);
   kern<<<(unsigned)grid, NT, SMEM_BYTES, L.stream>>>(tq, tk, a);
@@ -1127,11 +1135,9 @@ int launch(const FwdLaunch& L) {
     fwd_tc_finish<T><<<(unsigned)(want < cap ? want : cap), FW * kWarp, 0, L.stream>>>(f);
     rc = cudaPeekAtLastError() == cudaSuccess ? SDK_OK : SDK_ERR_CUDA;
   }
-  if (cudaFreeAsync(ws, L.stream) != cudaSuccess) rc = SDK_ERR_CUDA;
+  if (pooled && cudaFreeAsync(ws, L.stream) != cudaSuccess) rc = SDK_ERR_CUDA;
   return rc;
 }
-
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace
 
@@ -1143,6 +1149,12 @@ bool fwd_tensorcore_supports(const FwdLaunch& L) {
   if (L.slices * L.n > 0x7fffff00 || L.slices * L.m > 0x7fffffff) return false;
   if (!aligned16(L.q) || !aligned16(L.k) || !aligned16(L.v) || !aligned16(L.out)) return false;
   return encode_fn() != nullptr;
+}
+
+size_t fwd_tensorcore_workspace(int64_t rows, int d, int dv, int topk, int dtype) {
+  if (dtype != SDK_DTYPE_BF16 && dtype != SDK_DTYPE_F16) return 0;
+  if (d != D || dv != D || topk > 64 || rows <= 0) return 0;
+  return (size_t)rows * (CAP * 4 + 4);
 }
 
 int fwd_tensorcore(const FwdLaunch& L) {

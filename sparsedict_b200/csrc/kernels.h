@@ -40,6 +40,10 @@ struct FwdLaunch {
   const void* seg_bias = nullptr;
   int64_t seg_len = 0;
   int segs = 0;
+  // Scratch of the tensor-core forward (fwd_tensorcore_workspace bytes, 16-byte
+  // aligned); null: stream-ordered scratch from this library's memory pool.
+  void* workspace = nullptr;
+  size_t workspace_bytes = 0;
 };
 
 struct BwdLaunch {
@@ -82,6 +86,9 @@ int max_topk_generic(int dtype, int d);
 // SDK_ERR_UNSUPPORTED for shapes it does not take.
 int fwd_tensorcore(const FwdLaunch& L);
 bool fwd_tensorcore_supports(const FwdLaunch& L);
+// Scratch bytes the tensor-core forward needs for `rows` query rows when the
+// shape can take that path (bf16/fp16, d = dv = 64, topk <= 64), else 0.
+size_t fwd_tensorcore_workspace(int64_t rows, int d, int dv, int topk, int dtype);
 
 // Sparse backward (bwd.cu).
 int bwd_sparse(const BwdLaunch& L);

@@ -71,3 +71,24 @@ def test_max_topk_covers_the_benchmark_configurations(dtype):
     assert lib.sdk_max_topk(dtype, 64) >= 64
     assert lib.sdk_max_topk(dtype, 128) >= 128
     assert lib.sdk_max_topk(9, 64) == 0
+
+
+def test_forward_workspace_size_follows_the_tensor_core_shapes():
+    lib = _native.load()
+    per_row = 176 * 4 + 4  # candidate list and count per query row
+    for code in (_native.DTYPE_BF16, _native.DTYPE_F16):
+        assert lib.sdk_topk_attn_fwd_workspace_size(1000, 64, 64, 64, code) == 1000 * per_row
+        assert lib.sdk_topk_attn_fwd_workspace_size(3, 64, 64, 1, code) == 3 * per_row
+        assert lib.sdk_topk_attn_fwd_workspace_size(1000, 64, 64, 65, code) == 0
+        assert lib.sdk_topk_attn_fwd_workspace_size(1000, 32, 32, 8, code) == 0
+        assert lib.sdk_topk_attn_fwd_workspace_size(0, 64, 64, 8, code) == 0
+    for code in (_native.DTYPE_F32, _native.DTYPE_F64):
+        assert lib.sdk_topk_attn_fwd_workspace_size(1000, 64, 64, 64, code) == 0
+
+
+def test_forward_workspace_pointer_and_size_must_agree():
+    lib = _native.load()
+    fake = 0x1000
+    rc = lib.sdk_topk_attn_fwd_ws(fake, fake, fake, fake, fake, fake, None, None, None,
+                                  1, 4, 8, 16, 16, 2, 0.25, 0, 0, None, 64, None)
+    assert rc == _native.SDK_ERR_INVALID_ARGUMENT

@@ -377,6 +377,39 @@ def test_bf16_tensor_core_exact_ties_lower_index_wins(n, m, k):
     np.testing.assert_allclose(out.float().cpu().numpy(), o, rtol=2e-2, atol=2e-2)
 
 
+def test_tensor_core_forward_on_caller_workspace_matches_library_pool():
+    # The same forward through sdk_topk_attn_fwd (library memory pool) and
+    # sdk_topk_attn_fwd_ws (a torch-allocated workspace) gives identical
+    # results; a workspace one byte short, or misaligned, is refused before
+    # anything is launched.
+    lib = _native.load()
+    g = torch.Generator().manual_seed(11)
+    bh, n, m, d, k = 2, 300, 1000, 64, 16
+    q, kk, v = (torch.randn(bh, x, d, generator=g).to(torch.bfloat16).to(DEV) for x in (n, m, m))
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def run(ws, nbytes, pooled=False):
+        out = torch.zeros(bh, n, d, device=DEV, dtype=torch.bfloat16)
+        idx = torch.zeros(bh * n, k, device=DEV, dtype=torch.int32)
+        lse = torch.zeros(bh * n, device=DEV)
+        args = (q.data_ptr(), kk.data_ptr(), v.data_ptr(), out.data_ptr(), idx.data_ptr(), lse.data_ptr(),
+                None, None, None, bh, n, m, d, d, k, 0.125, 0, _native.DTYPE_BF16)
+        rc = lib.sdk_topk_attn_fwd(*args, stream) if pooled else lib.sdk_topk_attn_fwd_ws(*args, ws, nbytes, stream)
+        torch.cuda.synchronize()
+        return rc, out, idx, lse
+
+    need = lib.sdk_topk_attn_fwd_workspace_size(bh * n, d, d, k, _native.DTYPE_BF16)
+    assert need == bh * n * (176 * 4 + 4)
+    buf = torch.empty(need + 16, device=DEV, dtype=torch.uint8)
+    rc0, o0, i0, l0 = run(None, 0, pooled=True)
+    rc1, o1, i1, l1 = run(buf.data_ptr(), need)
+    assert rc0 == rc1 == _native.SDK_OK
+    assert torch.equal(o0, o1) and torch.equal(i0, i1) and torch.equal(l0, l1)
+    assert run(buf.data_ptr(), need - 1)[0] == _native.SDK_ERR_INVALID_ARGUMENT
+    assert run(buf.data_ptr() + 4, need)[0] == _native.SDK_ERR_INVALID_ARGUMENT
+    assert _native.device_status(clear=True) == 0
+
+
 # --- tie stress (configuration 5 shape family, reduced size) ----------------------
 
 
