@@ -96,12 +96,30 @@ constexpr int32_t kCandDead = -1;     // list could not be shrunk: re-select exa
 constexpr int32_t kCandAborted = -2;  // a pipeline wait timed out: nothing to finish
 
 struct TcArgs {
-  uint32_t* cand;   // [rows][CAP] list entries of each query row
-  int32_t* cand_n;  // [rows] entry count, kCandDead or kCandAborted
+  const void* k;     // key rows, for the magnitude check
+  uint32_t* cand;    // [rows][CAP] list entries of each query row
+  int32_t* cand_n;   // [rows] entry count, kCandDead or kCandAborted
+  uint32_t* unsafe;  // [slices] 1 when a key of the slice fails the magnitude check
   int64_t n, m;
   int tiles_per_slice, topk;
+  uint32_t big16;    // 16-bit magnitude field at which an element counts as unsafe
   unsigned int* status;
 };
+
+// Input magnitude check.  With every |q|, |k| < 2^60 and finite, each of the
+// 64 products is below 2^120 and their fp32 sum below 2^126, so no score can
+// overflow to inf or become NaN; the stream filter then needs no NaN
+// handling.  Rows whose inputs fail the check (a non-finite or huge element
+// in the query row or anywhere in the slice's keys) are re-selected exactly
+// by the finish kernel.  `big16` is the lowest 15-bit magnitude pattern that
+// fails: 2^60 for bf16 (0x5d80), inf/NaN for fp16 (0x7c00, fp16 has no
+// finite value that large).
+__device__ __forceinline__ uint32_t big_halves(uint32_t w, uint32_t add) {
+  // bit 15 / 31 set when that half's magnitude reaches big16 (add = 0x8000 -
+  // big16 in both halves; the sum of a half stays below 0x10000)
+  return ((w & 0x7fff7fffu) + add) & 0x80008000u;
+}
+
 
 // ---------------------------------------------------- bucketed list entries ---
 // Order-preserving form of an entry: the high 16 bits order the buckets like
@@ -495,7 +513,10 @@ __device__ __noinline__ void reselect_row(RowOut a, int64_t m, int topk, float s
   __syncwarp();
 }
 
-template <typename T>
+// kPrefilter: skip 32-key chunks in which no row of the warp has a hit.
+// That pays only for small k: with k >= 8, some row of the warp has a hit in
+// nearly every chunk and the test is pure overhead.
+template <typename T, bool kPrefilter>
 __global__ void __launch_bounds__(NT, 1)
     fused_fwd_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                  TcArgs a) {
@@ -513,6 +534,7 @@ __global__ void __launch_bounds__(NT, 1)
   uint64_t* s_empty = s_full + 2 * NTILE;     // [tile][buffer]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + OFF_MISC + 4);
+  volatile uint32_t* scan_big = reinterpret_cast<volatile uint32_t*>(sm + OFF_MISC + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t slice = blockIdx.x / a.tiles_per_slice;
@@ -567,6 +589,34 @@ __global__ void __launch_bounds__(NT, 1)
         while (!mbar_try_wait(q_full, 0) && global_timer() - t0 < kWaitLimitNs) {
         }
       }
+    }
+  } else if (warp == 2 || warp == 3) {
+    // The first CTA of each slice also checks the slice's keys for unsafe
+    // magnitudes, with its two otherwise idle warps reading the key rows
+    // from global memory (L2: the slice's CTAs are streaming them).
+    if (local0 == 0) {
+      const uint4* kp = reinterpret_cast<const uint4*>(static_cast<const T*>(a.k) + slice * a.m * D);
+      const int64_t total = a.m * (D / 8);
+      const uint32_t add = (0x8000u - a.big16) * 0x00010001u;
+      uint32_t big = 0;
+      const int64_t step = 2 * kWarp;
+      int64_t i = (int64_t)(warp - 2) * kWarp + lane;
+      for (; i + 15 * step < total; i += 16 * step) {
+        uint4 u[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) u[j] = __ldg(kp + i + j * step);
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          big |= big_halves(u[j].x, add) | big_halves(u[j].y, add) | big_halves(u[j].z, add) | big_halves(u[j].w, add);
+      }
+      for (; i < total; i += step) {
+        const uint4 u = __ldg(kp + i);
+        big |= big_halves(u.x, add) | big_halves(u.y, add) | big_halves(u.z, add) | big_halves(u.w, add);
+      }
+      const bool any_big = __any_sync(0xffffffffu, big != 0u);
+      if (warp == 3 && lane == 0) *scan_big = any_big ? 1u : 0u;
+      named_bar_sync(1, 2 * kWarp);
+      if (warp == 2 && lane == 0) a.unsafe[slice] = (any_big || *scan_big) ? 1u : 0u;
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -635,20 +685,17 @@ __global__ void __launch_bounds__(NT, 1)
       // its last chunk is in registers.
       auto chunk_step = [&](uint32_t(&v)[32], int c) {
         const int valid = tile_valid - c * 32;
-        float mx;
-        if (valid >= 32) {
-          mx = chunk_max(v);
-        } else {
-          mx = __int_as_float(0xff800000);
+        if (kPrefilter) {
+          float mx;
+          if (valid >= 32) {
+            mx = chunk_max(v);
+          } else {
+            mx = __int_as_float(0xff800000);
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (i < valid) mx = max_nan(mx, __uint_as_float(v[i]));
-        }
-        if (!__any_sync(0xffffffffu, !(mx <= tau))) return;
-        if (__any_sync(0xffffffffu, mx != mx)) {
-          // one NaN pattern, ranked above every number
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = ((v[i] & 0x7fffffffu) > 0x7f800000u) ? 0x7fffffffu : v[i];
+            for (int i = 0; i < 32; ++i)
+              if (i < valid) mx = max_nan(mx, __uint_as_float(v[i]));
+          }
+          if (!__any_sync(0xffffffffu, !(mx <= tau))) return;
         }
         append_chunk(v, dead ? 0 : valid, tau, (uint32_t)(key_tile + c * 32), lbase, cnt);
         // When one lane's list could overflow, every lane holding well over
@@ -732,9 +779,11 @@ struct FinArgs {
   float* top_scores;
   const uint32_t* cand;
   const int32_t* cand_n;
+  const uint32_t* unsafe;  // per slice, from the stream kernel's key check
   int64_t rows, n, m;
   int topk;
   float scale;
+  uint32_t big16;
 };
 
 struct __align__(16) FinWarp {
@@ -824,7 +873,12 @@ __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
     const int cnt = a.cand_n[r];
     if (cnt == kCandAborted) continue;
     const int64_t slice = r / a.n;
-    if (cnt < 0) {
+    const uint4 qg = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(a.q) + r * D) + g);
+    const uint32_t add = (0x8000u - a.big16) * 0x00010001u;
+    const bool unsafe = __any_sync(0xffffffffu, (big_halves(qg.x, add) | big_halves(qg.y, add) |
+                                                 big_halves(qg.z, add) | big_halves(qg.w, add)) != 0u) ||
+                        a.unsafe[slice] != 0u;
+    if (cnt < 0 || unsafe) {
       uint8_t* fix = reinterpret_cast<uint8_t*>(&w);
       reselect_row<T>(RowOut{a.q, a.k, a.v, a.out, a.top_idx, a.lse, a.top_scores}, a.m, a.topk, a.scale, slice, r,
                       reinterpret_cast<float*>(fix), reinterpret_cast<int*>(fix + FIX_CAP * 4),
@@ -861,7 +915,6 @@ __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
     }
     __syncwarp();
     // exact scores: group grp re-scores survivors grp, grp + 4, ...
-    const uint4 qg = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(a.q) + r * D) + g);
     const T* kbase = static_cast<const T*>(a.k) + slice * a.m * D;
     for (int s0 = 0; s0 < S; s0 += 4 * FUNR) {
       uint4 kc[FUNR];
@@ -1088,6 +1141,7 @@ int launch(const FwdLaunch& L) {
   if (!make_rows_map(&tk, L.k, L.slices * L.m, bf16)) return SDK_ERR_CUDA;
   const int64_t rows = L.slices * L.n;
   TcArgs a;
+  a.k = L.k;
   a.n = L.n;
   a.m = L.m;
   a.tiles_per_slice = (int)((L.n + RS - 1) / RS);
@@ -1095,10 +1149,10 @@ int launch(const FwdLaunch& L) {
   a.status = L.status;
   const int64_t grid = L.slices * a.tiles_per_slice;
   if (grid <= 0) return SDK_OK;
-  auto kern = fused_fwd_tc<T>;
+  auto kern = L.topk < 8 ? fused_fwd_tc<T, true> : fused_fwd_tc<T, false>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
     return SDK_ERR_CUDA;
-  const size_t need = (size_t)rows * (CAP * 4 + 4);
+  const size_t need = (size_t)rows * (CAP * 4 + 8);
   void* ws = L.workspace;
   const bool pooled = ws == nullptr;
   if (pooled) {
@@ -1108,8 +1162,11 @@ int launch(const FwdLaunch& L) {
   } else if (L.workspace_bytes < need || !aligned16(ws)) {
     return SDK_ERR_INVALID_ARGUMENT;
   }
+  // per row: CAP entries and a count; per slice (slices <= rows): a flag
   a.cand = static_cast<uint32_t*>(ws);
   a.cand_n = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + (size_t)rows * CAP * 4);
+  a.unsafe = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + (size_t)rows * (CAP * 4 + 4));
+  a.big16 = bf16 ? 0x5d80u : 0x7c00u;
   kern<<<(unsigned)grid, NT, SMEM_BYTES, L.stream>>>(tq, tk, a);
   int rc = cudaPeekAtLastError() == cudaSuccess ? SDK_OK : SDK_ERR_CUDA;
   if (rc == SDK_OK) {
@@ -1123,6 +1180,8 @@ int launch(const FwdLaunch& L) {
     f.top_scores = static_cast<float*>(L.top_scores);
     f.cand = a.cand;
     f.cand_n = a.cand_n;
+    f.unsafe = a.unsafe;
+    f.big16 = a.big16;
     f.rows = rows;
     f.n = L.n;
     f.m = L.m;
@@ -1154,7 +1213,7 @@ bool fwd_tensorcore_supports(const FwdLaunch& L) {
 size_t fwd_tensorcore_workspace(int64_t rows, int d, int dv, int topk, int dtype) {
   if (dtype != SDK_DTYPE_BF16 && dtype != SDK_DTYPE_F16) return 0;
   if (d != D || dv != D || topk > 64 || rows <= 0) return 0;
-  return (size_t)rows * (CAP * 4 + 4);
+  return (size_t)rows * (CAP * 4 + 8);
 }
 
 int fwd_tensorcore(const FwdLaunch& L) {

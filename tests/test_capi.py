@@ -75,7 +75,7 @@ def test_max_topk_covers_the_benchmark_configurations(dtype):
 
 def test_forward_workspace_size_follows_the_tensor_core_shapes():
     lib = _native.load()
-    per_row = 176 * 4 + 4  # candidate list and count per query row
+    per_row = 176 * 4 + 8  # candidate list, count and check word per query row
     for code in (_native.DTYPE_BF16, _native.DTYPE_F16):
         assert lib.sdk_topk_attn_fwd_workspace_size(1000, 64, 64, 64, code) == 1000 * per_row
         assert lib.sdk_topk_attn_fwd_workspace_size(3, 64, 64, 1, code) == 3 * per_row

@@ -399,7 +399,7 @@ def test_tensor_core_forward_on_caller_workspace_matches_library_pool():
         return rc, out, idx, lse
 
     need = lib.sdk_topk_attn_fwd_workspace_size(bh * n, d, d, k, _native.DTYPE_BF16)
-    assert need == bh * n * (176 * 4 + 4)
+    assert need == bh * n * (176 * 4 + 8)
     buf = torch.empty(need + 16, device=DEV, dtype=torch.uint8)
     rc0, o0, i0, l0 = run(None, 0, pooled=True)
     rc1, o1, i1, l1 = run(buf.data_ptr(), need)
@@ -408,6 +408,43 @@ def test_tensor_core_forward_on_caller_workspace_matches_library_pool():
     assert run(buf.data_ptr(), need - 1)[0] == _native.SDK_ERR_INVALID_ARGUMENT
     assert run(buf.data_ptr() + 4, need)[0] == _native.SDK_ERR_INVALID_ARGUMENT
     assert _native.device_status(clear=True) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_tensor_core_forward_unsafe_inputs_are_reselected_exactly(dtype):
+    # The fused stream filter assumes no score can overflow.  A query row
+    # holding NaN, a query row holding inf and, for bf16, a key slice holding
+    # a value of 2^100 fail the input check; those rows are re-selected
+    # exactly and must follow the reference order (NaN scores first, lower
+    # key index first on ties), the other rows take the fused path.
+    g = torch.Generator().manual_seed(23)
+    bh, n, m, d, k = 3, 300, 1000, 64, 16
+    q, kk = (torch.randn(bh, x, d, generator=g) for x in (n, m))
+    v = torch.randn(bh, m, d, generator=g)
+    q[0, 5, 3] = float("nan")
+    q[2, 7, 9] = float("inf")
+    if dtype == torch.bfloat16:
+        kk[1, 17, 0] = 2.0 ** 100
+    q, kk, v = (t.to(dtype) for t in (q, kk, v))
+    from sparsedict_b200 import _ops
+
+    out, idx, lse, _ = _ops.topk_attn_fwd(q.to(DEV), kk.to(DEV), v.to(DEV), k, 1 / 8)
+    assert _native.device_status(clear=True) == 0
+    got = idx.cpu().numpy().reshape(bh, n, k)
+    qf, kf, vf = (t.double().numpy() for t in (q, kk, v))
+    _, oi, _, _ = oracle.topk_attention_forward(qf, kf, vf, k, 1 / 8)
+    # the NaN row: every score NaN, so keys 0..k-1
+    assert sorted(got[0, 5]) == list(range(k))
+    scores = _oracle_scores64(qf, kf, 1 / 8)
+    finite = np.isfinite(scores).all(axis=-1)
+    exp = np.sort(oi.reshape(bh, n, k), axis=-1)
+    act = np.sort(got, axis=-1)
+    assert np.array_equal(act[~finite], exp[~finite])
+    _assert_indices(act[finite][None], exp[finite][None], scores[finite][None], tol=1e-4, ordered=False)
+    if dtype == torch.bfloat16:
+        # q·k of key 17 in slice 1 is about +-2^100·q[0]: first or excluded
+        top = (qf[1, :, 0] > 0)
+        assert (got[1][top] == 17).any(axis=-1).all()
 
 
 # --- tie stress (configuration 5 shape family, reduced size) ----------------------
