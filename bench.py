@@ -300,12 +300,13 @@ def run_native_arm(args):
 
     peaks = load_peaks()
     flops_tc, bytes_fb = roofline_terms(c["B"], c["H"], c["N"], c["M"], c["d"], c["k"], 2)
-    # dominant kernel: the fused forward (affinity MMA + selection + aggregate)
+    # dominant kernels: the forward (streaming kernel: affinity MMA + selection;
+    # finishing kernel: exact re-score, softmax, value gather), one call = two launches
     fwd_flops_per_launch = flops_tc / world
     achieved = fwd_flops_per_launch / (fwd_ms / 1000.0) / 1e12
     peak_tc = peaks["bf16_tflops_sustained"]
-    # ncu-measured DRAM bytes of one headline forward launch (profiles/traffic.json)
-    traffic = load_traffic().get("fused_fwd_cfg4") if (c["B"], c["H"], world) == (CFG["B"], CFG["H"], 1) else None
+    # ncu-measured DRAM bytes of one headline forward call (profiles/traffic.json)
+    traffic = load_traffic().get("forward_B16_H8_N16384_k64") if (c["B"], c["H"], world) == (CFG["B"], CFG["H"], 1) else None
     t_tensor = flops_tc / world / (peak_tc * 1e12)
     t_hbm = bytes_fb / world / (peaks["hbm_gbs"] * 1e9)
     t_roof = max(t_tensor, t_hbm)
