@@ -64,7 +64,12 @@ def load_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi samples (every 200 ms) while the timed region runs."""
+    """nvidia-smi samples (every 25 ms) while the timed region runs.
+
+    Entering waits (up to 5 s) for the sampler's first line and then drops it,
+    so every kept sample was taken inside the region; a multi-GPU step of a
+    few milliseconds still gets samples over a run of several steps.
+    """
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -79,9 +84,13 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "25"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            deadline = time.monotonic() + 5.0
+            while not self.lines and time.monotonic() < deadline and self.proc.poll() is None:
+                time.sleep(0.005)
+            self.lines.clear()
         except (OSError, ValueError):
             self.proc = None
         return self
