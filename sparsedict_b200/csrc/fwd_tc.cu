@@ -12,6 +12,8 @@
 //                for every K tile, each into one of two TMEM accumulators of
 //                its query tile, committing to "S full" / "stage free"
 //                mbarriers;
+//   warps 2, 3   in the first CTA of each slice: the input magnitude check
+//                of the slice's keys (below); idle elsewhere;
 //   warps 4..7   selection for tile A, warps 8..11 for tile B (two selection
 //                warps per SM sub-partition): thread i of a group owns query
 //                row i of its tile (TMEM lane i), reads its 128 scores of the
