@@ -317,12 +317,11 @@ int launch_d64(const BwdLaunch& L) {
   a.seg_len = 0;
   a.segs = 0;
   if (a.rows <= 0) return SDK_OK;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // One block per eight rows (not a resident grid-stride wave): blocks retire
+  // as they go, so kernels on other streams (the gradient exchange of an
+  // earlier bucket) get SMs while this one runs; measured no slower alone.
   const int64_t want = (a.rows + G8W - 1) / G8W;
-  const int64_t cap = (int64_t)sms * 4;
-  sparse_bwd_d64<T><<<(unsigned)(want < cap ? want : cap), G8W * kWarp, 0, L.stream>>>(a);
+  sparse_bwd_d64<T><<<(unsigned)want, G8W * kWarp, 0, L.stream>>>(a);
   return cudaPeekAtLastError() == cudaSuccess ? SDK_OK : SDK_ERR_CUDA;
 }
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }

@@ -117,7 +117,8 @@ class ShardedTopKAttention:
             self.stage_k = torch.zeros((full, m, d), device=self.device, dtype=dtype)
             self.stage_v = torch.zeros((full, m, dv), device=self.device, dtype=dtype)
         on_cuda = self.device.type == "cuda"
-        self.comm_stream = (torch.cuda.Stream(device=self.device)
+        # high priority: the exchange kernels take SMs as the backward's blocks retire
+        self.comm_stream = (torch.cuda.Stream(device=self.device, priority=-1)
                             if on_cuda and plan.world > 1 and reduce != "none" else None)
 
     def _bucket_ranges(self):
