@@ -38,7 +38,8 @@ WORKLOAD = "sharded bf16 fwd+bwd, B=16 H=8 N=M=16384 d=64 k=64"
 
 
 def roofline_terms(b, h, n, m, d, k, elem):
-    """Algorithmic work of one fwd+bwd over all slices (see DESIGN.md roofline)."""
+    """Algorithmic work of one fwd+bwd over all slices: the dense affinity flops and
+    the compulsory HBM bytes (read Q, K, V, dO; write O, dQ, dK, dV; indices and LSE)."""
     flops_tc = 2.0 * n * m * d * b * h  # the dense affinity, the only dense contraction
     bytes_fb = ((5 * n + 6 * m) * d * elem + 8 * n * (k + 1)) * b * h
     return flops_tc, bytes_fb
@@ -64,23 +65,70 @@ def load_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi samples (every 25 ms) while the timed region runs.
+    """SM clock and throttle-reason samples taken while the timed region runs.
 
-    Entering waits (up to 5 s) for the sampler's first line and then drops it,
-    so every kept sample was taken inside the region; a multi-GPU step of a
-    few milliseconds still gets samples over a run of several steps.
+    Polls NVML (read-only queries) every 2 ms from a thread, so that even a
+    timed region of a few milliseconds gets samples; falls back to
+    ``nvidia-smi --query-gpu`` every 25 ms when NVML is not importable.
+    Entering waits for the first sample and drops it, so every kept sample
+    was taken inside the region.
     """
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event-reason bits
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown"}
 
-    def __init__(self, index):
+    def __init__(self, index, device=None):
         self.index = index
+        self.device = device
         self.proc = None
         self.lines = []
+        self.samples = []  # (sm_mhz, max_mhz, reason_bits)
+        self._stop = threading.Event()
+        self._nvml = None
+
+    def _nvml_handle(self):
+        import pynvml
+
+        pynvml.nvmlInit()
+        handle = None
+        try:
+            import torch
+
+            bus = torch.cuda.get_device_properties(self.device).pci_bus_id
+            dom = torch.cuda.get_device_properties(self.device).pci_domain_id
+            dev = torch.cuda.get_device_properties(self.device).pci_device_id
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(f"{dom:08x}:{bus:02x}:{dev:02x}.0".encode())
+        except Exception:
+            handle = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+        reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        mx = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
+        return pynvml, handle, reasons, mx
+
+    def _poll(self):
+        nv, handle, reasons, mx = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(handle, nv.NVML_CLOCK_SM), mx, reasons(handle)))
+            except Exception:
+                pass
+            time.sleep(0.002)
 
     def __enter__(self):
+        try:
+            self._nvml = self._nvml_handle()
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            deadline = time.monotonic() + 5.0
+            while not self.samples and time.monotonic() < deadline:
+                time.sleep(0.001)
+            self.samples.clear()
+            return self
+        except Exception:
+            self._nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
@@ -100,6 +148,9 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        self._stop.set()
+        if self._nvml is not None:
+            self.thread.join(timeout=1)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -109,6 +160,12 @@ class ClockSampler:
 
     def summary(self):
         sm, mx, reasons = [], None, set()
+        for clk, cmax, bits in self.samples:
+            sm.append(float(clk))
+            mx = float(cmax)
+            for bit, name in self.REASONS.items():
+                if bits & bit:
+                    reasons.add(name)
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.lines:
             parts = [p.strip() for p in line.split(",")]
@@ -122,9 +179,11 @@ class ClockSampler:
             for name, flag in zip(names, parts[5:9]):
                 if flag.lower() == "active":
                     reasons.add(name)
+        src = "nvml" if self._nvml is not None else "nvidia-smi"
         if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0, "source": src}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+                "source": src}
 
 
 # ----------------------------------------------------------------- CPU arms --
@@ -182,13 +241,159 @@ def run_reference_arm(args):
 # ----------------------------------------------------------------- GPU arm --
 
 
+def run_e2e(args, c, world, dev, runner, tensors, barrier, total_queries):
+    """Same metric end to end through the public API, host buffers on both sides.
+
+    Every step copies its inputs (this rank's query and upstream-gradient
+    rows, the replicated keys and values) from pinned host memory, runs the
+    forward and backward, and copies every result (output and dQ rows, dK,
+    dV) back into pinned host memory.  Input copies of step i+1 run on a copy
+    stream while step i computes; result copies of step i run on a third
+    stream while step i+1 computes.  At one GPU the API is
+    ``fused_topk_attention`` + autograd, at several the sharded step
+    (``ShardedTopKAttention.step``).
+    """
+    import torch
+    import torch.distributed as dist
+
+    from sparsedict_b200 import fused_topk_attention
+
+    host = [t.cpu().pin_memory() for t in tensors]
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    main = torch.cuda.current_stream(dev)
+    copy_stream = torch.cuda.Stream(device=dev)
+    back_stream = torch.cuda.Stream(device=dev)
+    bufs = [[torch.empty_like(t, device=dev) for t in host] for _ in range(2)]
+    copied = [torch.cuda.Event() for _ in range(2)]
+    consumed = [torch.cuda.Event() for _ in range(2)]
+    q_rows, keys, values, dout_rows = tensors
+    # pinned result buffers: out and dQ of this rank's rows, dK and dV
+    res_host = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in (q_rows, q_rows, keys, values)]
+    d2h = sum(t.numel() * t.element_size() for t in res_host)
+
+    def issue_copy(slot):
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(consumed[slot])
+            for dst, src in zip(bufs[slot], host):
+                dst.copy_(src, non_blocking=True)
+            copied[slot].record(copy_stream)
+
+    def compute(slot):
+        main.wait_event(copied[slot])
+        qd, kd, vd, dod = bufs[slot]
+        if world == 1:
+            qd4, kd4, vd4 = (x.view(c["B"], c["H"], -1, c["d"]).requires_grad_(True) for x in (qd, kd, vd))
+            out = fused_topk_attention(qd4, kd4, vd4, c["k"])
+            dq, dk, dv = torch.autograd.grad(out, (qd4, kd4, vd4), dod.view_as(out))
+        else:
+            out, dq, dk, dv = runner.step(qd, kd, vd, dod)
+        consumed[slot].record(main)
+        results = (out, dq, dk, dv)
+        back_stream.wait_stream(main)
+        with torch.cuda.stream(back_stream):
+            for dst, src in zip(res_host, results):
+                dst.copy_(src.reshape(dst.shape), non_blocking=True)
+        for t in results:
+            t.record_stream(back_stream)
+
+    def run(steps):
+        for ev in consumed:
+            ev.record(main)
+        issue_copy(0)
+        for i in range(steps):
+            if i + 1 < steps:
+                issue_copy((i + 1) % 2)
+            compute(i % 2)
+        back_stream.synchronize()
+
+    run(max(1, args.warmup))
+    barrier()
+    t0 = time.perf_counter()
+    run(args.e2e_steps)
+    barrier()
+    e2e_s = torch.tensor([time.perf_counter() - t0], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
+    return {"value": total_queries * args.e2e_steps / float(e2e_s[0]), "unit": UNIT,
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": args.e2e_steps,
+            "note": "public API; every step copies its inputs from pinned host memory and copies out, dQ, dK "
+                    "and dV back into pinned host memory (input copies overlap the previous step's compute, "
+                    "result copies the next step's); bytes are per rank"}
+
+
+def check_parity(c, world, rank, dev, plan, runner, keys, values, q_rows, dout_rows, rows=256):
+    """Sharded results against a one-process recomputation, outside the timed region.
+
+    Each rank recomputes one of its own slices, and (at several GPUs) one
+    slice of the next rank — whose query and gradient rows it regenerates
+    from that rank's seed — with the single-GPU public API
+    (``fused_topk_attention`` + autograd on that slice alone), and compares
+    sampled rows of the sharded step's output and dQ (own slice) and of the
+    all-reduced dK and dV (both slices).  The forward must match bit for bit;
+    gradients within the bf16 tolerance.  All ranks take part in the same
+    reductions, so the verdict is global.
+    """
+    import torch
+    import torch.distributed as dist
+
+    from sparsedict_b200 import fused_topk_attention
+
+    out, dq, dk, dv = runner.step(q_rows, keys, values, dout_rows)
+    torch.cuda.synchronize(dev)
+    gen = torch.Generator(device=dev)
+    sel = torch.Generator().manual_seed(7)
+    worst = {"out": 0.0, "dq": 0.0, "dk": 0.0, "dv": 0.0}
+    exact_out = True
+    checked = []
+    owners = [rank] + ([(rank + 1) % world] if world > 1 else [])
+    for owner in owners:
+        local = 0 if owner == rank else plan.per_rank - 1
+        s = plan.global_slice(local, owner)
+        if owner == rank:
+            qs, dos = q_rows[local], dout_rows[local]
+        else:
+            gen.manual_seed(1234 + 1000 * (owner + 1))
+            qa = torch.randn(plan.per_rank, c["N"], c["d"], device=dev, generator=gen).to(q_rows.dtype)
+            da = torch.randn(plan.per_rank, c["N"], c["d"], device=dev, generator=gen).to(q_rows.dtype)
+            qs, dos = qa[local], da[local]
+        q4, k4, v4 = (t.reshape(1, 1, -1, c["d"]).clone().requires_grad_(True) for t in (qs, keys[s], values[s]))
+        ref_out = fused_topk_attention(q4, k4, v4, c["k"])
+        rdq, rdk, rdv = torch.autograd.grad(ref_out, (q4, k4, v4), dos.reshape(ref_out.shape))
+        r_idx = torch.randperm(c["N"], generator=sel)[:rows].to(dev)
+        k_idx = torch.randperm(c["M"], generator=sel)[:rows].to(dev)
+
+        def err(a, b):
+            a, b = a.float(), b.float()
+            return float((a - b).abs().max()) / max(1.0, float(b.abs().max()))
+
+        if owner == rank:
+            got_out = out[local][r_idx]
+            exact_out &= bool(torch.equal(got_out, ref_out.reshape(-1, c["d"])[r_idx]))
+            worst["out"] = max(worst["out"], err(got_out, ref_out.reshape(-1, c["d"])[r_idx]))
+            worst["dq"] = max(worst["dq"], err(dq[local][r_idx], rdq.reshape(-1, c["d"])[r_idx]))
+        dks, dvs = (dk[s], dv[s]) if runner.reduce != "none" else (dk[local], dv[local])
+        if runner.reduce != "none" or owner == rank:
+            worst["dk"] = max(worst["dk"], err(dks[k_idx], rdk.reshape(-1, c["d"])[k_idx]))
+            worst["dv"] = max(worst["dv"], err(dvs[k_idx], rdv.reshape(-1, c["d"])[k_idx]))
+        checked.append(s)
+    t = torch.tensor([worst["out"], worst["dq"], worst["dk"], worst["dv"], 0.0 if exact_out else 1.0],
+                     device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    worst = dict(zip(("out", "dq", "dk", "dv"), (float(x) for x in t[:4])))
+    ok = float(t[4]) == 0.0 and all(v <= 2e-2 for v in worst.values())
+    return {"ok": ok, "forward_bit_exact": float(t[4]) == 0.0, "max_rel_err": worst, "tolerance": 2e-2,
+            "checked": f"{rows} sampled rows of out/dQ (own slice) and of dK/dV (own slice"
+                       + (" and one slice of the next rank" if world > 1 else "") + ") against the single-GPU "
+                       "public API on that slice alone"}
+
+
 def run_native_arm(args):
     import torch
     import torch.distributed as dist
 
     from sparsedict_b200 import _native
-    from sparsedict_b200 import fused_topk_attention
-    from sparsedict_b200.sharded import ShardedTopKAttention, ShardPlan
+    from sparsedict_b200.sharded import ShardedTopKAttention, ShardPlan, pick_buckets
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -207,7 +412,7 @@ def run_native_arm(args):
 
     c = dict(CFG, B=args.batch, H=args.heads)
     slices = c["B"] * c["H"]
-    plan = ShardPlan(slices, world, rank)
+    plan = ShardPlan(slices, world, rank, buckets=pick_buckets(slices, world, args.buckets) if world > 1 else 1)
     gen = torch.Generator(device=dev).manual_seed(1234)
     dtype = torch.bfloat16
     keys = torch.randn(slices, c["M"], c["d"], device=dev, generator=gen).to(dtype)
@@ -216,7 +421,7 @@ def run_native_arm(args):
     q_rows = torch.randn(plan.per_rank, c["N"], c["d"], device=dev, generator=gen).to(dtype)
     dout_rows = torch.randn(plan.per_rank, c["N"], c["d"], device=dev, generator=gen).to(dtype)
     runner = ShardedTopKAttention(plan, c["M"], c["d"], c["d"], c["k"], dtype, dev, group=group,
-                                  reduce=args.reduce, buckets=args.buckets)
+                                  reduce=args.reduce)
 
     def barrier():
         if world > 1:
@@ -228,10 +433,9 @@ def run_native_arm(args):
     barrier()
 
     stream = torch.cuda.current_stream(dev)
-    fwd_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                  for _ in range(args.steps)]
+    fwd_events = [[] for _ in range(args.steps)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    with ClockSampler(local, dev) as clocks:
         barrier()
         start.record(stream)
         for i in range(args.steps):
@@ -239,7 +443,8 @@ def run_native_arm(args):
         stop.record(stream)
         barrier()
     elapsed = start.elapsed_time(stop) / 1000.0
-    fwd_ms = statistics.mean(a.elapsed_time(b) for a, b in fwd_events)
+    # forward time per step: the sum over the step's buckets
+    fwd_ms = statistics.mean(sum(a.elapsed_time(b) for a, b in evs) for evs in fwd_events)
     t = torch.tensor([elapsed, fwd_ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -255,57 +460,11 @@ def run_native_arm(args):
     # buffer sets while step i computes, as a training loader would.
     e2e = None
     if not args.skip_e2e:
-        host = [t.cpu().pin_memory() for t in (q_rows, keys, values, dout_rows)]
-        h2d = sum(t.numel() * t.element_size() for t in host)
-        main = torch.cuda.current_stream(dev)
-        copy_stream = torch.cuda.Stream(device=dev)
-        bufs = [[torch.empty_like(t, device=dev) for t in host] for _ in range(2)]
-        copied = [torch.cuda.Event() for _ in range(2)]
-        consumed = [torch.cuda.Event() for _ in range(2)]
+        e2e = run_e2e(args, c, world, dev, runner, (q_rows, keys, values, dout_rows), barrier, total_queries)
 
-        def issue_copy(slot):
-            with torch.cuda.stream(copy_stream):
-                copy_stream.wait_event(consumed[slot])
-                for dst, src in zip(bufs[slot], host):
-                    dst.copy_(src, non_blocking=True)
-                copied[slot].record(copy_stream)
-
-        def compute(slot):
-            main.wait_event(copied[slot])
-            qd, kd, vd, dod = bufs[slot]
-            if world == 1:
-                qd4, kd4, vd4 = (x.view(c["B"], c["H"], -1, c["d"]).requires_grad_(True) for x in (qd, kd, vd))
-                out = fused_topk_attention(qd4, kd4, vd4, c["k"])
-                torch.autograd.grad(out, (qd4, kd4, vd4), dod.view_as(out))
-                res = (out.float() * dod.view_as(out).float()).sum()
-            else:
-                out, dq, dk, dv = runner.step(qd, kd, vd, dod)
-                res = (out.float() * dod.float()).sum()
-            consumed[slot].record(main)
-            return res
-
-        def run(steps):
-            for ev in consumed:
-                ev.record(main)
-            issue_copy(0)
-            for i in range(steps):
-                if i + 1 < steps:
-                    issue_copy((i + 1) % 2)
-                compute(i % 2).cpu()
-
-        run(max(1, args.warmup))
-        barrier()
-        t0 = time.perf_counter()
-        run(args.e2e_steps)
-        barrier()
-        e2e_s = torch.tensor([time.perf_counter() - t0], device=dev, dtype=torch.float64)
-        if world > 1:
-            dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
-        e2e = {"value": total_queries * args.e2e_steps / float(e2e_s[0]), "unit": UNIT,
-               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4,
-               "note": "public API; every step copies its inputs from pinned host memory (on a second stream, "
-                       "overlapping the previous step's compute) and reads a scalar result back"}
-        del host, bufs
+    parity = None
+    if not args.skip_parity:
+        parity = check_parity(c, world, rank, dev, plan, runner, keys, values, q_rows, dout_rows)
 
     peaks = load_peaks()
     flops_tc, bytes_fb = roofline_terms(c["B"], c["H"], c["N"], c["M"], c["d"], c["k"], 2)
@@ -335,14 +494,14 @@ def run_native_arm(args):
                      # compulsory fwd+bwd bytes at the HBM peak
                      "step_frac_tensor": t_tensor / (ms_per_step / 1000.0),
                      "step_frac_hbm": t_hbm / (ms_per_step / 1000.0)},
-        # this library's kernels per step: the forward (stream + finish kernels), one
-        # backward per bucket, and two conversions per bucket (bucket-major all-reduce)
-        # or two in all
-        "gpu_launches": (2 + len(runner._bucket_ranges()) * (3 if runner._bucket_major else 1)
-                         + (0 if runner._bucket_major else 2)) * args.steps,
+        # this library's kernels per step: per bucket the forward (stream + finishing
+        # kernel) and the backward (row, transpose and key kernel)
+        "gpu_launches": runner.launches_per_step * args.steps,
     }
     if e2e is not None:
         line["e2e"] = e2e
+    if parity is not None:
+        line["parity"] = parity
     if rank == 0 and not args.skip_cpu:
         r, s, desc = cpu_reference_sample(rows=args.ref_rows)
         rates = [r]
@@ -376,6 +535,7 @@ def main():
     ap.add_argument("--ref-rows", type=int, default=256)
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-parity", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -58,8 +58,20 @@ int sdk_max_topk(int32_t dtype, int32_t d);
 
 /* Reads the device status word of the current device into *bits (bit 1: an
  * index outside [0, m) was met and skipped; bit 2: a bounded wait gave up),
- * clearing it when `clear` is nonzero.  Synchronises `stream`. */
+ * clearing it when `clear` is nonzero.  Synchronises `stream`.  A forward
+ * whose wait gave up writes NaN outputs and LSE and index -1 for the rows it
+ * could not finish; callers that must not consume those poll this after a
+ * forward. */
 int sdk_device_status(unsigned int* bits, int32_t clear, void* stream);
+
+/* Bound, in nanoseconds, of every pipeline wait of the tensor-core forward
+ * (launches made after the call; process-wide).  0 restores the default of
+ * 2 s; values above 60 s are refused.  A wait that runs out makes its CTA
+ * stop, let its in-flight copies land (those waits keep the 2 s bound), mark
+ * its rows as given up and raise device status bit 2: the kernel returns and
+ * the context stays usable.  No counterpart in the reference (Triton kernels
+ * have no bounded waits); used to check that path without a GPU fault. */
+int sdk_set_wait_limit(uint64_t ns);
 
 /*
  * Fused forward, stages 1-3: scaled affinity q·kᵀ, per-row top-k selection
@@ -88,16 +100,17 @@ int sdk_topk_attn_fwd(const void* q, const void* k, const void* v, void* out, in
 
 /*
  * Scratch of the forward: the bf16/fp16 tensor-core path (d = dv = 64,
- * topk <= 64) hands each query row's candidate list (176 four-byte entries and
- * a count) from its streaming kernel to its finishing kernel.  Returns the
- * bytes for `rows` query rows (slices*n, or the grouped row count), 0 when the
- * shape never takes that path.  The reference's wrapper allocates its
- * intermediate top-k buffers with torch (fused_topk_attn.py:1012-1017);
- * callers that own their memory allocate this and pass it to
- * sdk_topk_attn_fwd_ws.
+ * topk <= 64, m <= 65536, score_grid 0, uniform slices) hands each query row's
+ * candidate list (160 four-byte entries and a count) from its streaming
+ * kernel to its finishing kernel.  Returns the bytes for `rows` query rows
+ * (slices*n, or the grouped row count), 0 when the call will not take that
+ * path (`grouped`: row_offsets or row_index will be passed).  The reference's
+ * wrapper allocates its intermediate top-k buffers with torch
+ * (fused_topk_attn.py:1012-1017); callers that own their memory allocate this
+ * and pass it to sdk_topk_attn_fwd_ws.
  */
-size_t sdk_topk_attn_fwd_workspace_size(int64_t rows, int32_t d, int32_t dv, int32_t topk,
-                                        int32_t dtype);
+size_t sdk_topk_attn_fwd_workspace_size(int64_t rows, int64_t m, int32_t d, int32_t dv, int32_t topk,
+                                        int32_t score_grid, int32_t grouped, int32_t dtype);
 
 /*
  * sdk_topk_attn_fwd on caller scratch: `workspace` (16-byte aligned, at least
@@ -166,6 +179,41 @@ int sdk_topk_attn_bwd_biased(const void* q, const void* k, const void* v, const 
                              const void* seg_bias, void* dseg_bias, int64_t seg_len, int32_t segs,
                              int32_t dtype, void* stream);
 
+/*
+ * Scratch bytes of sdk_topk_attn_bwd_direct for `rows` query rows (slices*n,
+ * or the grouped row count with `grouped` nonzero), assuming 16-byte aligned
+ * tensors: the key-major kernels' per-row statistics and per-key row lists
+ * when the shape takes them (bf16/fp16, d = dv = 64, topk <= 64,
+ * m <= 16384, at most 65535 rows per slice — grouped: in all, score_grid 0),
+ * else fp32 (fp64) dK/dV accumulators.  0 for invalid sizes.
+ */
+size_t sdk_topk_attn_bwd_workspace_size(int64_t rows, int64_t slices, int64_t m, int32_t d, int32_t dv,
+                                        int32_t topk, int32_t score_grid, int32_t grouped, int32_t dtype);
+
+/*
+ * The backward written straight into output-dtype gradients: dq [rows, d],
+ * dk [slices, m, d] and dv [slices, m, dv_dim], all in `dtype` (the
+ * reference returns dq·scale, dk·scale and dv in the input dtype,
+ * kernels/fused_topk_attn.py:1195-1201).  dk == dv is allowed (d == dv_dim):
+ * it then receives dK + dV (keys and values that are one dictionary).
+ *
+ * On the shapes of sdk_topk_attn_bwd_workspace_size's key-major case it runs
+ * the deterministic key-major kernels: dq by a gathered contraction per query
+ * row, dK/dV per key over the rows that selected it, in ascending row order —
+ * no atomics, so the result is bit-identical from run to run, and every
+ * element is written once (keys no row selected get zeros).  Other shapes
+ * run the scatter kernel of sdk_topk_attn_bwd into accumulators in the
+ * workspace and convert.  `workspace`: 256-byte aligned, at least
+ * sdk_topk_attn_bwd_workspace_size bytes; SDK_ERR_INVALID_ARGUMENT otherwise.
+ * Index -1 (a forward row given up on) contributes nothing.
+ */
+int sdk_topk_attn_bwd_direct(const void* q, const void* k, const void* v, const void* dout,
+                             const int32_t* top_idx, const void* lse, void* dq, void* dk, void* dv,
+                             const int32_t* row_offsets, const int32_t* row_index, int64_t slices,
+                             int64_t n, int64_t m, int32_t d, int32_t dv_dim, int32_t topk, double scale,
+                             int32_t score_grid, int32_t dtype, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
 /* Capacity, in fp32 elements (16 MiB), of the library-owned scratch array
  * that sdk_topk_attn_bwd_noalloc accumulates dK and dV in. */
 #define SDK_NOALLOC_SCRATCH_FLOATS (4u * 1024u * 1024u)
@@ -187,9 +235,10 @@ int sdk_topk_attn_bwd_biased(const void* q, const void* k, const void* v, const 
  * slices*m*(d+dv_dim) <= SDK_NOALLOC_SCRATCH_FLOATS is refused with
  * SDK_ERR_TOO_LARGE before anything runs.  The call allocates nothing.
  *
- * The first call on each device looks up that array's device address
- * (cudaGetSymbolAddress, with the device current); make that first call
- * before any stream capture.  All calls share the one array: each clears the
+ * Every call looks up that array's device address (cudaGetSymbolAddress,
+ * with the call's device current) before it launches anything; the first
+ * call on a device also loads the library's device code there, so make that
+ * first call before any stream capture.  All calls share the one array: each clears the
  * part it uses before accumulating, and calls that overlap on the GPU (on
  * different streams or from different host threads) race on it.
  */

@@ -60,6 +60,7 @@ __all__ = [
     "gated_mixture_forward",
     "gated_mixture_backward",
     "gap_aware_index_mismatches",
+    "index_mismatch_counts",
 ]
 
 
@@ -447,6 +448,13 @@ def gated_mixture_backward(
 def gap_aware_index_mismatches(
     actual: np.ndarray, expected: np.ndarray, scores: np.ndarray, tol: float, ordered: bool = True
 ) -> int:
+    """Number of failing rows of ``index_mismatch_counts``."""
+    return index_mismatch_counts(actual, expected, scores, tol, ordered)[0]
+
+
+def index_mismatch_counts(
+    actual: np.ndarray, expected: np.ndarray, scores: np.ndarray, tol: float, ordered: bool = True
+) -> tuple[int, int]:
     """Count rows whose selected sets differ by more than a near-tie.
 
     A row passes when the index lists are equal, or when every key that is
@@ -454,7 +462,7 @@ def gap_aware_index_mismatches(
     oracle's k-th selected score (a flip inside the rounding noise of two
     different summation orders).  With ``ordered=False`` only the selected
     sets are compared (for kernels that return the top-k set unsorted).
-    Returns the number of failing rows.
+    Returns ``(failing rows, rows that differ but pass as near-ties)``.
     """
     act = actual.reshape(-1, actual.shape[-1]).astype(np.int64)
     exp = expected.reshape(-1, expected.shape[-1]).astype(np.int64)
@@ -464,7 +472,8 @@ def gap_aware_index_mismatches(
         exp_sorted = np.sort(exp, axis=1)
         differ = np.any(act != exp_sorted, axis=1)
         bad = 0
-        for r in np.nonzero(differ)[0]:
+        rows = np.nonzero(differ)[0]
+        for r in rows:
             diff = list(set(act[r].tolist()) ^ set(exp[r].tolist()))
             if any(i < 0 or i >= sc.shape[1] for i in diff):
                 bad += 1
@@ -472,9 +481,10 @@ def gap_aware_index_mismatches(
             boundary = np.min(sc[r, exp[r]])
             if not np.all(np.abs(sc[r, diff] - boundary) <= tol):
                 bad += 1
-        return bad
+        return bad, len(rows) - bad
     bad = 0
-    for r in np.nonzero(np.any(act != exp, axis=1))[0]:
+    rows = np.nonzero(np.any(act != exp, axis=1))[0]
+    for r in rows:
         a, e = set(act[r].tolist()), set(exp[r].tolist())
         boundary = sc[r, exp[r, -1]]
         diff = list(a ^ e)
@@ -491,4 +501,4 @@ def gap_aware_index_mismatches(
         if np.all(np.abs(sc[r, diff] - boundary) <= tol):
             continue
         bad += 1
-    return bad
+    return bad, len(rows) - bad

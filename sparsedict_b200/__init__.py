@@ -18,10 +18,16 @@ from .kernels.fused_topk_attn import (
     tiled_topk_aggregate,
 )
 from .kernels.hybrid_topk import _hybrid_topk_attention_with_aux, hybrid_topk_attention
+from ._ops import deterministic_backward, set_deterministic_backward
 from .mixture import GatedMixtureFunction, gated_mixture_attention
+from .sharded import ShardedTopKAttention, ShardPlan
 
 __all__ = [
     "FusedTopKAttentionFunction",
+    "ShardPlan",
+    "ShardedTopKAttention",
+    "deterministic_backward",
+    "set_deterministic_backward",
     "GatedMixtureFunction",
     "gated_mixture_attention",
     "fused_topk_attention",

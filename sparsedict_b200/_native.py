@@ -37,8 +37,9 @@ SIGNATURES = {
     "sdk_last_cuda_error": [],
     "sdk_max_topk": [_i32, _i32],
     "sdk_device_status": [ctypes.POINTER(ctypes.c_uint), _i32, _p],
+    "sdk_set_wait_limit": [ctypes.c_uint64],
     "sdk_topk_attn_fwd": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _i32, _f64, _i32, _i32, _p],
-    "sdk_topk_attn_fwd_workspace_size": [_i64, _i32, _i32, _i32, _i32],
+    "sdk_topk_attn_fwd_workspace_size": [_i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32],
     "sdk_topk_attn_fwd_ws": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _i32, _f64, _i32, _i32,
                              _p, ctypes.c_size_t, _p],
     "sdk_topk_attn_bwd": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _i32, _f64, _i32,
@@ -48,6 +49,9 @@ SIGNATURES = {
     "sdk_topk_attn_bwd_biased": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _i32, _f64,
                                  _i32, _i32, _p, _p, _i64, _i32, _i32, _p],
     "sdk_finalize_grad": [_p, _p, _i64, _f64, _i32, _p],
+    "sdk_topk_attn_bwd_workspace_size": [_i64, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32],
+    "sdk_topk_attn_bwd_direct": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _i32,
+                                 _f64, _i32, _i32, _p, ctypes.c_size_t, _p],
     "sdk_topk_attn_bwd_noalloc": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _i32, _f64, _i32, _p],
     "sdk_affinity": [_p, _p, _p, _i64, _i64, _i32, _i64, _i64, _i32, _p],
     "sdk_topk_select": [_p, _p, _p, _i64, _i64, _i64, _i32, _i32, _p],
@@ -55,7 +59,7 @@ SIGNATURES = {
     "sdk_route_top1": [_p, _i64, _i32, _p, _p, _p, _p],
 }
 _RESTYPES = {"sdk_status_string": ctypes.c_char_p, "sdk_last_cuda_error": ctypes.c_char_p,
-             "sdk_topk_attn_fwd_workspace_size": ctypes.c_size_t}
+             "sdk_topk_attn_fwd_workspace_size": ctypes.c_size_t, "sdk_topk_attn_bwd_workspace_size": ctypes.c_size_t}
 
 _lock = threading.Lock()
 _lib = None
@@ -135,3 +139,8 @@ def device_status(clear: bool = True, device: torch.device | None = None) -> int
     with torch.cuda.device(device):
         call("sdk_device_status", ctypes.byref(bits), int(clear), stream_of(device))
     return int(bits.value)
+
+
+def set_wait_limit(ns: int) -> None:
+    """Bound (ns) of each pipeline wait of the tensor-core forward; 0 restores 2 s."""
+    call("sdk_set_wait_limit", int(ns))

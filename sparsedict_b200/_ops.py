@@ -13,6 +13,26 @@ import torch
 from . import _native as nat
 
 
+_deterministic = False
+
+
+def set_deterministic_backward(flag: bool) -> None:
+    """Choose the backward used for gradients in the input dtype.
+
+    ``False`` (default): the scatter kernel — dK/dV accumulated with fp32
+    vector atomics (fastest; summation order, hence the last bits of dK/dV,
+    may vary from run to run).  ``True``: the key-major kernels — every
+    gradient element written once in a fixed order, bit-identical from run
+    to run (bf16/fp16 with d = dv = 64; other shapes always scatter).
+    """
+    global _deterministic
+    _deterministic = bool(flag)
+
+
+def deterministic_backward() -> bool:
+    return _deterministic
+
+
 def acc_dtype(dtype: torch.dtype) -> torch.dtype:
     """Accumulator / LSE dtype for an input dtype."""
     return torch.float64 if dtype == torch.float64 else torch.float32
@@ -61,7 +81,8 @@ def topk_attn_fwd(
         if seg_bias is None:
             # scratch from torch's allocator, like every other buffer of the op
             code = nat.TORCH_TO_SDK[q2.dtype]
-            nbytes = int(nat.load().sdk_topk_attn_fwd_workspace_size(rows, d, dv, topk, code))
+            nbytes = int(nat.load().sdk_topk_attn_fwd_workspace_size(
+                rows, m, d, dv, topk, int(score_grid), int(row_offsets is not None or row_index is not None), code))
             ws = torch.empty((nbytes,), device=dev, dtype=torch.uint8) if nbytes else None
             nat.call("sdk_topk_attn_fwd_ws", *head, code, nat.ptr(ws), nbytes, nat.stream_of(dev))
         else:
@@ -118,6 +139,104 @@ def topk_attn_bwd(
             nat.call("sdk_topk_attn_bwd_biased", *head, seg_bias.data_ptr(), nat.ptr(dseg_bias), m // segs, segs,
                      nat.TORCH_TO_SDK[q2.dtype], nat.stream_of(dev))
     return dq, dk_acc, dv_acc
+
+
+def topk_attn_bwd_direct(
+    q2: torch.Tensor,
+    k2: torch.Tensor,
+    v2: torch.Tensor,
+    dout2: torch.Tensor,
+    top_idx: torch.Tensor,
+    lse: torch.Tensor,
+    scale: float,
+    *,
+    score_grid: int = 0,
+    row_offsets: torch.Tensor | None = None,
+    row_index: torch.Tensor | None = None,
+    dq: torch.Tensor | None = None,
+    dk: torch.Tensor | None = None,
+    dv: torch.Tensor | None = None,
+    shared_kv: bool = False,
+):
+    """Backward straight into input-dtype gradients; returns ``(dq, dk, dv)``.
+
+    bf16/fp16 with d = dv = 64 and k <= 64 run the deterministic key-major
+    kernels (bit-identical from run to run, no accumulators); other shapes
+    scatter into fp32/fp64 accumulators inside the workspace and convert.
+    ``shared_kv``: keys and values are one tensor and ``dk`` (= ``dv``)
+    receives dK + dV.
+    """
+    slices, m, d = k2.shape
+    dvd = v2.shape[-1]
+    topk = top_idx.shape[-1]
+    grouped = row_offsets is not None
+    n = q2.shape[-2] if not grouped else q2.reshape(-1, d).shape[0]
+    rows = n if grouped else slices * n
+    dev = q2.device
+    if dq is None:
+        dq = torch.empty_like(q2)
+    if dk is None:
+        dk = torch.empty((slices, m, d), device=dev, dtype=q2.dtype)
+    if shared_kv:
+        dv = dk
+    elif dv is None:
+        dv = torch.empty((slices, m, dvd), device=dev, dtype=q2.dtype)
+    code = nat.TORCH_TO_SDK[q2.dtype]
+    lib = nat.load()
+    nbytes = int(lib.sdk_topk_attn_bwd_workspace_size(rows, slices, m, d, dvd, topk, int(score_grid), int(grouped),
+                                                      code))
+    ws = torch.empty((nbytes + 256,), device=dev, dtype=torch.uint8)
+    base = ws.data_ptr()
+    aligned = (base + 255) // 256 * 256
+    with torch.cuda.device(dev):
+        nat.call("sdk_topk_attn_bwd_direct", q2.data_ptr(), k2.data_ptr(), v2.data_ptr(), dout2.data_ptr(),
+                 top_idx.data_ptr(), lse.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                 nat.ptr(row_offsets), nat.ptr(row_index), slices, n, m, d, dvd, topk, float(scale),
+                 int(score_grid), code, aligned, nbytes, nat.stream_of(dev))
+    return dq, dk, dv
+
+
+def topk_attn_bwd_out(
+    q2: torch.Tensor,
+    k2: torch.Tensor,
+    v2: torch.Tensor,
+    dout2: torch.Tensor,
+    top_idx: torch.Tensor,
+    lse: torch.Tensor,
+    scale: float,
+    *,
+    score_grid: int = 0,
+    row_offsets: torch.Tensor | None = None,
+    row_index: torch.Tensor | None = None,
+    dq: torch.Tensor | None = None,
+    dk: torch.Tensor | None = None,
+    dv: torch.Tensor | None = None,
+    shared_kv: bool = False,
+):
+    """Backward into input-dtype ``(dq, dk, dv)`` by the selected kernel
+    (``set_deterministic_backward``): the key-major kernels, or the scatter
+    kernel into fp32/fp64 accumulators followed by one conversion."""
+    if _deterministic:
+        return topk_attn_bwd_direct(q2, k2, v2, dout2, top_idx, lse, scale, score_grid=score_grid,
+                                    row_offsets=row_offsets, row_index=row_index, dq=dq, dk=dk, dv=dv,
+                                    shared_kv=shared_kv)
+    slices, m, d = k2.shape
+    dvd = v2.shape[-1]
+    acc = acc_dtype(q2.dtype)
+    dk_acc = torch.empty((slices, m, d), device=q2.device, dtype=acc)
+    dv_acc = dk_acc if shared_kv else torch.empty((slices, m, dvd), device=q2.device, dtype=acc)
+    dq, dk_acc, dv_acc = topk_attn_bwd(q2, k2, v2, dout2, top_idx, lse, scale, score_grid=score_grid,
+                                       dk_acc=dk_acc, dv_acc=dv_acc, row_offsets=row_offsets,
+                                       row_index=row_index, dq=dq)
+    if dk is None:
+        dk = torch.empty((slices, m, d), device=q2.device, dtype=q2.dtype)
+    finalize_grad(dk_acc, q2.dtype, out=dk)
+    if shared_kv:
+        return dq, dk, dk
+    if dv is None:
+        dv = torch.empty((slices, m, dvd), device=q2.device, dtype=q2.dtype)
+    finalize_grad(dv_acc, q2.dtype, out=dv)
+    return dq, dk, dv
 
 
 def finalize_grad(acc: torch.Tensor, dtype: torch.dtype, multiplier: float = 1.0,

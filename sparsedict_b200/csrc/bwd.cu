@@ -320,13 +320,17 @@ int launch_d64(const BwdLaunch& L) {
   // One block per eight rows (not a resident grid-stride wave): blocks retire
   // as they go, so kernels on other streams (the gradient exchange of an
   // earlier bucket) get SMs while this one runs; measured no slower alone.
+  // (the kernel walks its rows grid-stride, so a clamped grid stays correct)
   const int64_t want = (a.rows + G8W - 1) / G8W;
-  sparse_bwd_d64<T><<<(unsigned)want, G8W * kWarp, 0, L.stream>>>(a);
+  const unsigned grid = (unsigned)(want < 0x7fffffff ? want : 0x7fffffff);
+  sparse_bwd_d64<T><<<grid, G8W * kWarp, 0, L.stream>>>(a);
   return cudaPeekAtLastError() == cudaSuccess ? SDK_OK : SDK_ERR_CUDA;
 }
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 bool d64_supported(const BwdLaunch& L) {
+  const int64_t rows = L.row_offsets ? L.n : L.slices * L.n;
+  if (rows > 0x7fffff00) return false;  // row indices and row * topk stay in range
   return (L.dtype == SDK_DTYPE_BF16 || L.dtype == SDK_DTYPE_F16) && L.d == 64 && L.dv == 64 && L.topk <= 64 &&
          L.score_grid == 0 && !L.seg_bias && !L.dseg_bias && aligned16(L.q) && aligned16(L.k) &&
          aligned16(L.v) && aligned16(L.dout) && aligned16(L.dq) && aligned16(L.dk_acc) && aligned16(L.dv_acc);

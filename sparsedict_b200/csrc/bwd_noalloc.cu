@@ -12,9 +12,9 @@
 // The array is `g_noalloc_scratch` below: SDK_NOALLOC_SCRATCH_FLOATS fp32
 // elements (16 MiB), held on every GPU that loads the library until the
 // process exits.  Its name is only a host-side stand-in in host code; the
-// device address is looked up with cudaGetSymbolAddress, once per device,
-// with that device current, on the first call made on that device.
-#include <mutex>
+// device address is looked up with cudaGetSymbolAddress on every call, with
+// the call's device current (a cheap host-side query), so no address outlives
+// the context it was taken in (a cudaDeviceReset between calls included).
 
 #include "common.cuh"
 #include "kernels.h"
@@ -24,25 +24,12 @@ namespace {
 
 static __device__ __align__(256) float g_noalloc_scratch[SDK_NOALLOC_SCRATCH_FLOATS];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_noalloc_mutex;
-float* g_noalloc_ptr[kMaxDevices] = {};
-
-// Device address of the scratch array on the current device (looked up on
-// the first call for that device).
+// Device address of the scratch array in the current device's context.
 int noalloc_scratch(float** out) {
-  int dev = 0;
-  cudaError_t err = cudaGetDevice(&dev);
+  void* p = nullptr;
+  const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
   if (err != cudaSuccess) return record_cuda_error(err);
-  if (dev < 0 || dev >= kMaxDevices) return SDK_ERR_UNSUPPORTED;
-  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (err != cudaSuccess) return record_cuda_error(err);
-    g_noalloc_ptr[dev] = static_cast<float*>(p);
-  }
-  *out = g_noalloc_ptr[dev];
+  *out = static_cast<float*>(p);
   return SDK_OK;
 }
 

@@ -5,9 +5,9 @@
 // itself is the tensor-core forward's stream-ordered scratch when the caller
 // passes no workspace (fwd_tc.cu) and the no-allocation backward's static
 // array (bwd_noalloc.cu).
+#include <atomic>
 #include <cstdio>
 #include <cstring>
-#include <mutex>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -18,8 +18,7 @@ __device__ unsigned int g_device_status;
 
 namespace {
 thread_local char g_last_cuda_error[256] = "";
-std::mutex g_status_mutex;
-unsigned int* g_status_ptr[64] = {};
+std::atomic<uint64_t> g_wait_limit_ns{0};  // 0: the default bound
 
 int record(cudaError_t err) {
   if (err == cudaSuccess) return SDK_OK;
@@ -57,21 +56,21 @@ int check_device() {
 
 int record_cuda_error(cudaError_t err) { return record(err); }
 
-// Device address of this library's status word on the current device, looked
-// up once per device with that device current.
+uint64_t wait_limit_ns() {
+  const uint64_t v = g_wait_limit_ns.load(std::memory_order_relaxed);
+  return v ? v : 2000000000ull;
+}
+
+// Device address of this library's status word in the current device's
+// context (looked up on every call: a cheap host-side query, and no address
+// outlives the context it was taken in).
 unsigned int* device_status_ptr() {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  std::lock_guard<std::mutex> lock(g_status_mutex);
-  if (!g_status_ptr[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) {
-      cudaGetLastError();
-      return nullptr;
-    }
-    g_status_ptr[dev] = static_cast<unsigned int*>(p);
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
   }
-  return g_status_ptr[dev];
+  return static_cast<unsigned int*>(p);
 }
 
 }  // namespace sdk
@@ -99,6 +98,12 @@ const char* sdk_last_cuda_error(void) { return g_last_cuda_error; }
 int sdk_max_topk(int32_t dtype, int32_t d) {
   if (!dtype_ok(dtype) || d <= 0) return 0;
   return max_topk_generic(dtype, d);
+}
+
+int sdk_set_wait_limit(uint64_t ns) {
+  if (ns > 60000000000ull) return SDK_ERR_INVALID_ARGUMENT;
+  g_wait_limit_ns.store(ns, std::memory_order_relaxed);
+  return SDK_OK;
 }
 
 int sdk_device_status(unsigned int* bits, int32_t clear, void* stream) {
@@ -166,6 +171,29 @@ int bwd_impl(const void* q, const void* k, const void* v, const void* dout, cons
   return finish(bwd_sparse(L));
 }
 
+// Backward into output-dtype dK/dV: the key-major kernels when the shape
+// takes them, else the scatter kernel into fp32 (fp64) accumulators carved
+// from the workspace, then one conversion.  Returns the bytes needed.
+size_t bwd_direct_bytes(int64_t rows, int64_t slices, int64_t m, int32_t d, int32_t dv, int32_t topk,
+                        int32_t score_grid, bool grouped, int32_t dtype, int64_t n, bool alias, bool aligned) {
+  BwdLaunch probe{};
+  probe.dtype = dtype;
+  probe.d = d;
+  probe.dv = dv;
+  probe.topk = topk;
+  probe.score_grid = score_grid;
+  probe.m = m;
+  probe.n = n;
+  probe.slices = slices;
+  probe.row_offsets = grouped ? reinterpret_cast<const int32_t*>(16) : nullptr;
+  const void* p16 = reinterpret_cast<const void*>(aligned ? 256 : 1);
+  probe.q = probe.k = probe.v = probe.dout = p16;
+  probe.dq = const_cast<void*>(p16);
+  if (bwd_keymajor_supports(probe)) return bwd_keymajor_workspace(rows, slices, m, topk);
+  const size_t acc = dtype == SDK_DTYPE_F64 ? 8 : 4;
+  return (size_t)slices * (size_t)m * (size_t)(d + (alias ? 0 : dv)) * acc + 256;
+}
+
 bool segments_ok(const void* seg_bias, int64_t seg_len, int32_t segs, int64_t m) {
   return seg_bias && seg_len >= 1 && segs >= 1 && seg_len * (int64_t)segs >= m;
 }
@@ -182,8 +210,9 @@ int sdk_topk_attn_fwd(const void* q, const void* k, const void* v, void* out, in
                   score_grid, nullptr, 0, 0, dtype, stream);
 }
 
-size_t sdk_topk_attn_fwd_workspace_size(int64_t rows, int32_t d, int32_t dv, int32_t topk, int32_t dtype) {
-  return fwd_tensorcore_workspace(rows, d, dv, topk, dtype);
+size_t sdk_topk_attn_fwd_workspace_size(int64_t rows, int64_t m, int32_t d, int32_t dv, int32_t topk,
+                                        int32_t score_grid, int32_t grouped, int32_t dtype) {
+  return fwd_tensorcore_workspace(rows, m, d, dv, topk, score_grid, grouped != 0, dtype);
 }
 
 int sdk_topk_attn_fwd_ws(const void* q, const void* k, const void* v, void* out, int32_t* top_idx, void* lse,
@@ -223,6 +252,48 @@ int sdk_topk_attn_bwd_biased(const void* q, const void* k, const void* v, const 
   if (!segments_ok(seg_bias, seg_len, segs, m)) return SDK_ERR_INVALID_ARGUMENT;
   return bwd_impl(q, k, v, dout, top_idx, lse, dq, dk_acc, dv_acc, row_offsets, row_index, slices, n, m, d, dv, topk,
                   scale, score_grid, accumulate, seg_bias, dseg_bias, seg_len, segs, dtype, stream);
+}
+
+size_t sdk_topk_attn_bwd_workspace_size(int64_t rows, int64_t slices, int64_t m, int32_t d, int32_t dv,
+                                        int32_t topk, int32_t score_grid, int32_t grouped, int32_t dtype) {
+  if (rows < 0 || slices <= 0 || m <= 0 || d <= 0 || dv <= 0 || topk < 1 || !dtype_ok(dtype)) return 0;
+  // the per-slice row limit of the key-major kernels is checked against the
+  // largest slice: rows (grouped) or rows / slices (uniform)
+  const int64_t n = grouped ? rows : rows / slices;
+  return bwd_direct_bytes(rows, slices, m, d, dv, topk, score_grid, grouped != 0, dtype, n, false, true);
+}
+
+int sdk_topk_attn_bwd_direct(const void* q, const void* k, const void* v, const void* dout, const int32_t* top_idx,
+                             const void* lse, void* dq, void* dk, void* dv, const int32_t* row_offsets,
+                             const int32_t* row_index, int64_t slices, int64_t n, int64_t m, int32_t d,
+                             int32_t dv_dim, int32_t topk, double scale, int32_t score_grid, int32_t dtype,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  if (!q || !k || !v || !dout || !top_idx || !lse || !dq || !dk || !dv) return SDK_ERR_INVALID_ARGUMENT;
+  if (!dtype_ok(dtype) || slices <= 0 || n < 0 || m <= 0 || d <= 0 || dv_dim <= 0) return SDK_ERR_INVALID_ARGUMENT;
+  if (topk < 1 || topk > m || !(scale > 0) || score_grid < 0) return SDK_ERR_INVALID_ARGUMENT;
+  if (dk == dv && d != dv_dim) return SDK_ERR_INVALID_ARGUMENT;
+  if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255)) return SDK_ERR_INVALID_ARGUMENT;
+  if (int rc = check_device()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t rows = row_offsets ? n : slices * n;
+  BwdLaunch L{q, k, v, dout, top_idx, lse, dq, nullptr, nullptr, row_offsets, row_index, slices, n, m, d, dv_dim, topk,
+              scale, score_grid, dtype, device_status_ptr(), st};
+  const bool alias = dk == dv;
+  if (bwd_keymajor_supports(L)) {
+    if (workspace_bytes < bwd_keymajor_workspace(rows, slices, m, topk)) return SDK_ERR_INVALID_ARGUMENT;
+    return finish(bwd_keymajor(L, dk, dv, 0, 0, workspace));
+  }
+  const size_t acc_sz = dtype == SDK_DTYPE_F64 ? 8 : 4;
+  const size_t dk_bytes = (size_t)slices * m * d * acc_sz;
+  const size_t need = dk_bytes + (alias ? 0 : (size_t)slices * m * dv_dim * acc_sz);
+  if (workspace_bytes < need) return SDK_ERR_INVALID_ARGUMENT;
+  L.dk_acc = workspace;
+  L.dv_acc = alias ? workspace : static_cast<uint8_t*>(workspace) + dk_bytes;
+  if (int rc = record(cudaMemsetAsync(workspace, 0, need, st))) return rc;
+  int rc = bwd_sparse(L);
+  if (rc == SDK_OK) rc = finalize_grad(L.dk_acc, dk, slices * m * d, 1.0, dtype, st);
+  if (rc == SDK_OK && !alias) rc = finalize_grad(L.dv_acc, dv, slices * m * dv_dim, 1.0, dtype, st);
+  return finish(rc);
 }
 
 int sdk_finalize_grad(const void* acc, void* out, int64_t count, double multiplier, int32_t dtype, void* stream) {

@@ -76,8 +76,9 @@ constexpr int RS = TQ * NTILE;  // rows per CTA; row stride of the slot-major li
 constexpr int TK = 128;         // keys per score tile (MMA N)
 constexpr int D = 64;           // feature width (one 128-byte swizzle row)
 constexpr int KSTAGES = 1;
-constexpr int CAP = 176;        // list slots per row (and candidate buffer entries per row)
+constexpr int CAP = 160;        // list slots per row (and candidate buffer entries per row)
 constexpr int FIX_CAP = 128;    // exact list of a row re-selected by one warp
+constexpr int kDenseHits = 8;   // a chunk row with more hits makes the warp append branch-free
 constexpr int NT = 384;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t TILE_BYTES = TK * D * 2;  // a K tile, also a Q tile
@@ -85,7 +86,8 @@ constexpr uint32_t TILE_BYTES = TK * D * 2;  // a K tile, also a Q tile
 constexpr int OFF_Q = 0;
 constexpr int OFF_K = OFF_Q + NTILE * (int)TILE_BYTES;
 constexpr int OFF_LIST = OFF_K + KSTAGES * (int)TILE_BYTES;
-constexpr int OFF_BAR = OFF_LIST + CAP * RS * 4;
+constexpr int OFF_STAGE = OFF_LIST + CAP * RS * 4;  // per row: the current chunk's 32 buckets
+constexpr int OFF_BAR = OFF_STAGE + RS * 64;
 constexpr int NBARS = 1 + 2 * KSTAGES + 4 * NTILE;
 constexpr int OFF_MISC = OFF_BAR + NBARS * 8;
 constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
@@ -106,6 +108,7 @@ struct TcArgs {
   int tiles_per_slice, topk;
   uint32_t big16;    // 16-bit magnitude field at which an element counts as unsafe
   unsigned int* status;
+  uint64_t wait_limit_ns;  // bound of each pipeline wait (sdk_set_wait_limit)
 };
 
 // Input magnitude check.  With every |q|, |k| < 2^60 and finite, each of the
@@ -299,18 +302,79 @@ __device__ __noinline__ Compacted compact_bucket_exact(const uint32_t* list_c, i
   return Compacted{w, fmaxf(tau, tau_of_bucket(pivot)), w < cnt};
 }
 
-// Append every key of a 32-key chunk whose score passes !(x <= tau) to the
-// row's list.  Branch-free: each key's slot is the running count and the
-// store is a predicated instruction, so lanes never diverge per key.
-__device__ __forceinline__ void append_chunk(const uint32_t* v, int valid, float tau, uint32_t key0,
-                                             uint32_t base, int& cnt) {
+// Threshold of the stream filter in bucket form, both halves of a bf16x2:
+// the bucket of tau (the lowest score of the compaction pivot's bucket), or
+// -inf before the first compaction.  A key passes when its bucket, compared
+// as a bf16 number, reaches this one: every key with score > tau passes
+// (truncation is monotonic), plus the other keys of tau's own bucket.
+__device__ __forceinline__ uint32_t packed_threshold(float tau) {
+  const uint32_t b = (tau != tau) ? 0xff80u : (__float_as_uint(tau) >> 16);
+  return b * 0x00010001u;
+}
+
+// Hit mask of a 32-key chunk: bit i is set when key i's bucket reaches the
+// packed threshold.  Word j of `p` receives the buckets of keys j (low half)
+// and j + 16 (high half); one byte permute, one packed bf16 compare and one
+// logic op cover two keys.
+__device__ __forceinline__ uint32_t hit_mask(const uint32_t (&v)[32], uint32_t tb2, uint32_t (&p)[16]) {
+  uint32_t m[4] = {0u, 0u, 0u, 0u};  // four independent chains, joined at the end
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    p[j] = __byte_perm(v[j], v[j + 16], 0x7632);
+    uint32_t w;
+    asm("set.ge.u32.bf16x2 %0, %1, %2;" : "=r"(w) : "r"(p[j]), "r"(tb2));
+    m[j & 3] |= w & (0x00010001u << j);
+  }
+  return (m[0] | m[1]) | (m[2] | m[3]);
+}
+
+// Append the keys of mask `m` of a chunk to the row's list, branch-free: each
+// key's slot is the running count and the store is a predicated instruction.
+// Used when some row of the warp has many hits in the chunk (early in the
+// stream, before the threshold has risen).
+__device__ __forceinline__ void append_dense(const uint32_t (&v)[32], uint32_t m, uint32_t key0, uint32_t base,
+                                             int& cnt) {
   uint32_t slot = (uint32_t)cnt;
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
-    const uint32_t take = (uint32_t)(i < valid && !(__uint_as_float(v[i]) <= tau));
+    const uint32_t take = (m >> i) & 1u;
     st_shared_u32_if(base + slot * (4u * RS), __byte_perm(key0 + (uint32_t)i, v[i], 0x7610), take);
     slot += take;
   }
+  cnt = (int)slot;
+}
+
+// Append the keys of mask `m` one hit at a time.  The chunk's packed buckets
+// are first stored to the row's 64-byte stage (four 16-byte stores, chunk c
+// at position c ^ sw so that eight lanes' stores cover all 32 banks); each
+// hit then reads its bucket back by its bit position.  A lane loops only over
+// its own hits, so a warp pays for its row with the most hits, usually two
+// or three per chunk.
+__device__ __forceinline__ void append_sparse(const uint32_t (&p)[16], uint32_t m, uint32_t key0, uint32_t stage,
+                                              uint32_t sw, uint32_t base, int& cnt) {
+  if (m == 0u) return;
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(stage + ((16u * c) ^ sw)), "r"(p[4 * c]),
+                 "r"(p[4 * c + 1]), "r"(p[4 * c + 2]), "r"(p[4 * c + 3])
+                 : "memory");
+  // two hits per iteration (most lanes have at most two): both bucket reads
+  // are in flight together
+  uint32_t slot = (uint32_t)cnt;
+  do {
+    const uint32_t b0 = 31u - __clz(m);
+    m ^= 1u << b0;
+    const uint32_t two = m != 0u;
+    const uint32_t b1 = two ? 31u - __clz(m) : b0;
+    m &= ~(two << b1);
+    uint32_t k0b, k1b;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=r"(k0b) : "r"(stage + ((((b0 << 2) & 60u) ^ sw) | ((b0 >> 3) & 2u))) : "memory");
+    asm volatile("ld.shared.u16 %0, [%1];" : "=r"(k1b) : "r"(stage + ((((b1 << 2) & 60u) ^ sw) | ((b1 >> 3) & 2u))) : "memory");
+    asm volatile("st.shared.u32 [%0], %1;" ::"r"(base + slot * (4u * RS)), "r"(__byte_perm(key0 + b0, k0b, 0x5410))
+                 : "memory");
+    st_shared_u32_if(base + (slot + 1u) * (4u * RS), __byte_perm(key0 + b1, k1b, 0x5410), two);
+    slot += 1u + two;
+  } while (m != 0u);
   cnt = (int)slot;
 }
 
@@ -574,7 +638,7 @@ __global__ void __launch_bounds__(NT, 1)
       for (int t = 0; t < ntiles; ++t) {
         const int s = t % KSTAGES;
         const uint32_t ph = (uint32_t)(t / KSTAGES) & 1u;
-        if (!mbar_wait(&k_empty[s], ph ^ 1u, abort_flag)) break;
+        if (!mbar_wait(&k_empty[s], ph ^ 1u, abort_flag, a.wait_limit_ns)) break;
         mbar_arrive_expect_tx(&k_full[s], TILE_BYTES);
         tma_load_2d(ks + s * TILE_BYTES, &tmap_k, 0, (int)(slice * a.m + (int64_t)t * TK), &k_full[s]);
         ++issued;
@@ -626,16 +690,16 @@ __global__ void __launch_bounds__(NT, 1)
       const uint32_t q_addr = smem_addr(qs);
       uint64_t* last_bar = nullptr;  // barrier of the last commit, for the abort path
       uint32_t last_ph = 0;
-      if (mbar_wait(q_full, 0, abort_flag)) {
+      if (mbar_wait(q_full, 0, abort_flag, a.wait_limit_ns)) {
         for (int t = 0; t < ntiles; ++t) {
           const int s = t % KSTAGES, b = t & 1;
           const uint32_t ph_s = ((uint32_t)(t >> 1) & 1u);
-          if (!mbar_wait(&k_full[s], (uint32_t)(t / KSTAGES) & 1u, abort_flag)) break;
+          if (!mbar_wait(&k_full[s], (uint32_t)(t / KSTAGES) & 1u, abort_flag, a.wait_limit_ns)) break;
           const uint32_t k_addr = smem_addr(ks + s * TILE_BYTES);
           bool stop = false;
 #pragma unroll
           for (int g = 0; g < NTILE; ++g) {
-            if (!mbar_wait(&s_empty[2 * g + b], ph_s ^ 1u, abort_flag)) {
+            if (!mbar_wait(&s_empty[2 * g + b], ph_s ^ 1u, abort_flag, a.wait_limit_ns)) {
               stop = true;
               break;
             }
@@ -669,13 +733,16 @@ __global__ void __launch_bounds__(NT, 1)
     uint64_t* my_full = s_full + 2 * wg;
     uint64_t* my_empty = s_empty + 2 * wg;
     const uint32_t lbase = smem_addr(list) + 4u * R;
+    const uint32_t sbase = smem_addr(sm + OFF_STAGE) + 64u * R;
+    const uint32_t sw = ((uint32_t)(R >> 1) & 3u) << 4;
     float tau = __int_as_float(0x7fc00000);  // "no threshold yet"
+    uint32_t tb2 = packed_threshold(tau);
     int cnt = 0;
     bool dead = false;  // list could not be shrunk: exact re-selection at the end
     bool ok = true;
     for (int t = 0; t < ntiles; ++t) {
       const int b = t & 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(&my_full[b], (uint32_t)(t >> 1) & 1u, abort_flag));
+      ok = __all_sync(0xffffffffu, mbar_wait(&my_full[b], (uint32_t)(t >> 1) & 1u, abort_flag, a.wait_limit_ns));
       if (!ok) break;
       tc_fence_after();
       const int64_t key_tile = (int64_t)t * TK;
@@ -699,7 +766,15 @@ __global__ void __launch_bounds__(NT, 1)
           }
           if (!__any_sync(0xffffffffu, !(mx <= tau))) return;
         }
-        append_chunk(v, dead ? 0 : valid, tau, (uint32_t)(key_tile + c * 32), lbase, cnt);
+        uint32_t p[16];
+        uint32_t m = hit_mask(v, tb2, p);
+        if (dead) m = 0u;
+        if (valid < 32) m &= valid > 0 ? (1u << valid) - 1u : 0u;
+        const uint32_t key0 = (uint32_t)(key_tile + c * 32);
+        if (__any_sync(0xffffffffu, __popc(m) > kDenseHits))
+          append_dense(v, m, key0, lbase, cnt);
+        else
+          append_sparse(p, m, key0, sbase, sw, lbase, cnt);
         // When one lane's list could overflow, every lane holding well over
         // k keys compacts in the same pass: under SIMT the warp pays for the
         // longest list either way.
@@ -712,6 +787,7 @@ __global__ void __launch_bounds__(NT, 1)
             if (r.cnt > CAP - 32) r = compact_bucket_exact(list, R, r.cnt, r.tau, a.topk);
             cnt = r.cnt;
             tau = r.tau;
+            tb2 = packed_threshold(tau);
             dead = cnt > CAP - 32;
           }
         }
@@ -873,7 +949,19 @@ __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
   FinWarp& w = sw[warp];
   for (int64_t r = (int64_t)blockIdx.x * FW + warp; r < a.rows; r += (int64_t)gridDim.x * FW) {
     const int cnt = a.cand_n[r];
-    if (cnt == kCandAborted) continue;
+    if (cnt == kCandAborted) {
+      // the stream kernel gave up on this row (a bounded wait ran out, device
+      // status bit 2): defined outputs that no caller can mistake for a
+      // result — NaN output and LSE, index -1 (the backward skips it)
+      for (int j = lane; j < a.topk; j += kWarp) {
+        a.top_idx[r * a.topk + j] = -1;
+        if (a.top_scores) a.top_scores[r * a.topk + j] = __int_as_float(0x7fc00000);
+      }
+      if (lane < D) static_cast<T*>(a.out)[r * D + lane] = from_acc<T>(__int_as_float(0x7fc00000));
+      if (lane + kWarp < D) static_cast<T*>(a.out)[r * D + lane + kWarp] = from_acc<T>(__int_as_float(0x7fc00000));
+      if (lane == 0) a.lse[r] = __int_as_float(0x7fc00000);
+      continue;
+    }
     const int64_t slice = r / a.n;
     const uint4 qg = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(a.q) + r * D) + g);
     const uint32_t add = (0x8000u - a.big16) * 0x00010001u;
@@ -1149,6 +1237,7 @@ int launch(const FwdLaunch& L) {
   a.tiles_per_slice = (int)((L.n + RS - 1) / RS);
   a.topk = L.topk;
   a.status = L.status;
+  a.wait_limit_ns = wait_limit_ns();
   const int64_t grid = L.slices * a.tiles_per_slice;
   if (grid <= 0) return SDK_OK;
   auto kern = L.topk < 8 ? fused_fwd_tc<T, true> : fused_fwd_tc<T, false>;
@@ -1210,19 +1299,29 @@ int launch(const FwdLaunch& L) {
 
 }  // namespace
 
+namespace {
+// The shape conditions of the tensor-core path (everything but pointers).
+bool tensorcore_shape(int64_t rows, int64_t m, int d, int dv, int topk, int score_grid, bool grouped, int dtype) {
+  if (dtype != SDK_DTYPE_BF16 && dtype != SDK_DTYPE_F16) return false;
+  if (d != D || dv != D || score_grid != 0 || grouped) return false;
+  if (m < 1 || m > 65536 || topk < 1 || topk > 64 || rows < 1) return false;
+  return rows <= 0x7fffff00;
+}
+}  // namespace
+
 bool fwd_tensorcore_supports(const FwdLaunch& L) {
-  if (L.dtype != SDK_DTYPE_BF16 && L.dtype != SDK_DTYPE_F16) return false;
-  if (L.d != D || L.dv != D || L.score_grid != 0) return false;
-  if (L.row_offsets || L.row_index || L.seg_bias) return false;
-  if (L.m > 65536 || L.topk > 64 || L.n < 1) return false;
-  if (L.slices * L.n > 0x7fffff00 || L.slices * L.m > 0x7fffffff) return false;
+  if (L.n < 1 || L.seg_bias) return false;
+  if (!tensorcore_shape(L.slices * L.n, L.m, L.d, L.dv, L.topk, L.score_grid, L.row_offsets || L.row_index,
+                        L.dtype))
+    return false;
+  if (L.slices * L.m > 0x7fffffff) return false;
   if (!aligned16(L.q) || !aligned16(L.k) || !aligned16(L.v) || !aligned16(L.out)) return false;
   return encode_fn() != nullptr;
 }
 
-size_t fwd_tensorcore_workspace(int64_t rows, int d, int dv, int topk, int dtype) {
-  if (dtype != SDK_DTYPE_BF16 && dtype != SDK_DTYPE_F16) return 0;
-  if (d != D || dv != D || topk > 64 || rows <= 0) return 0;
+size_t fwd_tensorcore_workspace(int64_t rows, int64_t m, int d, int dv, int topk, int score_grid, bool grouped,
+                                int dtype) {
+  if (!tensorcore_shape(rows, m, d, dv, topk, score_grid, grouped, dtype)) return 0;
   return (size_t)rows * (CAP * 4 + 8);
 }
 

@@ -74,6 +74,10 @@ struct BwdLaunch {
   int segs = 0;
 };
 
+// Bound of each pipeline wait of the tensor-core forward, in ns
+// (sdk_set_wait_limit; default sm100::kWaitLimitNs).  Defined in capi.cu.
+uint64_t wait_limit_ns();
+
 // Records a CUDA error for sdk_last_cuda_error(); returns SDK_ERR_CUDA (or
 // SDK_OK for cudaSuccess).  Defined in capi.cu.
 int record_cuda_error(cudaError_t err);
@@ -87,11 +91,21 @@ int max_topk_generic(int dtype, int d);
 int fwd_tensorcore(const FwdLaunch& L);
 bool fwd_tensorcore_supports(const FwdLaunch& L);
 // Scratch bytes the tensor-core forward needs for `rows` query rows when the
-// shape can take that path (bf16/fp16, d = dv = 64, topk <= 64), else 0.
-size_t fwd_tensorcore_workspace(int64_t rows, int d, int dv, int topk, int dtype);
+// shape takes that path (bf16/fp16, d = dv = 64, topk <= 64, m <= 65536,
+// score_grid 0, not grouped or routed), else 0.
+size_t fwd_tensorcore_workspace(int64_t rows, int64_t m, int d, int dv, int topk, int score_grid, bool grouped,
+                                int dtype);
 
 // Sparse backward (bwd.cu).
 int bwd_sparse(const BwdLaunch& L);
+
+// Deterministic key-major backward (bwd_km.cu): bf16/fp16, d = dv = 64,
+// topk <= 64, m <= 16384, at most 65535 rows per slice.  Writes dq and dk/dv
+// (input dtype, or fp32 accumulators when out_acc; dk == dv sums both) with
+// no atomics; `ws` holds bwd_keymajor_workspace bytes (256-byte aligned).
+bool bwd_keymajor_supports(const BwdLaunch& L);
+size_t bwd_keymajor_workspace(int64_t rows, int64_t slices, int64_t m, int topk);
+int bwd_keymajor(const BwdLaunch& L, void* dk, void* dv, int out_acc, int accumulate, void* ws);
 int finalize_grad(const void* acc, void* out, int64_t count, double multiplier, int dtype,
                   cudaStream_t stream);
 

@@ -11,6 +11,8 @@
 namespace sdk {
 namespace sm100 {
 
+// Default bound of a pipeline wait, and the fixed bound of the waits that
+// let in-flight copies and MMAs land before a CTA that gave up exits.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -70,14 +72,16 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 
 // Waits for the phase of `bar` with parity `parity` to complete.  Gives up
 // (returns false) when `abort_flag` is raised by another warp or after
-// kWaitLimitNs, in which case it raises the flag itself.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+// `limit_ns`, in which case it raises the flag itself.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer();
+  const uint32_t hint = limit_ns < 1000000u ? (uint32_t)limit_ns : 1000000u;
   while (true) {
-    if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
+    if (mbar_try_wait_sleep(bar, parity, hint)) return true;
     if (*abort_flag) return false;
-    if (global_timer() - t0 > kWaitLimitNs) {
+    if (global_timer() - t0 > limit_ns) {
       *abort_flag = 1;
       return false;
     }

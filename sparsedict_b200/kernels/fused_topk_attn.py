@@ -152,15 +152,9 @@ class FusedTopKAttentionFunction(torch.autograd.Function):
         batch_heads = batch * heads
         dtype = queries2.dtype
         grad_output2 = grad_output.reshape(batch_heads, query_count, feat_v).to(dtype).contiguous()
-        acc = _ops.acc_dtype(dtype)
-        dk_acc = torch.empty((batch_heads, key_count, feat_q), device=queries2.device, dtype=acc)
-        dv_acc = torch.empty((batch_heads, key_count, feat_v), device=queries2.device, dtype=acc)
-        dq, dk_acc, dv_acc = _ops.topk_attn_bwd(
-            queries2, keys2, values2, grad_output2, top_indices, lse, score_scale,
-            score_grid=score_grid, dk_acc=dk_acc, dv_acc=dv_acc,
+        dq, d_keys, d_values = _ops.topk_attn_bwd_out(
+            queries2, keys2, values2, grad_output2, top_indices, lse, score_scale, score_grid=score_grid,
         )
-        d_keys = _ops.finalize_grad(dk_acc, dtype)
-        d_values = _ops.finalize_grad(dv_acc, dtype)
         grads = (
             dq.view(batch, heads, query_count, feat_q),
             d_keys.view(batch, heads, key_count, feat_q),

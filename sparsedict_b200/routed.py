@@ -12,8 +12,8 @@ expert ``argmax(logits[n])`` only, the atoms serving as both keys and values.
 Here that runs without the dense ``(N, E*M)`` score tensor: a routing kernel
 groups tokens by expert (stable counting sort), the fused forward treats
 each expert as one slice of a ragged batch (reading queries through the
-routing permutation), and the backward accumulates the key and value
-gradients of an expert's dictionary into one buffer (``dDict = dK + dV``).
+routing permutation), and the backward writes the key and value gradients of
+an expert's dictionary into one buffer (``dDict = dK + dV``).
 """
 
 from __future__ import annotations
@@ -39,12 +39,12 @@ class RoutedDictionaryAttention(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_out, _g_expert, _g_idx):
         queries, dictionaries, idx, lse, order, offsets = ctx.saved_tensors
-        acc = torch.empty(dictionaries.shape, device=queries.device, dtype=_ops.acc_dtype(queries.dtype))
-        dq, acc, _ = _ops.topk_attn_bwd(
+        # keys and values are one dictionary: one gradient buffer receives dK + dV
+        dq, ddict, _ = _ops.topk_attn_bwd_out(
             queries, dictionaries, dictionaries, grad_out.to(queries.dtype).contiguous(), idx, lse, ctx.scale,
-            dk_acc=acc, dv_acc=acc, row_offsets=offsets, row_index=order,
+            row_offsets=offsets, row_index=order, shared_kv=True,
         )
-        return dq, _ops.finalize_grad(acc, dictionaries.dtype), None, None, None
+        return dq, ddict, None, None, None
 
 
 def routed_dictionary_attention(

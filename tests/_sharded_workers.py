@@ -15,32 +15,20 @@ import torch.distributed as dist
 import oracle
 from sparsedict_b200.sharded import ShardedTopKAttention, ShardPlan
 
-S, N, M, D, TOPK = 4, 24, 40, 8, 5
+S, N, M, D, TOPK = 8, 24, 40, 8, 5
 
 
 class OracleKernels:
-    def acc_dtype(self, dtype):
-        return torch.float64
+    def forward(self, q, k, v, topk, scale, out):
+        o, idx, lse, _ = oracle.topk_attention_forward(q.numpy(), k.numpy(), v.numpy(), topk, scale)
+        out.copy_(torch.from_numpy(o))
+        return out, torch.from_numpy(idx).reshape(-1, topk), torch.from_numpy(lse).reshape(-1)
 
-    def forward(self, q, k, v, topk, scale):
-        out, idx, lse, _ = oracle.topk_attention_forward(q.numpy(), k.numpy(), v.numpy(), topk, scale)
-        return torch.from_numpy(out), torch.from_numpy(idx).reshape(-1, topk), torch.from_numpy(lse).reshape(-1)
-
-    def backward(self, q, k, v, dout, idx, lse, scale, dk_acc, dv_acc, accumulate, dq):
+    def backward(self, q, k, v, dout, idx, lse, scale, dq, dk, dv):
         gq, gk, gv = oracle.topk_attention_backward(q.numpy(), k.numpy(), v.numpy(), idx.numpy(), dout.numpy(), scale)
         dq.copy_(torch.from_numpy(gq))
-        if accumulate:
-            dk_acc += torch.from_numpy(gk)
-            dv_acc += torch.from_numpy(gv)
-        else:
-            dk_acc.copy_(torch.from_numpy(gk))
-            dv_acc.copy_(torch.from_numpy(gv))
-
-    def finalize(self, acc, dtype, out=None):
-        if out is None:
-            return acc.to(dtype)
-        out.copy_(acc)
-        return out
+        dk.copy_(torch.from_numpy(gk))
+        dv.copy_(torch.from_numpy(gv))
 
 
 def inputs():
@@ -56,12 +44,13 @@ def run_rank(rank, world, port, reduce, fail_rank, results):
         os.environ["MASTER_PORT"] = str(port)
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=8))
         q, k, v, do = inputs()
-        plan = ShardPlan(S, world, rank)
-        runner = ShardedTopKAttention(plan, M, D, D, TOPK, torch.float64, "cpu", reduce=reduce, buckets=2,
+        plan = ShardPlan(S, world, rank, buckets=2)
+        runner = ShardedTopKAttention(plan, M, D, D, TOPK, torch.float64, "cpu", reduce=reduce,
                                       kernels=OracleKernels())
         if rank == fail_rank:
             raise RuntimeError("injected failure before the backward exchange")
-        out, dq, dk, dv = runner.step(q[plan.begin:plan.end], k, v, do[plan.begin:plan.end])
+        own = plan.owned()
+        out, dq, dk, dv = runner.step(q[own].contiguous(), k, v, do[own].contiguous())
         results.put(("ok", rank, out.numpy(), dq.numpy(), dk.numpy(), dv.numpy()))
         dist.destroy_process_group()
     except Exception as exc:  # reported to the parent, which asserts on it

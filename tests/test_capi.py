@@ -74,16 +74,23 @@ def test_max_topk_covers_the_benchmark_configurations(dtype):
 
 
 def test_forward_workspace_size_follows_the_tensor_core_shapes():
+    # Nonzero exactly when the call takes the tensor-core path: bf16/fp16,
+    # d = dv = 64, 1 <= k <= 64, m <= 65536, no score grid, uniform slices.
     lib = _native.load()
-    per_row = 176 * 4 + 8  # candidate list, count and check word per query row
+    size = lib.sdk_topk_attn_fwd_workspace_size
+    per_row = 160 * 4 + 8  # candidate list, count and check word per query row
     for code in (_native.DTYPE_BF16, _native.DTYPE_F16):
-        assert lib.sdk_topk_attn_fwd_workspace_size(1000, 64, 64, 64, code) == 1000 * per_row
-        assert lib.sdk_topk_attn_fwd_workspace_size(3, 64, 64, 1, code) == 3 * per_row
-        assert lib.sdk_topk_attn_fwd_workspace_size(1000, 64, 64, 65, code) == 0
-        assert lib.sdk_topk_attn_fwd_workspace_size(1000, 32, 32, 8, code) == 0
-        assert lib.sdk_topk_attn_fwd_workspace_size(0, 64, 64, 8, code) == 0
+        assert size(1000, 16384, 64, 64, 64, 0, 0, code) == 1000 * per_row
+        assert size(3, 100, 64, 64, 1, 0, 0, code) == 3 * per_row
+        assert size(1000, 65536, 64, 64, 64, 0, 0, code) == 1000 * per_row
+        assert size(1000, 65537, 64, 64, 64, 0, 0, code) == 0
+        assert size(1000, 16384, 64, 64, 65, 0, 0, code) == 0
+        assert size(1000, 16384, 32, 32, 8, 0, 0, code) == 0
+        assert size(0, 16384, 64, 64, 8, 0, 0, code) == 0
+        assert size(1000, 16384, 64, 64, 8, 64, 0, code) == 0
+        assert size(1000, 16384, 64, 64, 8, 0, 1, code) == 0
     for code in (_native.DTYPE_F32, _native.DTYPE_F64):
-        assert lib.sdk_topk_attn_fwd_workspace_size(1000, 64, 64, 64, code) == 0
+        assert size(1000, 16384, 64, 64, 64, 0, 0, code) == 0
 
 
 def test_forward_workspace_pointer_and_size_must_agree():

@@ -189,6 +189,10 @@ def test_gap_aware_mismatch_counter():
     scores = np.array([[5.0, 4.0, 3.99999, 1.0]], dtype=np.float32)
     assert oracle.gap_aware_index_mismatches(np.array([[0, 2]]), np.array([[0, 1]]), scores, 1e-4) == 0
     assert oracle.gap_aware_index_mismatches(np.array([[0, 3]]), np.array([[0, 1]]), scores, 1e-4) == 1
+    # the near-tie allowance is reported: (failing rows, rows passing as near-ties)
+    assert oracle.index_mismatch_counts(np.array([[0, 2]]), np.array([[0, 1]]), scores, 1e-4) == (0, 1)
+    assert oracle.index_mismatch_counts(np.array([[0, 1]]), np.array([[0, 1]]), scores, 1e-4) == (0, 0)
+    assert oracle.index_mismatch_counts(np.array([[2, 0]]), np.array([[0, 1]]), scores, 1e-4, ordered=False) == (0, 1)
 
 
 def test_partition_top_k_matches_lexsort_order():

@@ -48,9 +48,14 @@ def _oracle_scores64(q, k, scale):
     return np.einsum("bnd,bmd->bnm", _flat(q).astype(np.float64), _flat(k).astype(np.float64)) * scale
 
 
-def _assert_indices(actual, expected, scores, tol=1e-5, ordered=True):
-    bad = oracle.gap_aware_index_mismatches(actual, expected, scores, tol, ordered)
+def _assert_indices(actual, expected, scores, tol=1e-5, ordered=True, max_near_ties=0):
+    """Indices equal to the oracle's; a row may differ only by keys within ``tol``
+    of the oracle's k-th score, and at most ``max_near_ties`` rows may do so
+    (0 on the reference's golden grids)."""
+    bad, near = oracle.index_mismatch_counts(actual, expected, scores, tol, ordered)
     assert bad == 0, f"{bad} rows select different keys"
+    assert near <= max_near_ties, f"{near} rows differ inside the near-tie tolerance {tol} (limit {max_near_ties})"
+    return near
 
 
 # --- compile smoke -----------------------------------------------------------
@@ -86,6 +91,7 @@ def test_forward_parity_fp32_large_grid(golden):
     tag = "grid_4096_256_16_64"
     np.testing.assert_allclose(out.cpu().numpy()[..., ::8, :], golden[f"{tag}_out_rows8"], atol=1e-5, rtol=0)
     _, idx, _, _ = _hybrid_topk_attention_with_aux(q.to(DEV), k.to(DEV), v.to(DEV), 16, 1 / 8)
+    # the reference's golden grid: no near-tie allowance used
     _assert_indices(idx.cpu().numpy(), _flat(golden[f"{tag}_idx"]), _oracle_scores64(q.numpy(), k.numpy(), 1 / 8))
 
 
@@ -345,7 +351,7 @@ def test_low_precision_forward_backward_vs_oracle(dtype):
     gidx = gidx.cpu().numpy().reshape(idx.shape)
     # selected sets agree wherever the affinity gap exceeds bf16 rounding (here: 1e-4);
     # the tensor-core kernel returns each row's top-k set unordered
-    _assert_indices(gidx, idx, _oracle_scores64(qr, kr, scale), tol=1e-4, ordered=False)
+    _assert_indices(gidx, idx, _oracle_scores64(qr, kr, scale), tol=1e-4, ordered=False, max_near_ties=2)
     np.testing.assert_allclose(out.float().detach().cpu().numpy().reshape(o.shape), o, rtol=2e-2, atol=2e-2)
     # backward checked on the support the GPU selected
     ref = oracle.topk_attention_backward(_flat(qr), _flat(kr), _flat(vr), gidx, _flat(dor), scale)
@@ -398,8 +404,8 @@ def test_tensor_core_forward_on_caller_workspace_matches_library_pool():
         torch.cuda.synchronize()
         return rc, out, idx, lse
 
-    need = lib.sdk_topk_attn_fwd_workspace_size(bh * n, d, d, k, _native.DTYPE_BF16)
-    assert need == bh * n * (176 * 4 + 8)
+    need = lib.sdk_topk_attn_fwd_workspace_size(bh * n, m, d, d, k, 0, 0, _native.DTYPE_BF16)
+    assert need == bh * n * (160 * 4 + 8)
     buf = torch.empty(need + 16, device=DEV, dtype=torch.uint8)
     rc0, o0, i0, l0 = run(None, 0, pooled=True)
     rc1, o1, i1, l1 = run(buf.data_ptr(), need)
@@ -440,7 +446,8 @@ def test_tensor_core_forward_unsafe_inputs_are_reselected_exactly(dtype):
     exp = np.sort(oi.reshape(bh, n, k), axis=-1)
     act = np.sort(got, axis=-1)
     assert np.array_equal(act[~finite], exp[~finite])
-    _assert_indices(act[finite][None], exp[finite][None], scores[finite][None], tol=1e-4, ordered=False)
+    _assert_indices(act[finite][None], exp[finite][None], scores[finite][None], tol=1e-4, ordered=False,
+                    max_near_ties=2)
     if dtype == torch.bfloat16:
         # q·k of key 17 in slice 1 is about +-2^100·q[0]: first or excluded
         top = (qf[1, :, 0] > 0)
@@ -513,24 +520,67 @@ def test_routed_bf16_full_configuration_sampled_rows():
 # --- full-size configurations, sampled rows against the oracle --------------------
 
 
+def _oracle_slice_backward(q, k, v, idx, do, scale, chunk=2048):
+    """Float64 oracle gradients of one whole slice, in row chunks (dK/dV summed)."""
+    dq = np.zeros(q.shape, np.float64)
+    dk = np.zeros(k.shape, np.float64)
+    dv = np.zeros(v.shape, np.float64)
+    for r0 in range(0, q.shape[0], chunk):
+        r1 = min(q.shape[0], r0 + chunk)
+        a, b, c = oracle.topk_attention_backward(q[None, r0:r1], k[None], v[None], idx[None, r0:r1],
+                                                 do[None, r0:r1], scale)
+        dq[r0:r1] = a[0]
+        dk += b[0]
+        dv += c[0]
+    return dq, dk, dv
+
+
 @pytest.mark.parametrize(("b", "h", "n", "m", "d", "k"), [(8, 8, 4096, 4096, 64, 32), (16, 8, 16384, 16384, 64, 64)])
-def test_full_size_bf16_sampled_rows(b, h, n, m, d, k):
+def test_full_size_bf16_index_sets_outputs_and_gradients(b, h, n, m, d, k):
+    # The benchmarked shapes at full size (configuration 2: B=8 H=8 N=M=4096
+    # k=32; configuration 4: B=16 H=8 N=M=16384 k=64), bf16.  For sampled rows
+    # of four slices: the selected index SET equals the oracle's except where
+    # the keys that differ score within 1e-4 of the oracle's k-th score (at
+    # most 1 % of the rows may use that allowance), outputs and LSE, and dQ
+    # on the GPU's support.  For one whole slice: dK and dV against the
+    # float64 oracle.  The public API's output equals the op's bit for bit.
     gen = torch.Generator(device=DEV).manual_seed(2024)
     q = torch.randn(b, h, n, d, device=DEV, generator=gen).to(torch.bfloat16)
     kk = torch.randn(b, h, m, d, device=DEV, generator=gen).to(torch.bfloat16)
     v = torch.randn(b, h, m, d, device=DEV, generator=gen).to(torch.bfloat16)
-    out = fused_topk_attention(q, kk, v, k)
+    do = torch.randn(b, h, n, d, device=DEV, generator=gen).to(torch.bfloat16)
+    scale = 1 / math.sqrt(d)
+    from sparsedict_b200 import _ops
+
+    s_all = b * h
+    q3, k3, v3, do3 = (t.reshape(s_all, -1, d) for t in (q, kk, v, do))
+    out, idx, lse, _ = _ops.topk_attn_fwd(q3, k3, v3, k, scale)
+    assert torch.equal(fused_topk_attention(q, kk, v, k).reshape(out.shape), out)
+    idx3, lse2 = idx.view(s_all, n, k), lse.view(s_all, n)
+    dq, dk_acc, dv_acc = _ops.topk_attn_bwd(q3, k3, v3, do3, idx3, lse2, scale)
+    assert _native.device_status(clear=True) == 0
     rng = np.random.default_rng(1)
-    slices = rng.choice(b * h, 4, replace=False)
-    rows = rng.choice(n, 48, replace=False)
-    qf, kf, vf = (t.reshape(b * h, -1, d) for t in (q, kk, v))
+    slices = rng.choice(s_all, 4, replace=False)
+    rows = np.sort(rng.choice(n, 64, replace=False))
+    near = 0
     for s in slices:
-        qs = qf[s, rows].float().cpu().numpy()[None]
-        ks = kf[s].float().cpu().numpy()[None]
-        vs = vf[s].float().cpu().numpy()[None]
-        o, idx, _, _ = oracle.topk_attention_forward(qs, ks, vs, k, 1 / math.sqrt(d))
-        got = out.reshape(b * h, n, d)[s, rows].float().cpu().numpy()
-        np.testing.assert_allclose(got, o[0], rtol=2e-2, atol=2e-2)
+        qs, ks, vs, ds = (t[s].float().cpu().numpy() for t in (q3, k3, v3, do3))
+        o, oidx, olse, _ = oracle.topk_attention_forward(qs[None, rows], ks[None], vs[None], k, scale)
+        gidx = idx3[s, rows].cpu().numpy()
+        sc = np.einsum("nd,md->nm", qs[rows].astype(np.float64), ks.astype(np.float64)) * scale
+        near += _assert_indices(gidx[None], oidx, sc[None], tol=1e-4, ordered=False, max_near_ties=len(rows))
+        np.testing.assert_allclose(out[s, rows].float().cpu().numpy(), o[0], rtol=2e-2, atol=2e-2)
+        np.testing.assert_allclose(lse2[s, rows].cpu().numpy(), olse[0], rtol=1e-5, atol=1e-5)
+        rdq, _, _ = oracle.topk_attention_backward(qs[None, rows], ks[None], vs[None], gidx[None], ds[None, rows],
+                                                   scale)
+        got = dq[s, rows].float().cpu().numpy()
+        assert np.abs(got - rdq[0]).max() <= 2e-2 * max(1.0, np.abs(rdq).max())
+    assert near <= max(1, len(slices) * len(rows) // 100), f"{near} near-tie rows"
+    s0 = int(slices[0])
+    qs, ks, vs, ds = (t[s0].float().cpu().numpy() for t in (q3, k3, v3, do3))
+    _, rdk, rdv = _oracle_slice_backward(qs, ks, vs, idx3[s0].cpu().numpy(), ds, scale)
+    for got, exp in ((dk_acc[s0], rdk), (dv_acc[s0], rdv)):
+        np.testing.assert_allclose(got.float().cpu().numpy(), exp, rtol=1e-3, atol=1e-3 * np.abs(exp).max())
 
 
 def test_routed_bf16_backward_vs_oracle():
@@ -714,3 +764,99 @@ def test_straight_through_topk_all_float_dtypes(dtype):
     ov, oi = oracle.topk_order(scores.double().cpu().numpy(), 19)
     assert np.array_equal(idx.cpu().numpy(), oi)
     np.testing.assert_array_equal(vals.double().cpu().numpy(), ov)
+
+
+# --- deterministic key-major backward ---------------------------------------------
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize(("bh", "n", "m", "k"), [(2, 384, 1000, 32), (3, 257, 2000, 7), (2, 100, 129, 1),
+                                                 (2, 300, 4096, 64), (1, 70, 64, 64)])
+def test_key_major_backward_matches_oracle(dtype, bh, n, m, k):
+    # The direct backward (dq, dK, dV written once in the input dtype) against
+    # the float64 oracle on the support the forward selected.
+    from sparsedict_b200 import _ops
+
+    g = torch.Generator().manual_seed(bh * 1000 + n + m + k)
+    q, kk, v, do = (torch.randn(bh, x, 64, generator=g).to(dtype).to(DEV) for x in (n, m, m, n))
+    scale = 0.125
+    _, idx, lse, _ = _ops.topk_attn_fwd(q, kk, v, k, scale)
+    dq, dk, dv = _ops.topk_attn_bwd_direct(q, kk, v, do, idx.view(bh, n, k), lse.view(bh, n), scale)
+    assert dq.dtype == dk.dtype == dv.dtype == dtype
+    assert _native.device_status(clear=True) == 0
+    qf, kf, vf, dof = (t.float().cpu().numpy() for t in (q, kk, v, do))
+    ref = oracle.topk_attention_backward(qf, kf, vf, idx.view(bh, n, k).cpu().numpy(), dof, scale)
+    for got, exp in zip((dq, dk, dv), ref):
+        got = got.float().cpu().numpy()
+        assert np.abs(got - exp).max() <= 2e-2 * max(1.0, np.abs(exp).max())
+    # keys that no row selected get exact zeros
+    sel = np.zeros((bh, m), bool)
+    np.put_along_axis(sel, idx.view(bh, -1).long().cpu().numpy(), True, axis=1)
+    assert not dk.float().cpu().numpy()[~sel].any() and not dv.float().cpu().numpy()[~sel].any()
+
+
+def test_key_major_backward_is_bitwise_deterministic():
+    # dK/dV are written once per key in a fixed summation order: two runs agree
+    # bit for bit (the scatter with atomics it replaces does not).
+    from sparsedict_b200 import _ops
+
+    g = torch.Generator(device=DEV).manual_seed(99)
+    bh, n, m, k = 4, 2048, 4096, 64
+    q, kk, v, do = (torch.randn(bh, x, 64, device=DEV, generator=g).to(torch.bfloat16) for x in (n, m, m, n))
+    _, idx, lse, _ = _ops.topk_attn_fwd(q, kk, v, k, 0.125)
+    idx, lse = idx.view(bh, n, k), lse.view(bh, n)
+    first = _ops.topk_attn_bwd_direct(q, kk, v, do, idx, lse, 0.125)
+    for _ in range(2):
+        again = _ops.topk_attn_bwd_direct(q, kk, v, do, idx, lse, 0.125)
+        for a, b in zip(first, again):
+            assert torch.equal(a, b)
+
+
+def test_key_major_backward_skips_given_up_rows():
+    # Index -1 (a forward row the bounded wait gave up on) contributes nothing
+    # and raises no status bit; the other rows are unaffected.
+    from sparsedict_b200 import _ops
+
+    g = torch.Generator(device=DEV).manual_seed(5)
+    bh, n, m, k = 2, 256, 1024, 16
+    q, kk, v, do = (torch.randn(bh, x, 64, device=DEV, generator=g).to(torch.bfloat16) for x in (n, m, m, n))
+    _, idx, lse, _ = _ops.topk_attn_fwd(q, kk, v, k, 0.125)
+    idx, lse = idx.view(bh, n, k).clone(), lse.view(bh, n)
+    ref = _ops.topk_attn_bwd_direct(q, kk, v, do, idx, lse, 0.125)
+    do2 = do.clone()
+    do2[0, 7] = 0
+    base = _ops.topk_attn_bwd_direct(q, kk, v, do2, idx, lse, 0.125)
+    idx[0, 7] = -1
+    got = _ops.topk_attn_bwd_direct(q, kk, v, do, idx, lse, 0.125)
+    assert _native.device_status(clear=True) == 0
+    assert not got[0][0, 7].any()
+    assert torch.equal(got[0][:, 8:], ref[0][:, 8:])
+    # dK/dV without row 7 = dK/dV with row 7's upstream gradient zeroed (its dS
+    # and P·dout are zero there); the per-key lists shift, so not bit for bit
+    for a, b in ((got[1], base[1]), (got[2], base[2])):
+        assert (a.float() - b.float()).abs().max() <= 1e-2 * max(1.0, float(b.float().abs().max()))
+
+
+def test_deterministic_switch_routes_autograd_through_key_major_kernels():
+    # With the switch on, the public autograd path's dK/dV are bit-identical
+    # across runs and equal to the direct key-major entry point's.
+    from sparsedict_b200 import _ops, set_deterministic_backward
+
+    g = torch.Generator(device=DEV).manual_seed(41)
+    q, kk, v, do = (torch.randn(1, 2, x, 64, device=DEV, generator=g).to(torch.bfloat16) for x in (1024, 2048, 2048, 1024))
+    try:
+        set_deterministic_backward(True)
+        runs = []
+        for _ in range(2):
+            qd, kd, vd = (t.clone().requires_grad_(True) for t in (q, kk, v))
+            out = fused_topk_attention(qd, kd, vd, 32)
+            runs.append(torch.autograd.grad(out, (qd, kd, vd), do))
+    finally:
+        set_deterministic_backward(False)
+    for a, b in zip(*runs):
+        assert torch.equal(a, b)
+    _, idx, lse, _ = _ops.topk_attn_fwd(q.reshape(2, -1, 64), kk.reshape(2, -1, 64), v.reshape(2, -1, 64), 32, 1 / 8)
+    ref = _ops.topk_attn_bwd_direct(q.reshape(2, -1, 64), kk.reshape(2, -1, 64), v.reshape(2, -1, 64),
+                                    do.reshape(2, -1, 64), idx.view(2, -1, 32), lse.view(2, -1), 1 / 8)
+    for a, b in zip(runs[0], ref):
+        assert torch.equal(a.reshape(b.shape), b)

@@ -17,7 +17,7 @@ import torch
 
 import _sharded_workers as W
 import oracle
-from sparsedict_b200.sharded import ShardedTopKAttention, ShardPlan
+from sparsedict_b200.sharded import ShardedTopKAttention, ShardPlan, pick_buckets
 
 
 def _free_port():
@@ -46,12 +46,21 @@ def _run(world, reduce, fail_rank=-1, limit=60):
 
 
 def test_shard_plan_splits_whole_slices():
+    # one bucket: the plain contiguous split
     plans = [ShardPlan(128, 8, r) for r in range(8)]
-    assert [(p.begin, p.end) for p in plans] == [(16 * r, 16 * r + 16) for r in range(8)]
+    assert [p.owned() for p in plans] == [list(range(16 * r, 16 * r + 16)) for r in range(8)]
+    # four buckets: bucket b is slices [32b, 32b + 32), rank r owns [32b + 4r, 32b + 4r + 4)
+    plans = [ShardPlan(128, 8, r, buckets=4) for r in range(8)]
+    assert plans[3].owned() == [32 * b + 12 + i for b in range(4) for i in range(4)]
+    assert plans[3].block(2) == (64, 96) and plans[3].owned_range(2) == (76, 80)
+    assert plans[3].local_range(2) == (8, 12) and plans[3].global_slice(9) == 77
     with pytest.raises(ValueError):
         ShardPlan(10, 4, 0)
     with pytest.raises(ValueError):
         ShardPlan(8, 2, 2)
+    with pytest.raises(ValueError):
+        ShardPlan(16, 2, 0, buckets=3)
+    assert pick_buckets(128, 8, 4) == 4 and pick_buckets(24, 4, 4) == 3 and pick_buckets(8, 8, 4) == 1
 
 
 @pytest.mark.parametrize("reduce", ["allreduce", "allgather", "none"])
@@ -62,9 +71,8 @@ def test_two_ranks_match_single_process(reduce):
     scale = 1 / np.sqrt(W.D)
     o, idx, _, _ = oracle.topk_attention_forward(q, k, v, W.TOPK, scale)
     gq, gk, gv = oracle.topk_attention_backward(q, k, v, idx, do, scale)
-    per = W.S // 2
     for _, rank, out, dq, dk, dv in res:
-        rows = slice(rank * per, (rank + 1) * per)
+        rows = ShardPlan(W.S, 2, rank, buckets=2).owned()
         np.testing.assert_allclose(out, o[rows], atol=1e-12)
         np.testing.assert_allclose(dq, gq[rows], atol=1e-12)
         if reduce == "none":
@@ -82,25 +90,21 @@ def test_failed_rank_makes_peer_collective_fail_not_hang():
     assert elapsed < 55
 
 
-@pytest.mark.parametrize("slices,world,buckets", [(16, 2, 4), (40, 8, 2), (15, 3, 2), (128, 8, 4), (7, 7, 3)])
-def test_bucket_major_layout_is_a_bijection(slices, world, buckets):
-    # every (rank, local slice) maps to its own accumulator row, bucket j of all
-    # ranks is one contiguous block, and each rank's part of it is contiguous
-    class _Kernels:
-        def acc_dtype(self, dtype):
-            return torch.float32
-
+@pytest.mark.parametrize("slices,world,buckets", [(16, 2, 4), (48, 8, 2), (18, 3, 2), (128, 8, 4), (7, 7, 1)])
+def test_bucket_interleaved_ownership_is_a_partition(slices, world, buckets):
+    # every global slice is owned by exactly one (rank, local slice); bucket b
+    # of all ranks is one contiguous block in slice order and each rank's part
+    # of it is contiguous, so the exchanged buffer needs no reordering
     seen = {}
     for rank in range(world):
-        runner = ShardedTopKAttention(ShardPlan(slices, world, rank), 4, 2, 2, 1, torch.float32, "cpu",
-                                      reduce="allreduce", buckets=buckets, kernels=_Kernels())
-        assert runner._bucket_major == (world > 1)
-        for lo, hi in runner._bucket_ranges():
-            a0, a1 = runner._acc_range(lo, hi, rank)
-            assert a1 - a0 == hi - lo
-            if world > 1:
-                assert world * lo <= a0 and a1 <= world * hi
-            for i, row in enumerate(range(a0, a1)):
-                assert row not in seen
-                seen[row] = (rank, lo + i)
+        plan = ShardPlan(slices, world, rank, buckets=buckets)
+        for b in range(buckets):
+            b0, b1 = plan.block(b)
+            g0, g1 = plan.owned_range(b)
+            lo, hi = plan.local_range(b)
+            assert b0 <= g0 < g1 <= b1 and g1 - g0 == hi - lo
+            for i in range(lo, hi):
+                g = plan.global_slice(i)
+                assert g == g0 + i - lo and g not in seen
+                seen[g] = (rank, i)
     assert sorted(seen) == list(range(slices))
