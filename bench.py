@@ -13,6 +13,12 @@ work is fixed).  Inputs (268 MB each) are larger than the 126 MB L2.
 Prints one JSON line (rank 0).  ``--impl reference`` times the CPU
 restatement of the reference path (dense scores, hard top-k, softmax,
 gather, dense autograd-style backward) on this host's cores instead.
+
+``--workload routed`` measures the dictionary-MoE configuration instead:
+N=16384 tokens, d=64, 8 experts of M=1024 atoms (keys = values), top-1
+routing by the argmax of N(0,1) router logits, k=16 within the expert, bf16
+forward and backward through ``routed_dictionary_attention`` (one replica
+per GPU: the routed op is not sharded).
 """
 
 from __future__ import annotations
@@ -35,6 +41,10 @@ METRIC = "top-k attn fwd+bwd queries/sec @1/2/4/8 B200; % tensor-pipe & HBM roof
 UNIT = "queries/s"
 CFG = dict(B=16, H=8, N=16384, M=16384, d=64, k=64)
 WORKLOAD = "sharded bf16 fwd+bwd, B=16 H=8 N=M=16384 d=64 k=64"
+ROUTED_METRIC = "routed top-k dictionary attn fwd+bwd queries/sec (B200)"
+ROUTED_CFG = dict(N=16384, d=64, E=8, M=1024, k=16)
+ROUTED_WORKLOAD = "routed dictionary bf16 fwd+bwd, N=16384 tokens d=64, E=8 experts x M=1024 atoms, top-1, k=16"
+L2_FLUSH_BYTES = 256 << 20
 
 
 def roofline_terms(b, h, n, m, d, k, elem):
@@ -388,6 +398,183 @@ def check_parity(c, world, rank, dev, plan, runner, keys, values, q_rows, dout_r
                        "public API on that slice alone"}
 
 
+def routed_inputs(torch, dev, seed=1234):
+    c = ROUTED_CFG
+    gen = torch.Generator(device="cpu").manual_seed(seed)
+    q = torch.randn(c["N"], c["d"], generator=gen).to(torch.bfloat16)
+    atoms = (torch.randn(c["E"], c["M"], c["d"], generator=gen) / math.sqrt(c["d"])).to(torch.bfloat16)
+    logits = torch.randn(c["N"], c["E"], generator=gen)
+    do = torch.randn(c["N"], c["d"], generator=gen).to(torch.bfloat16)
+    return q, atoms, logits, do
+
+
+def cpu_routed_sample(tokens=ROUTED_CFG["N"], seed=0):
+    """The CPU restatement of the routed path on ``tokens`` tokens of the workload
+    (all 8 dictionaries), forward and backward.  Returns (queries/s, seconds, description)."""
+    import numpy as np
+
+    import oracle
+
+    c = ROUTED_CFG
+    rng = np.random.default_rng(seed)
+    q = oracle.round_to_bf16(rng.standard_normal((tokens, c["d"]), dtype=np.float32))
+    atoms = oracle.round_to_bf16(rng.standard_normal((c["E"], c["M"], c["d"]), dtype=np.float32) / 8)
+    logits = rng.standard_normal((tokens, c["E"]), dtype=np.float32)
+    do = rng.standard_normal((tokens, c["d"]), dtype=np.float32)
+    t0 = time.perf_counter()
+    experts = oracle.moe_route_top1(logits)
+    _, idx, _ = oracle.moe_topk_attention_forward(q, atoms, experts, c["k"], 1.0)
+    oracle.moe_topk_attention_backward(q, atoms, experts, idx, do, 1.0)
+    dt = time.perf_counter() - t0
+    return tokens / dt, dt, f"{tokens} tokens routed over E={c['E']} dictionaries of M={c['M']} atoms, d={c['d']}, " \
+                            f"k={c['k']}, fp32 on bf16-rounded inputs, fwd+bwd" + \
+        ("" if tokens == c["N"] else "; queries/s extrapolated")
+
+
+def run_routed_arm(args):
+    import torch
+    import torch.distributed as dist
+
+    from sparsedict_b200 import _native, routed_dictionary_attention
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        for _ in range(args.warmup):
+            cpu_routed_sample()
+        rates, secs = [], []
+        for i in range(args.steps):
+            r, sec, desc = cpu_routed_sample(seed=i + 1)
+            rates.append(r)
+            secs.append(sec)
+        value = statistics.median(rates)
+        print(json.dumps({
+            "metric": ROUTED_METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * statistics.median(secs),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": ROUTED_WORKLOAD, **ROUTED_CFG},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count() or 1, "kind": "port",
+                             "sample": desc},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}), flush=True)
+        return 0
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    _native.load()
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    c = ROUTED_CFG
+    hq, ha, hl, hd = routed_inputs(torch, dev)
+    q = hq.to(dev).requires_grad_(True)
+    atoms = ha.to(dev).requires_grad_(True)
+    logits, do = hl.to(dev), hd.to(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def step():
+        out = routed_dictionary_attention(q, atoms, logits, c["k"], 1.0)
+        return (out,) + torch.autograd.grad(out, (q, atoms), grad_outputs=do)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    stream = torch.cuda.current_stream(dev)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    with ClockSampler(local, dev) as clocks:
+        barrier()
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)  # evict the previous step's inputs and outputs from L2 (outside the events)
+            ev[i][0].record(stream)
+            out = routed_dictionary_attention(q, atoms, logits, c["k"], 1.0)
+            ev[i][1].record(stream)
+            torch.autograd.grad(out, (q, atoms), grad_outputs=do)
+            ev[i][2].record(stream)
+        barrier()
+    elapsed = sum(e[0].elapsed_time(e[2]) for e in ev) / 1000.0
+    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    t = torch.tensor([elapsed, fwd_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed, fwd_ms = float(t[0]), float(t[1])
+    value = world * c["N"] * args.steps / elapsed
+
+    e2e = None
+    if not args.skip_e2e:
+        # public API end to end: pinned host inputs in, fwd+bwd, O, dQ and dDict back to pinned host
+        pins = [t.pin_memory() for t in (hq, ha, hl, hd)]
+        outs = [torch.empty((c["N"], c["d"]), dtype=torch.bfloat16).pin_memory(),
+                torch.empty((c["N"], c["d"]), dtype=torch.bfloat16).pin_memory(),
+                torch.empty((c["E"], c["M"], c["d"]), dtype=torch.bfloat16).pin_memory()]
+        h2d = sum(t.numel() * t.element_size() for t in pins)
+        d2h = sum(t.numel() * t.element_size() for t in outs)
+
+        def e2e_step():
+            dq_, da_, dl, dd = (t.to(dev, non_blocking=True) for t in pins)
+            dq_.requires_grad_(True)
+            da_.requires_grad_(True)
+            o = routed_dictionary_attention(dq_, da_, dl, c["k"], 1.0)
+            g = torch.autograd.grad(o, (dq_, da_), grad_outputs=dd)
+            for h, dsrc in zip(outs, (o.detach(), g[0], g[1])):
+                h.copy_(dsrc, non_blocking=True)
+
+        for _ in range(3):
+            e2e_step()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        barrier()
+        et = torch.tensor([e0.elapsed_time(e1) / 1000.0], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(et, op=dist.ReduceOp.MAX)
+        e2e = {"value": world * c["N"] * args.e2e_steps / float(et[0]), "unit": UNIT,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "api": "sparsedict_b200.routed_dictionary_attention + torch.autograd.grad"}
+
+    peaks = load_peaks()
+    flops = 2.0 * c["N"] * c["M"] * c["d"]  # each token against the M atoms of its expert
+    achieved = flops / (fwd_ms / 1000.0) / 1e12
+    peak_tc = peaks["bf16_tflops"]
+    line = {
+        "metric": ROUTED_METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000 * elapsed / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": ROUTED_WORKLOAD, **c, "parallelism": f"replicas{world}",
+                   "l2": f"flushed between steps ({L2_FLUSH_BYTES >> 20} MB write outside the timed events)"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tc, "unit": "TFLOP/s",
+                     "frac": achieved / peak_tc, "traffic": None,
+                     "kernel": "forward (routing + stream + finish kernels)", "fwd_ms": fwd_ms,
+                     "peak_source": f"{peaks['source']} bf16_tflops"},
+        # per step: the router's count, scan and place kernels, the forward's stream
+        # and finishing kernels, the backward's scatter kernel and the
+        # dictionary-gradient conversion
+        "gpu_launches": 7 * args.steps,
+    }
+    if e2e is not None:
+        line["e2e"] = e2e
+    if rank == 0 and not args.skip_cpu:
+        r, sec, desc = cpu_routed_sample()
+        line["cpu_baseline"] = {"value": r, "unit": UNIT, "cores": os.cpu_count() or 1, "kind": "port",
+                                "sample": desc}
+    line["clocks"] = clocks.summary()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return 0
+
+
 def run_native_arm(args):
     import torch
     import torch.distributed as dist
@@ -536,9 +723,12 @@ def main():
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-parity", action="store_true")
+    ap.add_argument("--workload", choices=["sharded", "routed"], default="sharded")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.workload == "routed":
+        return run_routed_arm(args)
     if args.impl == "reference":
         return run_reference_arm(args)
     return run_native_arm(args)

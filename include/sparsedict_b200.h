@@ -6,8 +6,9 @@
  * cudaStream_t passed as void* (NULL = the legacy default stream).  No call
  * synchronises the host or throws: each returns 0 (SDK_OK) or one of the
  * status codes below; sdk_status_string() names it.  No call allocates
- * device memory except sdk_topk_attn_fwd on the tensor-core path, which takes
- * stream-ordered scratch from a memory pool of this library (kept for reuse);
+ * device memory except sdk_topk_attn_fwd on the tensor-core path and
+ * sdk_route_top1 (4 bytes per expert per 256 rows), which take stream-ordered
+ * scratch from a memory pool of this library (kept for reuse);
  * sdk_topk_attn_fwd_ws is the same forward on the caller's scratch.
  *
  * Layout conventions (the reference's flattened layout,
@@ -104,7 +105,9 @@ int sdk_topk_attn_fwd(const void* q, const void* k, const void* v, void* out, in
  * candidate list (160 four-byte entries and a count) from its streaming
  * kernel to its finishing kernel.  Returns the bytes for `rows` query rows
  * (slices*n, or the grouped row count), 0 when the call will not take that
- * path (`grouped`: row_offsets or row_index will be passed).  The reference's
+ * path.  `grouped` (row_offsets or row_index will be passed) does not change
+ * the size: grouped slices take the same path with the same scratch per row.
+ * The reference's
  * wrapper allocates its intermediate top-k buffers with torch
  * (fused_topk_attn.py:1012-1017); callers that own their memory allocate this
  * and pass it to sdk_topk_attn_fwd_ws.
@@ -286,10 +289,53 @@ int sdk_topk_aggregate(const void* top_scores, const void* top_idx, const void* 
  * argmax_e logits[i, e] (lowest e on ties; models/modules/router.py:139-145),
  * then a stable counting sort: order[] lists rows grouped by expert and
  * offsets[e] .. offsets[e+1] delimits expert e's rows in it.
- * offsets needs experts+1 entries.  logits are float32.
+ * offsets needs experts+1 entries.  logits are float32; experts <= 16.
+ * Three launches (per-block counts, their scan, placement); the block counts
+ * live in stream-ordered scratch from the library pool.
  */
 int sdk_route_top1(const float* logits, int64_t n, int32_t experts, int32_t* expert,
                    int32_t* order, int32_t* offsets, void* stream);
+
+/*
+ * Sparse top-k attention over given dense scores, after the selection
+ * (sdk_topk_select): the body of sparse_topk_attention
+ * (models/modules/topk_select.py:146-161).  For each of `rows` score rows with
+ * selected scores top_scores[r, j] at keys top_idx[r, j] (int64, j < topk):
+ *   out[r]           = sum_j softmax(top_scores[r])_j values[b, top_idx[r, j]]
+ *   weights[r, :]    = 0 except the softmax weights at the selected keys
+ *   masked_scores[r] = -inf except the selected scores at the selected keys
+ * with values [batches, m, dv] and b = r / rows_per_batch (rows_per_batch 0:
+ * one shared [m, dv] matrix).  top_scores, weights and masked_scores are in
+ * score_dtype; values and out in out_dtype, which is score_dtype or the wider
+ * of the two float types (F32 for F16/BF16 scores, F64).  topk <= 256.
+ */
+int sdk_sparse_topk_attn_fwd(const void* top_scores, const int64_t* top_idx, const void* values, void* out,
+                             void* weights, void* masked_scores, int64_t rows, int64_t rows_per_batch,
+                             int32_t topk, int64_t m, int32_t dv, int32_t score_dtype, int32_t out_dtype,
+                             void* stream);
+
+/*
+ * Gradient of sdk_sparse_topk_attn_fwd with respect to the dense scores and
+ * the values, given the gradients of out (grad_out, out_dtype) and, nullable,
+ * of weights and masked_scores (dense, score_dtype).  grad_scores [rows, m]
+ * (score_dtype) is written in full (zero off the selection); the values'
+ * gradient is added to grad_values_acc [batches, m, dv] (float32, float64
+ * when out_dtype is F64), which the caller zeroes first.
+ */
+int sdk_sparse_topk_attn_bwd(const void* top_scores, const int64_t* top_idx, const void* values,
+                             const void* grad_out, const void* grad_weights, const void* grad_masked,
+                             void* grad_scores, void* grad_values_acc, int64_t rows, int64_t rows_per_batch,
+                             int32_t topk, int64_t m, int32_t dv, int32_t score_dtype, int32_t out_dtype,
+                             void* stream);
+
+/*
+ * dst[r, :] = fill, then dst[r, idx[r, j]] = src[r, j] for rows r < rows,
+ * j < k (idx int64, dst [rows, m], src [rows, k], both `dtype`): the hard
+ * top-k mask (fill -inf, topk_select.py:94-103) and the straight-through
+ * gradient of the selected scores (fill 0, :33-45).
+ */
+int sdk_fill_scatter(const void* src, const int64_t* idx, void* dst, int64_t rows, int32_t k, int64_t m,
+                     double fill, int32_t dtype, void* stream);
 
 #ifdef __cplusplus
 }

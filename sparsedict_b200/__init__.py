@@ -20,6 +20,7 @@ from .kernels.fused_topk_attn import (
 from .kernels.hybrid_topk import _hybrid_topk_attention_with_aux, hybrid_topk_attention
 from ._ops import deterministic_backward, set_deterministic_backward
 from .mixture import GatedMixtureFunction, gated_mixture_attention
+from .routed import RoutedDictionaryAttention, routed_dictionary_attention
 from .sharded import ShardedTopKAttention, ShardPlan
 
 __all__ = [
@@ -30,6 +31,8 @@ __all__ = [
     "set_deterministic_backward",
     "GatedMixtureFunction",
     "gated_mixture_attention",
+    "RoutedDictionaryAttention",
+    "routed_dictionary_attention",
     "fused_topk_attention",
     "hybrid_topk_attention",
     "tiled_affinity",

@@ -57,6 +57,9 @@ SIGNATURES = {
     "sdk_topk_select": [_p, _p, _p, _i64, _i64, _i64, _i32, _i32, _p],
     "sdk_topk_aggregate": [_p, _p, _p, _p, _i64, _i32, _i64, _i32, _i64, _i64, _i64, _i32, _i32, _i32, _p],
     "sdk_route_top1": [_p, _i64, _i32, _p, _p, _p, _p],
+    "sdk_sparse_topk_attn_fwd": [_p, _p, _p, _p, _p, _p, _i64, _i64, _i32, _i64, _i32, _i32, _i32, _p],
+    "sdk_sparse_topk_attn_bwd": [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i32, _i64, _i32, _i32, _i32, _p],
+    "sdk_fill_scatter": [_p, _p, _p, _i64, _i32, _i64, _f64, _i32, _p],
 }
 _RESTYPES = {"sdk_status_string": ctypes.c_char_p, "sdk_last_cuda_error": ctypes.c_char_p,
              "sdk_topk_attn_fwd_workspace_size": ctypes.c_size_t, "sdk_topk_attn_bwd_workspace_size": ctypes.c_size_t}

@@ -18,7 +18,8 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libsparsedict_b200.so"
-SOURCES = ["capi.cu", "fwd_generic.cu", "fwd_tc.cu", "bwd.cu", "bwd_km.cu", "stages.cu", "bwd_noalloc.cu"]
+SOURCES = ["capi.cu", "fwd_generic.cu", "fwd_tc.cu", "bwd.cu", "bwd_km.cu", "stages.cu", "select_attn.cu",
+           "bwd_noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

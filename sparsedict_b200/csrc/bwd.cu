@@ -45,16 +45,6 @@ template <typename Acc> struct BwdArgs {
   int segs;
 };
 
-__device__ __forceinline__ int64_t slice_of_row(const SliceGeometry& g, int64_t r) {
-  if (!g.row_offsets) return r / g.n;
-  int64_t lo = 0, hi = g.slices - 1;
-  while (lo < hi) {  // last slice whose first row is <= r
-    const int64_t mid = (lo + hi + 1) >> 1;
-    if ((int64_t)g.row_offsets[mid] <= r) lo = mid; else hi = mid - 1;
-  }
-  return lo;
-}
-
 __device__ __forceinline__ void red_add(float* p, float x) { atomicAdd(p, x); }
 __device__ __forceinline__ void red_add(double* p, double x) { atomicAdd(p, x); }
 

@@ -9,6 +9,8 @@
 #include <cstdio>
 #include <cstring>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -71,6 +73,30 @@ unsigned int* device_status_ptr() {
     return nullptr;
   }
   return static_cast<unsigned int*>(p);
+}
+
+// Stream-ordered scratch (the tensor-core forward's candidate buffer, the
+// router's block counts): a memory pool of this library per device that keeps
+// what it has reserved (no release at synchronisation), so repeated calls
+// reuse the same device memory.
+cudaMemPool_t scratch_pool() {
+  static std::mutex mu;
+  static cudaMemPool_t pools[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!pools[dev]) {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t pool = nullptr;
+    if (cudaMemPoolCreate(&pool, &props) != cudaSuccess) return nullptr;
+    uint64_t keep = ~0ull;
+    if (cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep) != cudaSuccess) return nullptr;
+    pools[dev] = pool;
+  }
+  return pools[dev];
 }
 
 }  // namespace sdk
@@ -333,6 +359,43 @@ int sdk_topk_aggregate(const void* top_scores, const void* top_idx, const void* 
   return finish(topk_aggregate(top_scores, top_idx, values, out, rows, topk, m, dv, score_row_stride,
                                idx_row_stride, value_row_stride, score_dtype, idx_bits, value_dtype,
                                device_status_ptr(), static_cast<cudaStream_t>(stream)));
+}
+
+int sdk_sparse_topk_attn_fwd(const void* top_scores, const int64_t* top_idx, const void* values, void* out,
+                             void* weights, void* masked_scores, int64_t rows, int64_t rows_per_batch, int32_t topk,
+                             int64_t m, int32_t dv, int32_t score_dtype, int32_t out_dtype, void* stream) {
+  if (!top_scores || !top_idx || !values || !out || !weights || !masked_scores) return SDK_ERR_INVALID_ARGUMENT;
+  if (rows < 0 || rows_per_batch < 0 || topk < 1 || topk > 256 || topk > m || dv < 1) return SDK_ERR_INVALID_ARGUMENT;
+  if (!dtype_ok(score_dtype) || !dtype_ok(out_dtype)) return SDK_ERR_INVALID_ARGUMENT;
+  if (int rc = check_device()) return rc;
+  if (rows == 0) return SDK_OK;
+  return finish(sparse_attn_forward(top_scores, top_idx, values, out, weights, masked_scores, rows, rows_per_batch,
+                                    topk, m, dv, score_dtype, out_dtype, device_status_ptr(),
+                                    static_cast<cudaStream_t>(stream)));
+}
+
+int sdk_sparse_topk_attn_bwd(const void* top_scores, const int64_t* top_idx, const void* values, const void* grad_out,
+                             const void* grad_weights, const void* grad_masked, void* grad_scores,
+                             void* grad_values_acc, int64_t rows, int64_t rows_per_batch, int32_t topk, int64_t m,
+                             int32_t dv, int32_t score_dtype, int32_t out_dtype, void* stream) {
+  if (!top_scores || !top_idx || !values || !grad_out || !grad_scores || !grad_values_acc)
+    return SDK_ERR_INVALID_ARGUMENT;
+  if (rows < 0 || rows_per_batch < 0 || topk < 1 || topk > 256 || topk > m || dv < 1) return SDK_ERR_INVALID_ARGUMENT;
+  if (!dtype_ok(score_dtype) || !dtype_ok(out_dtype)) return SDK_ERR_INVALID_ARGUMENT;
+  if (int rc = check_device()) return rc;
+  if (rows == 0) return SDK_OK;
+  return finish(sparse_attn_backward(top_scores, top_idx, values, grad_out, grad_weights, grad_masked, grad_scores,
+                                     grad_values_acc, rows, rows_per_batch, topk, m, dv, score_dtype, out_dtype,
+                                     device_status_ptr(), static_cast<cudaStream_t>(stream)));
+}
+
+int sdk_fill_scatter(const void* src, const int64_t* idx, void* dst, int64_t rows, int32_t k, int64_t m, double fill,
+                     int32_t dtype, void* stream) {
+  if (!src || !idx || !dst || rows < 0 || k < 1 || m < 1 || !dtype_ok(dtype)) return SDK_ERR_INVALID_ARGUMENT;
+  if (int rc = check_device()) return rc;
+  if (rows == 0) return SDK_OK;
+  return finish(fill_scatter(src, idx, dst, rows, k, m, fill, dtype, device_status_ptr(),
+                             static_cast<cudaStream_t>(stream)));
 }
 
 int sdk_route_top1(const float* logits, int64_t n, int32_t experts, int32_t* expert, int32_t* order,

@@ -124,6 +124,7 @@ enum DeviceStatusBits : unsigned int {
 };
 
 unsigned int* device_status_ptr();  // defined in capi.cu
+cudaMemPool_t scratch_pool();       // this library's stream-ordered scratch pool (capi.cu)
 
 // ------------------------------------------------------ launch geometry ---
 struct SliceGeometry {
@@ -136,6 +137,18 @@ struct SliceGeometry {
 
 __device__ __forceinline__ int64_t slice_row_begin(const SliceGeometry& g, int64_t s) {
   return g.row_offsets ? (int64_t)g.row_offsets[s] : s * g.n;
+}
+
+// The slice that holds logical row r (grouped: the last slice whose first
+// row is <= r, which skips empty slices).
+__device__ __forceinline__ int64_t slice_of_row(const SliceGeometry& g, int64_t r) {
+  if (!g.row_offsets) return r / g.n;
+  int64_t lo = 0, hi = g.slices - 1;
+  while (lo < hi) {
+    const int64_t mid = (lo + hi + 1) >> 1;
+    if ((int64_t)g.row_offsets[mid] <= r) lo = mid; else hi = mid - 1;
+  }
+  return lo;
 }
 
 // Map a CTA's tile id to (slice, first row, row count) for tiles of `tile`

@@ -179,7 +179,9 @@ __global__ void __launch_bounds__(NT) fused_fwd_generic(FwdArgs<typename AccOf<T
     int* ri = ci + r * capp;
     compact_row(rv, ri, cnt[r], a.topk, &tau[r], lane);
     const int64_t lr = row0 + r;
-    const Acc mx = rv[0];
+    // softmax shift: the row maximum, or 0 when it is not finite (all
+    // selected scores -inf gives LSE -inf)
+    const Acc mx = isfinite(rv[0]) ? rv[0] : Acc(0);
     Acc part = 0;
     for (int j = lane; j < a.topk; j += kWarp) part += exp_acc(rv[j] - mx);
 #pragma unroll

@@ -100,15 +100,24 @@ constexpr int32_t kCandDead = -1;     // list could not be shrunk: re-select exa
 constexpr int32_t kCandAborted = -2;  // a pipeline wait timed out: nothing to finish
 
 struct TcArgs {
+  const void* q;     // query rows, gathered through row_index when that is set
   const void* k;     // key rows, for the magnitude check
+  const int32_t* row_index;  // nullable: logical row -> query row (grouped slices)
   uint32_t* cand;    // [rows][CAP] list entries of each query row
   int32_t* cand_n;   // [rows] entry count, kCandDead or kCandAborted
-  uint32_t* unsafe;  // [slices] 1 when a key of the slice fails the magnitude check
-  int64_t n, m;
-  int tiles_per_slice, topk;
+  uint32_t* unsafe;  // [rows], at each slice's first row: 1 when a key of the slice fails the magnitude check
+  SliceGeometry geo;
+  int64_t m;
+  int topk;
   uint32_t big16;    // 16-bit magnitude field at which an element counts as unsafe
   unsigned int* status;
   uint64_t wait_limit_ns;  // bound of each pipeline wait (sdk_set_wait_limit)
+  // kBias: score(r, j) = dot * scale + seg_bias[r * segs + j / seg_len], with
+  // seg_len a multiple of TK so that each key tile lies in one segment
+  const float* seg_bias;
+  int64_t seg_len;
+  int segs;
+  float scale;
 };
 
 // Input magnitude check.  With every |q|, |k| < 2^60 and finite, each of the
@@ -497,6 +506,8 @@ __device__ __forceinline__ void write_row(const T* vbase, ScoreOf score_of, Inde
   }
 }
 
+__device__ __forceinline__ float finite_or_zero(float x) { return isfinite(x) ? x : 0.f; }
+
 // Order-preserving 64-bit rank key: larger key = ranks higher.  The high
 // word maps the float onto an unsigned order (NaN highest, -0 == +0); the
 // low word is the complemented key index, so equal scores rank the lower
@@ -528,10 +539,11 @@ struct RowOut {
 };
 
 template <typename T>
-__device__ __noinline__ void reselect_row(RowOut a, int64_t m, int topk, float scale, int64_t slice, int64_t gr,
-                                          float* fv, int* fi, float* ftau, int lane) {
+__device__ __noinline__ void reselect_row(RowOut a, int64_t m, int topk, float scale, int64_t slice, int64_t gr, int64_t pr,
+                                          const float* bias_row, int64_t seg_len, float* fv, int* fi, float* ftau,
+                                          int lane) {
   const int g = lane & 7, grp = lane >> 3;
-  const uint4 qg = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(a.q) + gr * D) + g);
+  const uint4 qg = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(a.q) + pr * D) + g);
   const T* kbase = static_cast<const T*>(a.k) + slice * m * D;
   if (lane == 0) *ftau = __int_as_float(0x7fc00000);
   __syncwarp();
@@ -550,6 +562,8 @@ __device__ __noinline__ void reselect_row(RowOut a, int64_t m, int topk, float s
     }
     const int64_t key = k0 + lane;
     const bool valid = key < m;
+    // biased: the final score, scaled then shifted by the key's segment bias
+    if (bias_row && valid) s = __fadd_rn(__fmul_rn(s, scale), bias_row[key / seg_len]);
     const bool pass = valid && !(s <= tau);
     const unsigned bal = __ballot_sync(0xffffffffu, pass);
     if (pass) {
@@ -566,7 +580,10 @@ __device__ __noinline__ void reselect_row(RowOut a, int64_t m, int topk, float s
   }
   __syncwarp();
   c0 = compact_row(fv, fi, c0, topk, ftau, lane);  // sorted, c0 == topk (topk <= m)
-  const float mxs = fv[0] * scale;
+  if (bias_row) scale = 1.f;  // the list already holds final scores
+  // softmax shift: the row maximum, or 0 when it is not finite (all scores
+  // -inf gives LSE -inf; a NaN or +inf maximum gives NaN / +inf)
+  const float mxs = finite_or_zero(fv[0] * scale);
   float part = 0.f;
   for (int j = lane; j < c0; j += kWarp) part += expf(fv[j] * scale - mxs);
 #pragma unroll
@@ -574,7 +591,7 @@ __device__ __noinline__ void reselect_row(RowOut a, int64_t m, int topk, float s
   const float lse = mxs + logf(part);
   if (lane == 0) a.lse[gr] = lse;
   write_row<T>(static_cast<const T*>(a.v) + slice * m * D, [&](int j) { return fv[j]; }, [&](int j) { return fi[j]; },
-               c0, scale, lse, static_cast<T*>(a.out) + gr * D, a.top_idx + gr * topk,
+               c0, scale, lse, static_cast<T*>(a.out) + pr * D, a.top_idx + gr * topk,
                a.top_scores ? a.top_scores + gr * topk : nullptr, lane);
   __syncwarp();
 }
@@ -582,7 +599,10 @@ __device__ __noinline__ void reselect_row(RowOut a, int64_t m, int topk, float s
 // kPrefilter: skip 32-key chunks in which no row of the warp has a hit.
 // That pays only for small k: with k >= 8, some row of the warp has a hit in
 // nearly every chunk and the test is pure overhead.
-template <typename T, bool kPrefilter>
+// kBias: each row's scores of a key tile are shifted by the bias of the
+// tile's segment, fma(dot, scale, bias), before the filter (the finish kernel
+// recomputes the exact fl(fl(dot * scale) + bias)).
+template <typename T, bool kPrefilter, bool kBias>
 __global__ void __launch_bounds__(NT, 1)
     fused_fwd_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                  TcArgs a) {
@@ -603,9 +623,11 @@ __global__ void __launch_bounds__(NT, 1)
   volatile uint32_t* scan_big = reinterpret_cast<volatile uint32_t*>(sm + OFF_MISC + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t slice = blockIdx.x / a.tiles_per_slice;
-  const int64_t local0 = (int64_t)(blockIdx.x % a.tiles_per_slice) * RS;
-  const int64_t row0 = slice * a.n + local0;
+  int64_t slice, row0;
+  int count;  // rows of this CTA (RS, fewer at a slice's end, 0 for a surplus grouped CTA)
+  locate_tile(a.geo, blockIdx.x, RS, &slice, &row0, &count);
+  if (count <= 0) return;
+  const int64_t slice_row0 = slice_row_begin(a.geo, slice);
   const int ntiles = (int)((a.m + TK - 1) / TK);
 
   if (threadIdx.x == 0) {
@@ -633,8 +655,10 @@ __global__ void __launch_bounds__(NT, 1)
   if (warp == 0) {
     if (lane == 0) {
       int issued = 0;
-      mbar_arrive_expect_tx(q_full, NTILE * TILE_BYTES);
-      for (int g = 0; g < NTILE; ++g) tma_load_2d(qs + g * TILE_BYTES, &tmap_q, 0, (int)(row0 + g * TQ), q_full);
+      if (!a.row_index) {  // else warps 2 and 3 gather the query rows
+        mbar_arrive_expect_tx(q_full, NTILE * TILE_BYTES);
+        for (int g = 0; g < NTILE; ++g) tma_load_2d(qs + g * TILE_BYTES, &tmap_q, 0, (int)(row0 + g * TQ), q_full);
+      }
       for (int t = 0; t < ntiles; ++t) {
         const int s = t % KSTAGES;
         const uint32_t ph = (uint32_t)(t / KSTAGES) & 1u;
@@ -657,10 +681,33 @@ __global__ void __launch_bounds__(NT, 1)
       }
     }
   } else if (warp == 2 || warp == 3) {
+    if (a.row_index) {
+      // Grouped rows read through the permutation: the two warps gather the
+      // CTA's query rows into the layout the TMA would have written (128-byte
+      // rows, 16-byte chunk c of row r at chunk c ^ (r & 7)); rows past the
+      // CTA's count are zero.  The copies are made visible to the tensor
+      // cores' async proxy before q_full is signalled.
+      const int t = (int)threadIdx.x - 2 * kWarp;
+      const T* qrows = static_cast<const T*>(a.q);
+      const uint32_t qbase = smem_addr(qs);
+      for (int c = t; c < RS * (D / 8); c += 2 * kWarp) {
+        const int r = c >> 3, ch = c & 7;
+        const uint32_t dst = qbase + (uint32_t)(r / TQ) * TILE_BYTES + (uint32_t)(r % TQ) * (D * 2) +
+                             ((uint32_t)(ch ^ (r & 7)) << 4);
+        if (r < count)
+          cp_async_16(dst, qrows + (int64_t)a.row_index[row0 + r] * D + ch * 8);
+        else
+          st_shared_zero16(dst);
+      }
+      cp_async_wait_all();
+      fence_proxy_async_shared();
+      named_bar_sync(1, 2 * kWarp);
+      if (t == 0) mbar_arrive(q_full);
+    }
     // The first CTA of each slice also checks the slice's keys for unsafe
     // magnitudes, with its two otherwise idle warps reading the key rows
     // from global memory (L2: the slice's CTAs are streaming them).
-    if (local0 == 0) {
+    if (row0 == slice_row0) {
       const uint4* kp = reinterpret_cast<const uint4*>(static_cast<const T*>(a.k) + slice * a.m * D);
       const int64_t total = a.m * (D / 8);
       const uint32_t add = (0x8000u - a.big16) * 0x00010001u;
@@ -682,7 +729,7 @@ __global__ void __launch_bounds__(NT, 1)
       const bool any_big = __any_sync(0xffffffffu, big != 0u);
       if (warp == 3 && lane == 0) *scan_big = any_big ? 1u : 0u;
       named_bar_sync(1, 2 * kWarp);
-      if (warp == 2 && lane == 0) a.unsafe[slice] = (any_big || *scan_big) ? 1u : 0u;
+      if (warp == 2 && lane == 0) a.unsafe[slice_row0] = (any_big || *scan_big) ? 1u : 0u;
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -727,8 +774,8 @@ __global__ void __launch_bounds__(NT, 1)
     const int wg = (warp - 4) >> 2, quarter = warp & 3;
     const int rl = quarter * kWarp + lane;  // row within the query tile == TMEM lane
     const int R = wg * TQ + rl;              // list column
-    const int64_t tile_left = a.n - local0 - (int64_t)wg * TQ;
-    const int rows = (int)(tile_left < 0 ? 0 : (tile_left < TQ ? tile_left : TQ));
+    const int tile_left = count - wg * TQ;
+    const int rows = tile_left < 0 ? 0 : (tile_left < TQ ? tile_left : TQ);
     const uint32_t tm = tmem + ((uint32_t)(quarter * kWarp) << 16) + (uint32_t)(2 * wg * TK);
     uint64_t* my_full = s_full + 2 * wg;
     uint64_t* my_empty = s_empty + 2 * wg;
@@ -747,6 +794,9 @@ __global__ void __launch_bounds__(NT, 1)
       tc_fence_after();
       const int64_t key_tile = (int64_t)t * TK;
       const int tile_valid = (int)((a.m - key_tile) < TK ? (a.m - key_tile) : TK);
+      float tile_bias = 0.f;
+      if (kBias && rl < rows)
+        tile_bias = __ldg(a.seg_bias + (row0 + wg * TQ + rl) * a.segs + key_tile / a.seg_len);
       // One 32-column chunk at a time; the TMEM load of the next chunk is in
       // flight while the current one is filtered.  The loop body holds two
       // chunk steps (two register buffers) so that the hot path stays small
@@ -754,6 +804,10 @@ __global__ void __launch_bounds__(NT, 1)
       // its last chunk is in registers.
       auto chunk_step = [&](uint32_t(&v)[32], int c) {
         const int valid = tile_valid - c * 32;
+        if (kBias) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(fmaf(__uint_as_float(v[i]), a.scale, tile_bias));
+        }
         if (kPrefilter) {
           float mx;
           if (valid >= 32) {
@@ -857,8 +911,13 @@ struct FinArgs {
   float* top_scores;
   const uint32_t* cand;
   const int32_t* cand_n;
-  const uint32_t* unsafe;  // per slice, from the stream kernel's key check
-  int64_t rows, n, m;
+  const uint32_t* unsafe;  // at each slice's first row, from the stream kernel's key check
+  const int32_t* row_index;  // nullable: logical row -> query/output row
+  const float* seg_bias;     // nullable: per (logical row, key segment), as in TcArgs
+  int64_t seg_len;
+  int segs;
+  SliceGeometry geo;
+  int64_t rows, m;
   int topk;
   float scale;
   uint32_t big16;
@@ -957,20 +1016,27 @@ __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
         a.top_idx[r * a.topk + j] = -1;
         if (a.top_scores) a.top_scores[r * a.topk + j] = __int_as_float(0x7fc00000);
       }
-      if (lane < D) static_cast<T*>(a.out)[r * D + lane] = from_acc<T>(__int_as_float(0x7fc00000));
-      if (lane + kWarp < D) static_cast<T*>(a.out)[r * D + lane + kWarp] = from_acc<T>(__int_as_float(0x7fc00000));
+      const int64_t orow = a.row_index ? (int64_t)a.row_index[r] : r;
+      if (lane < D) static_cast<T*>(a.out)[orow * D + lane] = from_acc<T>(__int_as_float(0x7fc00000));
+      if (lane + kWarp < D) static_cast<T*>(a.out)[orow * D + lane + kWarp] = from_acc<T>(__int_as_float(0x7fc00000));
       if (lane == 0) a.lse[r] = __int_as_float(0x7fc00000);
       continue;
     }
-    const int64_t slice = r / a.n;
-    const uint4 qg = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(a.q) + r * D) + g);
+    const int64_t slice = slice_of_row(a.geo, r);
+    const int64_t pr = a.row_index ? (int64_t)a.row_index[r] : r;  // query and output row
+    const uint4 qg = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(a.q) + pr * D) + g);
     const uint32_t add = (0x8000u - a.big16) * 0x00010001u;
     const bool unsafe = __any_sync(0xffffffffu, (big_halves(qg.x, add) | big_halves(qg.y, add) |
                                                  big_halves(qg.z, add) | big_halves(qg.w, add)) != 0u) ||
-                        a.unsafe[slice] != 0u;
-    if (cnt < 0 || unsafe) {
+                        a.unsafe[slice_row_begin(a.geo, slice)] != 0u;
+    const float* brow = a.seg_bias ? a.seg_bias + r * a.segs : nullptr;
+    bool bias_nan = false;  // a NaN bias makes NaN scores, which the stream filter does not rank
+    if (brow)
+      for (int j = lane; j < a.segs; j += kWarp) bias_nan |= brow[j] != brow[j];
+    if (cnt < 0 || unsafe || __any_sync(0xffffffffu, bias_nan)) {
       uint8_t* fix = reinterpret_cast<uint8_t*>(&w);
-      reselect_row<T>(RowOut{a.q, a.k, a.v, a.out, a.top_idx, a.lse, a.top_scores}, a.m, a.topk, a.scale, slice, r,
+      reselect_row<T>(RowOut{a.q, a.k, a.v, a.out, a.top_idx, a.lse, a.top_scores}, a.m, a.topk, a.scale, slice, r, pr,
+                      brow, a.seg_len,
                       reinterpret_cast<float*>(fix), reinterpret_cast<int*>(fix + FIX_CAP * 4),
                       reinterpret_cast<float*>(fix + FIX_CAP * 8), lane);
       continue;
@@ -1018,7 +1084,8 @@ __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
       for (int u = 0; u < FUNR; ++u) {
         const int s = s0 + 4 * u + grp;
         const float d = group_dot<T>(qg, kc[u]);
-        if (g == 0 && s < S) w.sc[s] = d;
+        if (g == 0 && s < S)
+          w.sc[s] = brow ? __fadd_rn(__fmul_rn(d, a.scale), brow[w.si[s] / a.seg_len]) : d;
       }
     }
     __syncwarp();
@@ -1096,15 +1163,16 @@ __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
       __syncwarp();
       sel = pos;
     }
-    // LSE; lane j holds selections j and j + 32 (k <= 64)
+    // LSE; lane j holds selections j and j + 32 (k <= 64).  Biased scores are final.
+    const float sc_mul = brow ? 1.f : a.scale;
     const bool v0 = lane < sel, v1 = lane + kWarp < sel;
     const float x0 = v0 ? w.sc[lane] : 0.f, x1 = v1 ? w.sc[lane + kWarp] : 0.f;
     const int k0 = v0 ? w.si[lane] : 0, k1 = v1 ? w.si[lane + kWarp] : 0;
     float mx = fmaxf(v0 ? x0 : __int_as_float(0xff800000), v1 ? x1 : __int_as_float(0xff800000));
 #pragma unroll
     for (int o2 = 16; o2 > 0; o2 >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o2));
-    const float mxs = mx * a.scale;
-    float part = (v0 ? expf(x0 * a.scale - mxs) : 0.f) + (v1 ? expf(x1 * a.scale - mxs) : 0.f);
+    const float mxs = finite_or_zero(mx * sc_mul);
+    float part = (v0 ? expf(x0 * sc_mul - mxs) : 0.f) + (v1 ? expf(x1 * sc_mul - mxs) : 0.f);
 #pragma unroll
     for (int o2 = 16; o2 > 0; o2 >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o2);
     const float lse = mxs + logf(part);
@@ -1112,14 +1180,14 @@ __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
     float* pw = reinterpret_cast<float*>(w.hist);  // softmax weight of each selection
     int32_t* idx_row = a.top_idx + r * a.topk;
     if (v0) {
-      pw[lane] = expf(x0 * a.scale - lse);
+      pw[lane] = expf(x0 * sc_mul - lse);
       idx_row[lane] = k0;
-      if (a.top_scores) a.top_scores[r * a.topk + lane] = x0 * a.scale;
+      if (a.top_scores) a.top_scores[r * a.topk + lane] = x0 * sc_mul;
     }
     if (v1) {
-      pw[lane + kWarp] = expf(x1 * a.scale - lse);
+      pw[lane + kWarp] = expf(x1 * sc_mul - lse);
       idx_row[lane + kWarp] = k1;
-      if (a.top_scores) a.top_scores[r * a.topk + lane + kWarp] = x1 * a.scale;
+      if (a.top_scores) a.top_scores[r * a.topk + lane + kWarp] = x1 * sc_mul;
     }
     __syncwarp();
     // softmax-weighted sum of the value rows: group grp takes selections
@@ -1157,7 +1225,7 @@ __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
       T* ev = reinterpret_cast<T*>(&u);
 #pragma unroll
       for (int h = 0; h < 8; ++h) ev[h] = from_acc<T>(acc[h]);
-      reinterpret_cast<uint4*>(static_cast<T*>(a.out) + r * D)[g] = u;
+      reinterpret_cast<uint4*>(static_cast<T*>(a.out) + pr * D)[g] = u;
     }
     __syncwarp();
   }
@@ -1200,47 +1268,36 @@ bool make_rows_map(CUtensorMap* map, const void* base, int64_t rows, bool bf16) 
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-// Stream-ordered scratch for the candidate buffer: a memory pool of this
-// library per device that keeps what it has reserved (no release at
-// synchronisation), so repeated calls reuse the same device memory.
-cudaMemPool_t scratch_pool() {
-  static std::mutex mu;
-  static cudaMemPool_t pools[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  std::lock_guard<std::mutex> lock(mu);
-  if (!pools[dev]) {
-    cudaMemPoolProps props = {};
-    props.allocType = cudaMemAllocationTypePinned;
-    props.location.type = cudaMemLocationTypeDevice;
-    props.location.id = dev;
-    cudaMemPool_t pool = nullptr;
-    if (cudaMemPoolCreate(&pool, &props) != cudaSuccess) return nullptr;
-    uint64_t keep = ~0ull;
-    if (cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep) != cudaSuccess) return nullptr;
-    pools[dev] = pool;
-  }
-  return pools[dev];
-}
-
 template <typename T>
 int launch(const FwdLaunch& L) {
   CUtensorMap tq, tk;
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
-  if (!make_rows_map(&tq, L.q, L.slices * L.n, bf16)) return SDK_ERR_CUDA;
+  const bool grouped = L.row_offsets != nullptr;
+  // grouped: n is the total row count, slice s owns rows [row_offsets[s], row_offsets[s+1])
+  const int64_t rows = grouped ? L.n : L.slices * L.n;
+  if (rows <= 0) return SDK_OK;
+  if (!make_rows_map(&tq, L.q, rows, bf16)) return SDK_ERR_CUDA;
   if (!make_rows_map(&tk, L.k, L.slices * L.m, bf16)) return SDK_ERR_CUDA;
-  const int64_t rows = L.slices * L.n;
   TcArgs a;
+  a.q = L.q;
   a.k = L.k;
-  a.n = L.n;
+  a.row_index = L.row_index;
+  a.geo = SliceGeometry{L.row_offsets, L.slices, L.n};
   a.m = L.m;
-  a.tiles_per_slice = (int)((L.n + RS - 1) / RS);
   a.topk = L.topk;
   a.status = L.status;
   a.wait_limit_ns = wait_limit_ns();
-  const int64_t grid = L.slices * a.tiles_per_slice;
+  a.seg_bias = static_cast<const float*>(L.seg_bias);
+  a.seg_len = L.seg_len;
+  a.segs = L.segs;
+  a.scale = (float)L.scale;
+  // grouped: at most ceil(rows / RS) + slices tiles; CTAs past the last exit at once
+  const int64_t grid = grouped ? (rows + RS - 1) / RS + L.slices : L.slices * ((L.n + RS - 1) / RS);
   if (grid <= 0) return SDK_OK;
-  auto kern = L.topk < 8 ? fused_fwd_tc<T, true> : fused_fwd_tc<T, false>;
+  if (grid > 0x7fffffff) return SDK_ERR_UNSUPPORTED;
+  const bool bias = L.seg_bias != nullptr;
+  auto kern = L.topk < 8 ? (bias ? fused_fwd_tc<T, true, true> : fused_fwd_tc<T, true, false>)
+                         : (bias ? fused_fwd_tc<T, false, true> : fused_fwd_tc<T, false, false>);
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
     return SDK_ERR_CUDA;
   const size_t need = (size_t)rows * (CAP * 4 + 8);
@@ -1253,7 +1310,7 @@ int launch(const FwdLaunch& L) {
   } else if (L.workspace_bytes < need || !aligned16(ws)) {
     return SDK_ERR_INVALID_ARGUMENT;
   }
-  // per row: CAP entries and a count; per slice (slices <= rows): a flag
+  // per row: CAP entries, a count and a flag (set at the first row of each slice)
   a.cand = static_cast<uint32_t*>(ws);
   a.cand_n = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + (size_t)rows * CAP * 4);
   a.unsafe = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + (size_t)rows * (CAP * 4 + 4));
@@ -1272,9 +1329,13 @@ int launch(const FwdLaunch& L) {
     f.cand = a.cand;
     f.cand_n = a.cand_n;
     f.unsafe = a.unsafe;
+    f.row_index = L.row_index;
+    f.seg_bias = a.seg_bias;
+    f.seg_len = L.seg_len;
+    f.segs = L.segs;
+    f.geo = a.geo;
     f.big16 = a.big16;
     f.rows = rows;
-    f.n = L.n;
     f.m = L.m;
     f.topk = L.topk;
     f.scale = (float)L.scale;
@@ -1301,18 +1362,21 @@ int launch(const FwdLaunch& L) {
 
 namespace {
 // The shape conditions of the tensor-core path (everything but pointers).
-bool tensorcore_shape(int64_t rows, int64_t m, int d, int dv, int topk, int score_grid, bool grouped, int dtype) {
+bool tensorcore_shape(int64_t rows, int64_t m, int d, int dv, int topk, int score_grid, int dtype) {
   if (dtype != SDK_DTYPE_BF16 && dtype != SDK_DTYPE_F16) return false;
-  if (d != D || dv != D || score_grid != 0 || grouped) return false;
+  if (d != D || dv != D || score_grid != 0) return false;
   if (m < 1 || m > 65536 || topk < 1 || topk > 64 || rows < 1) return false;
   return rows <= 0x7fffff00;
 }
 }  // namespace
 
 bool fwd_tensorcore_supports(const FwdLaunch& L) {
-  if (L.n < 1 || L.seg_bias) return false;
-  if (!tensorcore_shape(L.slices * L.n, L.m, L.d, L.dv, L.topk, L.score_grid, L.row_offsets || L.row_index,
-                        L.dtype))
+  if (L.n < 1) return false;
+  // a segment bias needs whole key tiles per segment
+  if (L.seg_bias && (L.segs < 1 || L.seg_len < 1 || L.seg_len % TK != 0 || L.seg_len * L.segs != L.m ||
+                     !aligned16(L.seg_bias)))
+    return false;
+  if (!tensorcore_shape(L.row_offsets ? L.n : L.slices * L.n, L.m, L.d, L.dv, L.topk, L.score_grid, L.dtype))
     return false;
   if (L.slices * L.m > 0x7fffffff) return false;
   if (!aligned16(L.q) || !aligned16(L.k) || !aligned16(L.v) || !aligned16(L.out)) return false;
@@ -1321,7 +1385,8 @@ bool fwd_tensorcore_supports(const FwdLaunch& L) {
 
 size_t fwd_tensorcore_workspace(int64_t rows, int64_t m, int d, int dv, int topk, int score_grid, bool grouped,
                                 int dtype) {
-  if (!tensorcore_shape(rows, m, d, dv, topk, score_grid, grouped, dtype)) return 0;
+  (void)grouped;  // grouped and uniform slices need the same scratch per row
+  if (!tensorcore_shape(rows, m, d, dv, topk, score_grid, dtype)) return 0;
   return (size_t)rows * (CAP * 4 + 8);
 }
 

@@ -121,4 +121,15 @@ int topk_aggregate(const void* top_scores, const void* top_idx, const void* valu
 int route_top1(const float* logits, int64_t n, int experts, int32_t* expert, int32_t* order,
                int32_t* offsets, cudaStream_t stream);
 
+// Sparse top-k attention over given dense scores (select_attn.cu).
+int sparse_attn_forward(const void* sel, const int64_t* idx, const void* values, void* out, void* weights,
+                        void* masked, int64_t rows, int64_t rows_per_batch, int k, int64_t m, int dv, int score_dtype,
+                        int out_dtype, unsigned int* status, cudaStream_t stream);
+int sparse_attn_backward(const void* sel, const int64_t* idx, const void* values, const void* g_out,
+                         const void* g_weights, const void* g_masked, void* g_scores, void* g_values, int64_t rows,
+                         int64_t rows_per_batch, int k, int64_t m, int dv, int score_dtype, int out_dtype,
+                         unsigned int* status, cudaStream_t stream);
+int fill_scatter(const void* src, const int64_t* idx, void* dst, int64_t rows, int k, int64_t m, double fill,
+                 int dtype, unsigned int* status, cudaStream_t stream);
+
 }  // namespace sdk

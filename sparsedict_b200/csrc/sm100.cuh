@@ -215,6 +215,23 @@ __device__ __forceinline__ void st_shared_u32_if(uint32_t addr, uint32_t v, uint
                : "memory");
 }
 
+// 16-byte global -> shared copy (cp.async, bypassing L1) and its completion.
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+__device__ __forceinline__ void st_shared_zero16(uint32_t addr) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0u) : "memory");
+}
+
+// Orders this thread's earlier shared-memory writes (generic proxy) before
+// later async-proxy reads of them (tcgen05.mma operands, TMA stores).
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Barrier `id` (1..15) over `count` threads (a multiple of 32) of the CTA.
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

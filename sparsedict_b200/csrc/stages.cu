@@ -8,7 +8,8 @@
 //              rows, reference tiled_topk_aggregate
 //              (kernels/fused_topk_attn.py:339-408)
 //   route      top-1 expert per token and a stable grouping of tokens by
-//              expert (models/modules/router.py:139-145)
+//              expert (models/modules/router.py:139-145); per-block counts
+//              in stream-ordered scratch from the library pool
 #include "common.cuh"
 #include "kernels.h"
 
@@ -142,52 +143,92 @@ __global__ void aggregate_kernel(const TS* __restrict__ ts, const TI* __restrict
 }
 
 // --------------------------------------------------------------- route ---
-constexpr int R_NT = 512, R_MAXE = 16;
+// Three launches over blocks of RB tokens (one per thread):
+//   count  each token's expert (the first maximum, NaN ranking highest, as
+//          torch.argmax) and the block's per-expert counts;
+//   scan   one block: for each expert, the exclusive sum of the counts over
+//          the blocks before each block, plus the expert offsets;
+//   place  each token's position: its expert's offset + the block's prefix
+//          + its rank among the block's tokens of that expert (warp
+//          match/popc, then a prefix over the block's warps), so the order
+//          within an expert is ascending token index (a stable sort).
+constexpr int R_NT = 256, R_MAXE = 16, R_WARPS = R_NT / kWarp;
 
-__global__ void __launch_bounds__(R_NT) route_kernel(const float* __restrict__ logits, int64_t n, int experts,
-                                                     int32_t* __restrict__ expert, int32_t* __restrict__ order,
-                                                     int32_t* __restrict__ offsets) {
-  __shared__ int counts[R_MAXE][R_NT];
-  __shared__ int totals[R_MAXE + 1];
-  const int t = threadIdx.x;
-  const int64_t per = (n + R_NT - 1) / R_NT;
-  const int64_t b = t * per, e = b + per < n ? b + per : n;
-  int local[R_MAXE];
-#pragma unroll
-  for (int x = 0; x < R_MAXE; ++x) local[x] = 0;
-  for (int64_t i = b; i < e; ++i) {
+__global__ void __launch_bounds__(R_NT) route_count(const float* __restrict__ logits, int64_t n, int experts,
+                                                    int32_t* __restrict__ expert, int32_t* __restrict__ counts) {
+  __shared__ int wc[R_WARPS][R_MAXE];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int64_t i = (int64_t)blockIdx.x * R_NT + t;
+  int best = -1;
+  if (i < n) {
     const float* row = logits + i * experts;
-    int best = 0;
-    float bv = row[0];
-    for (int x = 1; x < experts; ++x)
-      if (ranks_above(row[x], x, bv, best)) { bv = row[x]; best = x; }
+    float v[R_MAXE];
+#pragma unroll
+    for (int x = 0; x < R_MAXE; ++x) v[x] = x < experts ? __ldg(row + x) : 0.f;
+    best = 0;
+    float bv = v[0];
+#pragma unroll
+    for (int x = 1; x < R_MAXE; ++x)
+      if (x < experts && ranks_above(v[x], x, bv, best)) { bv = v[x]; best = x; }
     expert[i] = best;
-#pragma unroll
-    for (int x = 0; x < R_MAXE; ++x) local[x] += (x == best);
   }
-#pragma unroll
-  for (int x = 0; x < R_MAXE; ++x) counts[x][t] = local[x];
+  for (int x = 0; x < experts; ++x) {
+    const unsigned b = __ballot_sync(0xffffffffu, best == x);
+    if (lane == 0) wc[warp][x] = __popc(b);
+  }
   __syncthreads();
-  if (t < experts) {  // serial exclusive scan of one expert's per-thread counts
+  if (t < experts) {
+    int c = 0;
+#pragma unroll
+    for (int w = 0; w < R_WARPS; ++w) c += wc[w][t];
+    counts[(int64_t)blockIdx.x * experts + t] = c;
+  }
+}
+
+// One block of R_NT threads: thread x < experts scans expert x's column of
+// the block counts (in place, exclusive); then the expert offsets.
+__global__ void __launch_bounds__(R_NT) route_scan(int32_t* __restrict__ counts, int64_t blocks, int experts,
+                                                   int32_t* __restrict__ offsets) {
+  __shared__ int tot[R_MAXE];
+  const int t = threadIdx.x;
+  if (t < experts) {
     int run = 0;
-    for (int u = 0; u < R_NT; ++u) { const int c = counts[t][u]; counts[t][u] = run; run += c; }
-    totals[t] = run;
+    for (int64_t b = 0; b < blocks; ++b) {
+      const int c = counts[b * experts + t];
+      counts[b * experts + t] = run;
+      run += c;
+    }
+    tot[t] = run;
   }
   __syncthreads();
   if (t == 0) {
     int run = 0;
-    for (int x = 0; x < experts; ++x) { const int c = totals[x]; totals[x] = run; offsets[x] = run; run += c; }
+    for (int x = 0; x < experts; ++x) {
+      offsets[x] = run;
+      run += tot[x];
+    }
     offsets[experts] = run;
   }
+}
+
+__global__ void __launch_bounds__(R_NT) route_place(const int32_t* __restrict__ expert, int64_t n, int experts,
+                                                    const int32_t* __restrict__ counts,
+                                                    const int32_t* __restrict__ offsets, int32_t* __restrict__ order) {
+  __shared__ int wc[R_WARPS][R_MAXE];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int64_t i = (int64_t)blockIdx.x * R_NT + t;
+  const int x = i < n ? expert[i] : -1;
+  const unsigned same = __match_any_sync(0xffffffffu, x);
+  const int rank = __popc(same & ((1u << lane) - 1u));
+  for (int y = 0; y < experts; ++y)
+    if (lane == 0) wc[warp][y] = 0;
+  __syncwarp();
+  if (x >= 0 && rank == 0) wc[warp][x] = __popc(same);
   __syncthreads();
-  int cursor[R_MAXE];
-#pragma unroll
-  for (int x = 0; x < R_MAXE; ++x) cursor[x] = (x < experts) ? totals[x] + counts[x][t] : 0;
-  for (int64_t i = b; i < e; ++i) {
-    const int x = expert[i];
-#pragma unroll
-    for (int y = 0; y < R_MAXE; ++y)
-      if (y == x) order[cursor[y]++] = (int32_t)i;
+  if (x >= 0) {
+    int pos = offsets[x] + counts[(int64_t)blockIdx.x * experts + x] + rank;
+    for (int w = 0; w < warp; ++w) pos += wc[w][x];
+    order[pos] = (int32_t)i;
   }
 }
 
@@ -280,8 +321,21 @@ int topk_aggregate(const void* ts, const void* ti, const void* v, float* out, in
 int route_top1(const float* logits, int64_t n, int experts, int32_t* expert, int32_t* order, int32_t* offsets,
                cudaStream_t stream) {
   if (experts < 1 || experts > R_MAXE) return SDK_ERR_UNSUPPORTED;
-  route_kernel<<<1, R_NT, 0, stream>>>(logits, n, experts, expert, order, offsets);
-  return cudaPeekAtLastError() == cudaSuccess ? SDK_OK : SDK_ERR_CUDA;
+  const int64_t blocks = (n + R_NT - 1) / R_NT;
+  if (blocks > 0x7fffffff) return SDK_ERR_UNSUPPORTED;
+  // per-block counts: stream-ordered scratch from the library pool
+  cudaMemPool_t pool = scratch_pool();
+  if (!pool) return SDK_ERR_CUDA;
+  void* scratch = nullptr;
+  if (cudaMallocFromPoolAsync(&scratch, (size_t)blocks * experts * sizeof(int32_t), pool, stream) != cudaSuccess)
+    return SDK_ERR_CUDA;
+  int32_t* counts = static_cast<int32_t*>(scratch);
+  route_count<<<(unsigned)blocks, R_NT, 0, stream>>>(logits, n, experts, expert, counts);
+  route_scan<<<1, R_NT, 0, stream>>>(counts, blocks, experts, offsets);
+  route_place<<<(unsigned)blocks, R_NT, 0, stream>>>(expert, n, experts, counts, offsets, order);
+  int rc = cudaPeekAtLastError() == cudaSuccess ? SDK_OK : SDK_ERR_CUDA;
+  if (cudaFreeAsync(scratch, stream) != cudaSuccess) rc = SDK_ERR_CUDA;
+  return rc;
 }
 
 }  // namespace sdk

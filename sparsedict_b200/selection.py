@@ -6,10 +6,13 @@
 score tensor ``(..., Q, M)``.  Same names, arguments, results and error
 messages.  The per-row top-k runs in the select kernel (``sdk_topk_select``:
 descending score, lower index on ties, NaN first; exact for fp32, fp16, bf16
-and fp64); the small ``(..., Q, k)`` softmax/gather that follows is the
-reference's own formula.  Both selection modes route a selected score's
-gradient to that score only (``topk_select.py:33-45``; ``torch.topk`` does the
-same for ``"hard"``), so they differ in name only.
+and fp64); the softmax over the selected scores, the dense weights and masked
+scores and the weighted sum of the gathered value rows run in one warp-per-row
+kernel (``sdk_sparse_topk_attn_fwd``), their gradient in another
+(``sdk_sparse_topk_attn_bwd``), and the masks in ``sdk_fill_scatter``.  Both
+selection modes route a selected score's gradient to that score only
+(``topk_select.py:33-45``; ``torch.topk`` does the same for ``"hard"``), so
+they differ in name only.
 
 The fused kernels (``fused_topk_attention``) never materialise the dense
 scores; these operators exist for callers that already hold them.
@@ -21,7 +24,6 @@ import math
 from typing import NamedTuple
 
 import torch
-import torch.nn.functional as F
 
 from . import _native, _ops
 
@@ -53,7 +55,21 @@ def _select(scores: torch.Tensor, k: int):
     return vals.reshape(*scores.shape[:-1], k), idx.reshape(*scores.shape[:-1], k)
 
 
+def _fill_scatter(src: torch.Tensor, idx: torch.Tensor, shape, fill: float) -> torch.Tensor:
+    """Dense ``shape`` tensor of ``fill`` with ``src`` at ``idx`` along the last axis (native kernel)."""
+    out = torch.empty(shape, dtype=src.dtype, device=src.device)
+    k = idx.size(-1)
+    rows = idx.numel() // k
+    src_c, idx_c = src.contiguous(), idx.contiguous()
+    with torch.cuda.device(src.device):
+        _native.call("sdk_fill_scatter", src_c.data_ptr(), idx_c.data_ptr(), out.data_ptr(), rows, k, shape[-1],
+                     float(fill), _native.TORCH_TO_SDK[src.dtype], _native.stream_of(src.device))
+    return out
+
+
 class _StraightThroughTopK(torch.autograd.Function):
+    """Top-k whose gradient reaches the selected scores only."""
+
     @staticmethod
     def forward(ctx, scores, k):
         vals, idx = _select(scores, k)
@@ -67,7 +83,21 @@ class _StraightThroughTopK(torch.autograd.Function):
         if grad_vals is None:
             return None, None
         (idx,) = ctx.saved_tensors
-        return grad_vals.new_zeros(ctx.input_shape).scatter(-1, idx, grad_vals), None
+        return _fill_scatter(grad_vals, idx, ctx.input_shape, 0.0), None
+
+
+class _MaskSelected(torch.autograd.Function):
+    """``-inf`` everywhere but the selected scores (gradient: the selected entries)."""
+
+    @staticmethod
+    def forward(ctx, vals, idx, shape):
+        ctx.save_for_backward(idx)
+        return _fill_scatter(vals, idx, shape, float("-inf"))
+
+    @staticmethod
+    def backward(ctx, grad):
+        (idx,) = ctx.saved_tensors
+        return grad.gather(-1, idx), None, None
 
 
 def straight_through_topk(scores: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Tensor]:
@@ -80,7 +110,7 @@ def hard_topk_mask(scores: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Te
     """All but the top-k scores set to ``-inf`` along the last axis, and the indices."""
     _validate_scores(scores, k)
     vals, idx = _StraightThroughTopK.apply(scores, k)
-    return torch.full_like(scores, float("-inf")).scatter(-1, idx, vals), idx
+    return _MaskSelected.apply(vals, idx, scores.shape), idx
 
 
 def gumbel_perturbed_topk(
@@ -114,6 +144,55 @@ def gumbel_perturbed_topk(
     return torch.stack(vals), torch.stack(idxs)
 
 
+class _SparseTopKAttention(torch.autograd.Function):
+    """Selection, softmax, dense weights and masked scores, and the value sum, on the
+    native kernels; the gradient reaches the selected scores and the gathered
+    value rows.  ``values`` is already in the output dtype."""
+
+    @staticmethod
+    def forward(ctx, scores, values, k):
+        vals, idx = _select(scores, k)
+        shape = scores.shape
+        q, m = shape[-2], shape[-1]
+        rows = idx.numel() // k
+        rpb = q if values.ndim > 2 else 0
+        dv = values.size(-1)
+        dev = scores.device
+        out = torch.empty((*shape[:-1], dv), dtype=values.dtype, device=dev)
+        weights = torch.empty(shape, dtype=scores.dtype, device=dev)
+        masked = torch.empty(shape, dtype=scores.dtype, device=dev)
+        values_c = values.contiguous()
+        with torch.cuda.device(dev):
+            _native.call("sdk_sparse_topk_attn_fwd", vals.data_ptr(), idx.data_ptr(), values_c.data_ptr(),
+                         out.data_ptr(), weights.data_ptr(), masked.data_ptr(), rows, rpb, k, m, dv,
+                         _native.TORCH_TO_SDK[scores.dtype], _native.TORCH_TO_SDK[values.dtype],
+                         _native.stream_of(dev))
+        ctx.save_for_backward(vals, idx, values_c)
+        ctx.geometry = (shape, rows, rpb, k, m, dv)
+        ctx.mark_non_differentiable(idx)
+        return out, weights, idx, masked
+
+    @staticmethod
+    def backward(ctx, g_out, g_weights, g_idx, g_masked):
+        vals, idx, values = ctx.saved_tensors
+        shape, rows, rpb, k, m, dv = ctx.geometry
+        dev = vals.device
+        if g_out is None:
+            g_out = torch.zeros((*shape[:-1], dv), dtype=values.dtype, device=dev)
+        g_out = g_out.contiguous()
+        g_weights = None if g_weights is None else g_weights.contiguous()
+        g_masked = None if g_masked is None else g_masked.contiguous()
+        g_scores = torch.empty(shape, dtype=vals.dtype, device=dev)
+        acc = torch.float64 if values.dtype == torch.float64 else torch.float32
+        g_values = torch.zeros(values.shape, dtype=acc, device=dev)
+        with torch.cuda.device(dev):
+            _native.call("sdk_sparse_topk_attn_bwd", vals.data_ptr(), idx.data_ptr(), values.data_ptr(),
+                         g_out.data_ptr(), _native.ptr(g_weights), _native.ptr(g_masked), g_scores.data_ptr(),
+                         g_values.data_ptr(), rows, rpb, k, m, dv, _native.TORCH_TO_SDK[vals.dtype],
+                         _native.TORCH_TO_SDK[values.dtype], _native.stream_of(dev))
+        return g_scores, g_values.to(values.dtype), None
+
+
 def sparse_topk_attention(
     scores: torch.Tensor,
     values: torch.Tensor,
@@ -124,15 +203,13 @@ def sparse_topk_attention(
 
     ``values`` is shared ``(M, D)`` or batch-specific ``(..., M, D)``.  Returns
     the reference's ``TopKAttentionResult(output, weights, indices,
-    masked_scores)`` (``topk_select.py:106-162``).
+    masked_scores)`` (``topk_select.py:106-162``) with its argument checks and
+    messages; the output has the promoted dtype of scores and values.  Both
+    selection modes have the same forward and gradient.
     """
-    if selection == "hard":
-        masked_scores, indices = hard_topk_mask(scores, k)
-    elif selection == "ste":
-        selected, indices = straight_through_topk(scores, k)
-        masked_scores = torch.full_like(scores, float("-inf")).scatter(-1, indices, selected)
-    else:
+    if selection not in ("hard", "ste"):
         raise ValueError(f"selection must be 'hard' or 'ste'; got {selection!r}")
+    _validate_scores(scores, k)
     if values.ndim < 2:
         raise ValueError(f"expected values with atom and feature dimensions, got {tuple(values.shape)}")
     if values.size(-2) != scores.size(-1):
@@ -146,10 +223,8 @@ def sparse_topk_attention(
             "values must be shared across batches or have leading dimensions "
             f"{tuple(batch_shape)}; got {tuple(value_batch_shape)}"
         )
-    selected_weights = F.softmax(masked_scores.gather(-1, indices), dim=-1)
-    weights = torch.zeros_like(scores).scatter(-1, indices, selected_weights)
-    q = scores.size(-2)
-    expanded = values.unsqueeze(-3).expand(*batch_shape, q, values.size(-2), values.size(-1))
-    selected_values = expanded.gather(-2, indices.unsqueeze(-1).expand(*indices.shape, values.size(-1)))
-    output = (selected_values * selected_weights.unsqueeze(-1)).sum(dim=-2)
-    return TopKAttentionResult(output, weights, indices, masked_scores)
+    if k > 256:
+        raise ValueError(f"k must be at most 256 on this path; got {k}")
+    out_dtype = torch.promote_types(scores.dtype, values.dtype)
+    output, weights, indices, masked = _SparseTopKAttention.apply(scores, values.to(out_dtype), k)
+    return TopKAttentionResult(output, weights, indices, masked)

@@ -75,7 +75,8 @@ def test_max_topk_covers_the_benchmark_configurations(dtype):
 
 def test_forward_workspace_size_follows_the_tensor_core_shapes():
     # Nonzero exactly when the call takes the tensor-core path: bf16/fp16,
-    # d = dv = 64, 1 <= k <= 64, m <= 65536, no score grid, uniform slices.
+    # d = dv = 64, 1 <= k <= 64, m <= 65536, no score grid; uniform or grouped
+    # slices alike.
     lib = _native.load()
     size = lib.sdk_topk_attn_fwd_workspace_size
     per_row = 160 * 4 + 8  # candidate list, count and check word per query row
@@ -88,7 +89,7 @@ def test_forward_workspace_size_follows_the_tensor_core_shapes():
         assert size(1000, 16384, 32, 32, 8, 0, 0, code) == 0
         assert size(0, 16384, 64, 64, 8, 0, 0, code) == 0
         assert size(1000, 16384, 64, 64, 8, 64, 0, code) == 0
-        assert size(1000, 16384, 64, 64, 8, 0, 1, code) == 0
+        assert size(1000, 16384, 64, 64, 8, 0, 1, code) == 1000 * per_row
     for code in (_native.DTYPE_F32, _native.DTYPE_F64):
         assert size(1000, 16384, 64, 64, 64, 0, 0, code) == 0
 

@@ -517,6 +517,113 @@ def test_routed_bf16_full_configuration_sampled_rows():
     np.testing.assert_allclose(out.float().cpu().numpy()[rows], o, rtol=2e-2, atol=2e-2)
 
 
+@pytest.mark.parametrize(("n", "e"), [(1, 1), (255, 3), (16384, 8), (70001, 16)])
+def test_route_top1_is_a_stable_grouping(n, e):
+    # expert = first maximum (NaN ranks highest, the lower expert on ties);
+    # order = tokens grouped by expert in ascending token order; offsets.
+    from sparsedict_b200 import _ops
+
+    rng = np.random.default_rng(n + e)
+    logits = rng.standard_normal((n, e)).astype(np.float32)
+    logits[rng.random(n) < 0.05] = 0.5  # whole-row ties
+    logits[rng.random((n, e)) < 0.01] = np.nan
+    expert, order, offsets = _ops.route_top1(torch.from_numpy(logits).to(DEV))
+    assert _native.device_status(clear=True) == 0
+    exp = oracle.moe_route_top1(logits)
+    assert np.array_equal(expert.cpu().numpy(), exp)
+    assert np.array_equal(order.cpu().numpy(), np.argsort(exp, kind="stable"))
+    assert np.array_equal(offsets.cpu().numpy(), np.concatenate([[0], np.cumsum(np.bincount(exp, minlength=e))]))
+
+
+def _routed_case(sizes, m, k, seed):
+    """Queries routed to experts with exactly ``sizes[e]`` tokens each (tokens shuffled)."""
+    rng = np.random.default_rng(seed)
+    e, n, d = len(sizes), int(sum(sizes)), 64
+    experts = rng.permutation(np.repeat(np.arange(e), sizes))
+    logits = rng.standard_normal((n, e)).astype(np.float32)
+    logits[np.arange(n), experts] += 20.0
+    q = oracle.round_to_bf16(rng.standard_normal((n, d)).astype(np.float32))
+    atoms = oracle.round_to_bf16((rng.standard_normal((e, m, d)) / 8).astype(np.float32))
+    return q, atoms, logits, experts
+
+
+@pytest.mark.parametrize(("sizes", "m", "k"), [((0, 1, 255, 256, 257, 700), 320, 16),
+                                               ((513, 0, 0, 40, 7, 1), 1024, 64),
+                                               ((300,) * 8, 96, 1)])
+def test_routed_tensor_core_ragged_experts(sizes, m, k):
+    # Expert groups of 0, 1, just under / at / over one 256-row CTA and several
+    # CTAs, and key counts that end in a partial 128-key tile: selected index
+    # sets (grouped row order), outputs and LSE against the oracle, bf16 d=64
+    # (the tensor-core forward).
+    from sparsedict_b200 import _ops
+
+    q, atoms, logits, experts = _routed_case(sizes, m, k, seed=sum(sizes) + m + k)
+    qd = torch.from_numpy(q).to(DEV, torch.bfloat16)
+    ad = torch.from_numpy(atoms).to(DEV, torch.bfloat16)
+    out, expert, idx = routed_dictionary_attention(qd, ad, torch.from_numpy(logits).to(DEV), k, 1.0,
+                                                   return_routing=True)
+    assert _native.device_status(clear=True) == 0
+    assert np.array_equal(expert.cpu().numpy(), experts)
+    o, oidx, olse = oracle.moe_topk_attention_forward(q, atoms, experts, k, 1.0)
+    order = np.argsort(experts, kind="stable")
+    sc = np.stack([q[t].astype(np.float64) @ atoms[experts[t]].astype(np.float64).T for t in order])
+    _assert_indices(idx.cpu().numpy()[None], oidx[order][None], sc[None], tol=1e-4, ordered=False,
+                    max_near_ties=max(1, len(order) // 100))
+    np.testing.assert_allclose(out.float().cpu().numpy(), o, rtol=2e-2, atol=2e-2)
+    # the same call through the op: grouped LSE in the accumulator type
+    _, order_d, offsets = _ops.route_top1(torch.from_numpy(logits).to(DEV))
+    _, _, lse, _ = _ops.topk_attn_fwd(qd, ad, ad, k, 1.0, row_offsets=offsets, row_index=order_d)
+    np.testing.assert_allclose(lse.cpu().numpy(), olse[order], rtol=1e-5, atol=1e-5)
+
+
+def test_grouped_rows_without_permutation_tensor_core():
+    # Grouped slices whose query rows are already in slice order (offsets, no
+    # row index): the tensor-core forward reads them by TMA across slice ends.
+    from sparsedict_b200 import _ops
+
+    sizes, m, k = (130, 0, 383, 1, 256), 256, 32
+    q, atoms, _, _ = _routed_case(sizes, m, k, seed=7)
+    experts = np.repeat(np.arange(len(sizes)), sizes)
+    qd = torch.from_numpy(q).to(DEV, torch.bfloat16)
+    ad = torch.from_numpy(atoms).to(DEV, torch.bfloat16)
+    offsets = torch.tensor(np.concatenate([[0], np.cumsum(sizes)]), dtype=torch.int32, device=DEV)
+    out, idx, lse, _ = _ops.topk_attn_fwd(qd, ad, ad, k, 1.0, row_offsets=offsets)
+    assert _native.device_status(clear=True) == 0
+    o, oidx, olse = oracle.moe_topk_attention_forward(q, atoms, experts, k, 1.0)
+    sc = np.stack([q[t].astype(np.float64) @ atoms[experts[t]].astype(np.float64).T for t in range(len(q))])
+    _assert_indices(idx.cpu().numpy()[None], oidx[None], sc[None], tol=1e-4, ordered=False,
+                    max_near_ties=max(1, len(q) // 100))
+    np.testing.assert_allclose(out.float().cpu().numpy(), o, rtol=2e-2, atol=2e-2)
+    np.testing.assert_allclose(lse.cpu().numpy(), olse, rtol=1e-5, atol=1e-5)
+
+
+def test_routed_bf16_full_configuration_index_sets():
+    # Configuration 3 at full size (N=16384 tokens, E=8 experts of M=1024
+    # atoms, k=16, bf16): every token's selected set against the oracle.
+    torch.manual_seed(3)
+    n, d, e, m, k = 16384, 64, 8, 1024, 16
+    q = torch.randn(n, d).to(torch.bfloat16)
+    atoms = (torch.randn(e, m, d) / math.sqrt(d)).to(torch.bfloat16)
+    logits = torch.randn(n, e)
+    out, expert, idx = routed_dictionary_attention(q.to(DEV), atoms.to(DEV), logits.to(DEV), k, 1.0,
+                                                   return_routing=True)
+    assert _native.device_status(clear=True) == 0
+    qr, ar = q.float().numpy(), atoms.float().numpy()
+    experts = oracle.moe_route_top1(logits.numpy())
+    assert np.array_equal(expert.cpu().numpy(), experts)
+    order = np.argsort(experts, kind="stable")
+    gidx = idx.cpu().numpy()
+    near = 0
+    for ex in range(e):
+        rows = order[experts[order] == ex]
+        pos = np.nonzero(experts[order] == ex)[0]
+        o, oidx, _, _ = oracle.topk_attention_forward(qr[rows][None], ar[ex][None], ar[ex][None], k, 1.0)
+        sc = (qr[rows].astype(np.float64) @ ar[ex].astype(np.float64).T)[None]
+        near += _assert_indices(gidx[pos][None], oidx, sc, tol=1e-4, ordered=False, max_near_ties=len(rows))
+        np.testing.assert_allclose(out.float().cpu().numpy()[rows], o[0], rtol=2e-2, atol=2e-2)
+    assert near <= max(1, n // 100), f"{near} near-tie rows"
+
+
 # --- full-size configurations, sampled rows against the oracle --------------------
 
 
@@ -676,6 +783,46 @@ def test_gated_mixture_bf16_vs_oracle():
     for got, exp in zip(grads, ref):
         got = got.float().cpu().numpy()
         assert np.abs(got - exp).max() <= 2e-2 * max(1.0, np.abs(exp).max())
+
+
+def test_gated_mixture_tensor_core_bias_rows():
+    # bf16, d = 64 and whole 128-atom expert segments: the biased forward on
+    # the tensor cores.  Top-2 gates (six experts at -inf per token), a token
+    # whose gates are all 0 (every score -inf: the k lowest indices, NaN
+    # output), one with a NaN gate (NaN scores rank first) and one with a gate
+    # below the clamp.  Flat index sets against the oracle (near ties aside),
+    # outputs and LSE.
+    from sparsedict_b200 import _ops
+
+    gen = torch.Generator().manual_seed(23)
+    b, n, dk, e, m, k = 1, 700, 64, 8, 128, 16
+    q = torch.randn(b, n, dk, generator=gen).to(torch.bfloat16)
+    keys = (torch.randn(e, m, dk, generator=gen) / 8).to(torch.bfloat16)
+    values = torch.randn(e, m, dk, generator=gen).to(torch.bfloat16)
+    logits = torch.randn(b, n, e, generator=gen)
+    top_l, top_e = logits.topk(2, dim=-1)
+    gates = torch.zeros_like(logits).scatter(-1, top_e, torch.softmax(top_l, -1))
+    gates[0, 5] = 0.0
+    gates[0, 7, 3] = float("nan")
+    gates[0, 9, top_e[0, 9, 0]] = 1e-42
+    qf, kf, vf, gf = (t.float().numpy() for t in (q, keys, values, gates))
+    o, oidx, olse, _ = oracle.gated_mixture_forward(qf, kf, vf, gf, k)
+    bias = torch.from_numpy(oracle.gate_bias(gf)).reshape(b * n, e).contiguous()
+    out, idx, lse, _ = _ops.topk_attn_fwd(q.reshape(1, b * n, dk).to(DEV), keys.reshape(1, e * m, dk).to(DEV),
+                                          values.reshape(1, e * m, dk).to(DEV), k, 1.0, seg_bias=bias.to(DEV))
+    assert _native.device_status(clear=True) == 0
+    gidx = idx.cpu().numpy().reshape(b * n, k)
+    oidx = oidx.reshape(b * n, k)
+    special = [5, 7]
+    for r in special:
+        assert np.array_equal(np.sort(gidx[r]), np.sort(oidx[r])), r
+    rest = np.setdiff1d(np.arange(b * n), special)
+    sc = np.einsum("nd,md->nm", qf.reshape(-1, dk).astype(np.float64), kf.reshape(-1, dk).astype(np.float64))
+    sc = sc + np.repeat(oracle.gate_bias(gf).reshape(b * n, e).astype(np.float64), m, axis=1)
+    _assert_indices(gidx[rest][None], oidx[rest][None], sc[rest][None], tol=1e-4, ordered=False,
+                    max_near_ties=max(1, len(rest) // 100))
+    np.testing.assert_allclose(out.float().cpu().numpy().reshape(b, n, dk), o, rtol=2e-2, atol=2e-2)
+    np.testing.assert_allclose(lse.cpu().numpy().reshape(b, n), olse, rtol=1e-5, atol=1e-5)
 
 
 def test_gated_mixture_without_gates_is_flat_top_k():
@@ -860,3 +1007,56 @@ def test_deterministic_switch_routes_autograd_through_key_major_kernels():
                                     do.reshape(2, -1, 64), idx.view(2, -1, 32), lse.view(2, -1), 1 / 8)
     for a, b in zip(runs[0], ref):
         assert torch.equal(a.reshape(b.shape), b)
+
+
+def _torch_sparse_attention(scores, values, k):
+    # plain torch fp32 restatement of the op, for the gradient check below
+    sel, idx = scores.topk(k, dim=-1)
+    p = torch.softmax(sel, dim=-1)
+    weights = torch.zeros_like(scores).scatter(-1, idx, p)
+    masked = torch.full_like(scores, float("-inf")).scatter(-1, idx, sel)
+    if values.ndim == 2:
+        gathered = values[idx]
+    else:
+        gathered = torch.stack([values[b][idx[b]] for b in range(values.shape[0])])
+    out = (gathered * p.unsqueeze(-1)).sum(-2)
+    return out, weights, idx, masked
+
+
+@pytest.mark.parametrize("batched", [False, True])
+def test_sparse_topk_attention_kernels_vs_torch_with_all_gradients(batched):
+    # Output, dense weights and masked scores, and the gradients that reach the
+    # scores and values through all three, against a plain torch restatement.
+    from sparsedict_b200 import selection
+
+    g = torch.Generator(device=DEV).manual_seed(17)
+    b, q, m, d, k = 3, 40, 100, 16, 9
+    scores = torch.randn(b, q, m, device=DEV, generator=g).requires_grad_(True)
+    values = (torch.randn(b, m, d, device=DEV, generator=g) if batched
+              else torch.randn(m, d, device=DEV, generator=g)).requires_grad_(True)
+    A, B, C = (torch.randn(s, device=DEV, generator=g) for s in ((b, q, d), (b, q, m), (b, q, m)))
+    res = selection.sparse_topk_attention(scores, values, k)
+    ref = _torch_sparse_attention(scores, values, k)
+    assert torch.equal(res.indices, ref[2])
+    for got, exp in ((res.output, ref[0]), (res.weights, ref[1]), (res.masked_scores, ref[3])):
+        torch.testing.assert_close(got, exp, atol=1e-5, rtol=1e-5)
+
+    def loss(out, weights, masked):
+        return (out * A).sum() + (weights * B).sum() + (masked.masked_fill(torch.isinf(masked), 0) * C).sum()
+
+    got = torch.autograd.grad(loss(res.output, res.weights, res.masked_scores), (scores, values))
+    exp = torch.autograd.grad(loss(ref[0], ref[1], ref[3]), (scores, values))
+    for a, e in zip(got, exp):
+        torch.testing.assert_close(a, e, atol=1e-5, rtol=1e-5)
+
+
+def test_sparse_topk_attention_promotes_mixed_dtypes():
+    from sparsedict_b200 import selection
+
+    g = torch.Generator(device=DEV).manual_seed(3)
+    scores = torch.randn(50, 64, device=DEV, generator=g).to(torch.bfloat16)
+    values = torch.randn(64, 8, device=DEV, generator=g)
+    res = selection.sparse_topk_attention(scores, values, 5)
+    assert res.output.dtype == torch.float32 and res.weights.dtype == torch.bfloat16
+    ref = _torch_sparse_attention(scores.float(), values, 5)
+    torch.testing.assert_close(res.output, ref[0], atol=1e-5, rtol=1e-5)
