@@ -14,10 +14,13 @@
 //              B_i = sum_j P_ij k_j in one pass over the gathered rows;
 //              dq_i = scale·(A_i - delta_i B_i) = scale·sum_j dS_ij k_j
 //              (dS = P (g - delta)).  It writes dq_i and (lse_i, delta_i).
-//   transpose  one CTA per slice: a stable counting sort of the slice's
-//              (row, key) pairs by key — per-warp 16-bit histograms over
-//              contiguous row ranges, an exclusive scan, then each warp
-//              places its entries in row order (ties inside a 32-entry batch
+//   transpose  a stable counting sort of each slice's (row, key) pairs by
+//              key, in three launches over chunks of CH rows (one warp per
+//              chunk): count (the chunk's per-key 16-bit counts, from a
+//              shared-memory histogram), scan (per slice: for each key the
+//              exclusive sum over the slice's chunks in order, and the key
+//              offsets), place (each warp walks its chunk's entries in order
+//              from its prefix cursors, equal keys inside a 32-entry batch
 //              ranked by lane) — giving each key the list of rows that
 //              selected it, in ascending row order.
 //   keys       one warp per key j: over its rows i (four per load, eight
@@ -38,8 +41,10 @@ namespace {
 
 constexpr int D = 64;
 constexpr int RW = 8;        // warps per block of the row and key passes
-constexpr int TW = 4;        // warps of a transpose CTA (one histogram each)
-constexpr int kMaxKeys = 16384;  // keys per slice the transpose histograms hold
+constexpr int CH = 256;      // rows per transpose chunk (one warp)
+constexpr int TW = 6;        // chunk warps per block of the count and place kernels
+constexpr int SCAN_NT = 1024;    // threads of a scan block (one per slice)
+constexpr int kMaxKeys = 16384;  // keys per slice the 16-bit chunk histograms hold
 
 template <typename T>
 __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
@@ -62,16 +67,6 @@ __device__ __forceinline__ float group_sum8(float x) {
   return x;
 }
 
-__device__ __forceinline__ int64_t slice_of(const SliceGeometry& g, int64_t r) {
-  if (!g.row_offsets) return r / g.n;
-  int64_t lo = 0, hi = g.slices - 1;
-  while (lo < hi) {
-    const int64_t mid = (lo + hi + 1) >> 1;
-    if ((int64_t)g.row_offsets[mid] <= r) lo = mid; else hi = mid - 1;
-  }
-  return lo;
-}
-
 struct KmArgs {
   const void* q;
   const void* k;
@@ -85,12 +80,15 @@ struct KmArgs {
   SliceGeometry geo;
   const int32_t* row_index;
   int64_t rows, m;
+  int64_t phys_rows;   // rows of q / dout (the physical row space)
   int topk;
   float scale;
   unsigned int* status;
   float2* rowstat;     // [physical row] (lse, delta)
   int32_t* key_off;    // [slices][m + 1] start of each key's row list
   int32_t* key_rows;   // [rows * topk] physical rows, grouped by key
+  uint32_t* chunk_cnt; // [chunks][m / 2] 16-bit per-key counts, then prefixes
+  int64_t chunks;      // chunk ids launched (grouped: surplus ids are empty)
   int out_acc;         // 1: dk/dv are fp32 accumulators
   int accumulate;      // with out_acc: add to them instead of overwriting
 };
@@ -103,7 +101,7 @@ __global__ void __launch_bounds__(RW * kWarp, 4) km_rows(KmArgs a) {
   const T* __restrict__ q = static_cast<const T*>(a.q);
   const T* __restrict__ dout = static_cast<const T*>(a.dout);
   for (int64_t r = (int64_t)blockIdx.x * RW + warp; r < a.rows; r += (int64_t)gridDim.x * RW) {
-    const int64_t slice = slice_of(a.geo, r);
+    const int64_t slice = slice_of_row(a.geo, r);
     const int64_t pr = a.row_index ? (int64_t)a.row_index[r] : r;
     const uint4* __restrict__ kmat = reinterpret_cast<const uint4*>(static_cast<const T*>(a.k) + slice * a.m * D) + l8;
     const uint4* __restrict__ vmat = reinterpret_cast<const uint4*>(static_cast<const T*>(a.v) + slice * a.m * D) + l8;
@@ -172,33 +170,27 @@ __global__ void __launch_bounds__(RW * kWarp, 4) km_rows(KmArgs a) {
 }
 
 // ------------------------------------------------------------ transpose ---
-// Shared memory: TW histograms of m 16-bit counters (two per 32-bit word),
-// then m + 1 32-bit list offsets.
-__device__ __forceinline__ uint32_t hist_get(const uint32_t* h, int key) {
-  return (h[key >> 1] >> ((key & 1) * 16)) & 0xffffu;
-}
+// Chunk c: rows [row0, row0 + count) of one slice (locate_tile with CH rows).
+// A chunk's histogram holds m 16-bit counters, two per 32-bit word; a chunk
+// has at most CH rows, so a key's count (one entry per row for distinct
+// selections) stays far below 2^16, and a slice's per-key prefix stays below
+// 2^16 with at most 65535 rows per slice.
+__device__ __forceinline__ uint32_t half_get(uint32_t w, int key) { return (w >> ((key & 1) * 16)) & 0xffffu; }
 
-__global__ void __launch_bounds__(TW * kWarp) km_transpose(KmArgs a) {
-  extern __shared__ uint32_t tsm[];
+__global__ void __launch_bounds__(TW * kWarp) km_count(KmArgs a) {
+  extern __shared__ uint32_t csm[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t slice = blockIdx.x;
-  const int m = (int)a.m;
-  const int hw = (m + 1) >> 1;  // words per histogram
-  uint32_t* hist = tsm;         // [TW][hw]
-  int32_t* off = reinterpret_cast<int32_t*>(tsm + TW * hw);  // [m + 1]
-  __shared__ int32_t carry[TW * kWarp];
-  const int64_t rb = a.geo.row_offsets ? (int64_t)a.geo.row_offsets[slice] : slice * a.geo.n;
-  const int64_t re = a.geo.row_offsets ? (int64_t)a.geo.row_offsets[slice + 1] : rb + a.geo.n;
-  for (int i = threadIdx.x; i < TW * hw; i += blockDim.x) hist[i] = 0u;
-  __syncthreads();
-  // rows of warp w: [w0, w1)
-  const int64_t per = (re - rb + TW - 1) / TW;
-  const int64_t w0 = rb + warp * per < re ? rb + warp * per : re;
-  const int64_t w1 = w0 + per < re ? w0 + per : re;
-  const int64_t e0 = w0 * a.topk, e1 = w1 * a.topk;
-  uint32_t* myh = hist + warp * hw;
-  // eight 32-entry batches per step: their loads are in flight together
-  constexpr int U = 8;
+  const int64_t c = (int64_t)blockIdx.x * TW + warp;
+  if (c >= a.chunks) return;
+  const int m = (int)a.m, hw = (m + 1) >> 1;
+  uint32_t* h = csm + warp * hw;
+  for (int i = lane; i < hw; i += kWarp) h[i] = 0u;
+  __syncwarp();
+  int64_t slice, row0;
+  int count;
+  locate_tile(a.geo, c, CH, &slice, &row0, &count);
+  const int64_t e0 = row0 * a.topk, e1 = (row0 + count) * a.topk;
+  constexpr int U = 8;  // eight 32-entry batches in flight
   for (int64_t e = e0; e < e1; e += U * kWarp) {
     int key[U];
 #pragma unroll
@@ -208,58 +200,121 @@ __global__ void __launch_bounds__(TW * kWarp) km_transpose(KmArgs a) {
     }
 #pragma unroll
     for (int u = 0; u < U; ++u)
-      if (key[u] >= 0 && key[u] < m) atomicAdd(&myh[key[u] >> 1], 1u << ((key[u] & 1) * 16));
+      if (key[u] >= 0 && key[u] < m) atomicAdd(&h[key[u] >> 1], 1u << ((key[u] & 1) * 16));
   }
-  __syncthreads();
-  // exclusive scan of the per-key totals; each thread takes a contiguous run of keys
-  const int nt = TW * kWarp;
-  // an even run: a histogram word holds two keys' counters, so every word has
-  // exactly one owner in the read-modify-write below
-  const int run = (((m + nt - 1) / nt) + 1) & ~1;
-  const int k0 = threadIdx.x * run < m ? threadIdx.x * run : m;
-  const int k1 = k0 + run < m ? k0 + run : m;
-  int32_t sum = 0;
-  for (int key = k0; key < k1; ++key)
-    for (int w = 0; w < TW; ++w) sum += (int32_t)hist_get(hist + w * hw, key);
-  carry[threadIdx.x] = sum;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int32_t acc = 0;
-    for (int t = 0; t < nt; ++t) {
-      const int32_t c = carry[t];
-      carry[t] = acc;
-      acc += c;
+  __syncwarp();
+  uint32_t* dst = a.chunk_cnt + c * hw;
+  for (int i = lane; i < hw; i += kWarp) dst[i] = h[i];
+}
+
+// One block per slice: each thread walks counter words (two keys) over the
+// slice's chunks in order, replacing each count by the exclusive prefix, and
+// keeps the per-key totals; a block-wide exclusive scan of the totals gives
+// the key offsets.
+__global__ void __launch_bounds__(SCAN_NT) km_scan(KmArgs a) {
+  extern __shared__ uint32_t ssm[];  // [hw] per-key totals, two per word
+  __shared__ int32_t wsum[SCAN_NT / kWarp];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int64_t slice = blockIdx.x;
+  const int m = (int)a.m, hw = (m + 1) >> 1;
+  int64_t rb, re, c0;
+  if (a.geo.row_offsets) {
+    rb = a.geo.row_offsets[slice];
+    re = a.geo.row_offsets[slice + 1];
+    c0 = 0;
+    for (int64_t s = 0; s < slice; ++s)
+      c0 += ((int64_t)a.geo.row_offsets[s + 1] - a.geo.row_offsets[s] + CH - 1) / CH;
+  } else {
+    rb = slice * a.geo.n;
+    re = rb + a.geo.n;
+    c0 = slice * ((a.geo.n + CH - 1) / CH);
+  }
+  const int64_t nc = (re - rb + CH - 1) / CH;
+  for (int w = t; w < hw; w += SCAN_NT) {
+    uint32_t run = 0u;  // two 16-bit running sums (no carry: each stays below 2^16)
+    constexpr int U = 8;  // chunk words in flight
+    for (int64_t cb = c0; cb < c0 + nc; cb += U) {
+      uint32_t v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) v[u] = cb + u < c0 + nc ? a.chunk_cnt[(cb + u) * hw + w] : 0u;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (cb + u < c0 + nc) a.chunk_cnt[(cb + u) * hw + w] = run;
+        run += v[u];
+      }
     }
+    ssm[w] = run;
   }
   __syncthreads();
-  int32_t base = carry[threadIdx.x] + (int32_t)(rb * a.topk);
+  // keys [k0, k1) of thread t, contiguous
+  const int per = (m + SCAN_NT - 1) / SCAN_NT;
+  const int k0 = t * per < m ? t * per : m, k1 = k0 + per < m ? k0 + per : m;
+  int32_t local = 0;
+  for (int key = k0; key < k1; ++key) local += (int32_t)half_get(ssm[key >> 1], key);
+  int32_t incl = local;
+#pragma unroll
+  for (int o = 1; o < kWarp; o <<= 1) {
+    const int32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == kWarp - 1) wsum[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int32_t x = lane < SCAN_NT / kWarp ? wsum[lane] : 0;
+    int32_t xi = x;
+#pragma unroll
+    for (int o = 1; o < kWarp; o <<= 1) {
+      const int32_t y = __shfl_up_sync(0xffffffffu, xi, o);
+      if (lane >= o) xi += y;
+    }
+    if (lane < SCAN_NT / kWarp) wsum[lane] = xi - x;
+  }
+  __syncthreads();
+  int32_t base = (int32_t)(rb * a.topk) + wsum[warp] + (incl - local);
+  int32_t* koff = a.key_off + slice * (a.m + 1);
   for (int key = k0; key < k1; ++key) {
-    off[key] = base;
-    a.key_off[slice * (a.m + 1) + key] = base;
-    // turn warp w's count into the number of entries of warps before w
-    int32_t before = 0;
-    for (int w = 0; w < TW; ++w) {
-      uint32_t* hp = hist + w * hw + (key >> 1);
-      const uint32_t sh = (key & 1) * 16;
-      const int32_t c = (int32_t)((*hp >> sh) & 0xffffu);
-      *hp = (*hp & ~(0xffffu << sh)) | ((uint32_t)before << sh);
-      before += c;
-    }
-    base += before;
+    koff[key] = base;
+    base += (int32_t)half_get(ssm[key >> 1], key);
   }
-  if (threadIdx.x == nt - 1) a.key_off[slice * (a.m + 1) + m] = base;
-  __syncthreads();
-  // place the entries: warp w walks its rows in order; inside a batch of 32
-  // entries, lanes holding the same key are ranked by lane
+  // the end of the last key's list: the slice start plus every counted entry
+  // (entries with keys outside [0, m) are not listed)
+  if (t == SCAN_NT - 1) koff[m] = base;
+}
+
+__global__ void __launch_bounds__(TW * kWarp) km_place(KmArgs a) {
+  extern __shared__ uint32_t psm[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t c = (int64_t)blockIdx.x * TW + warp;
+  if (c >= a.chunks) return;
+  const int m = (int)a.m, hw = (m + 1) >> 1;
+  int64_t slice, row0;
+  int count;
+  locate_tile(a.geo, c, CH, &slice, &row0, &count);
+  if (count <= 0) return;
+  uint32_t* cur = psm + warp * hw;
+  const uint32_t* src = a.chunk_cnt + c * hw;
+  for (int i = lane; i < hw; i += kWarp) cur[i] = src[i];
+  __syncwarp();
+  const int32_t* koff = a.key_off + slice * (a.m + 1);
+  const int64_t rb = slice_row_begin(a.geo, slice);
+  const int64_t lo = rb * a.topk, hi = (int64_t)koff[m];  // the slice's list range
+  const int64_t e0 = row0 * a.topk, e1 = (row0 + count) * a.topk;
   const unsigned lt = (1u << lane) - 1u;
+  // row of an entry: floor((x + 0.5) / topk) for the chunk-local entry x < CH * 64;
+  // the float quotient's error (< 2^-13) stays below the 1/(2 topk) margin
+  const float inv_topk = 1.f / (float)a.topk;
+  constexpr int U = 8;
   for (int64_t e = e0; e < e1; e += U * kWarp) {
     int keys[U];
+    int32_t kb[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int64_t ee = e + u * kWarp + lane;
       keys[u] = ee < e1 ? a.top_idx[ee] : -1;
       if (keys[u] >= m) keys[u] = -1;
     }
+#pragma unroll
+    for (int u = 0; u < U; ++u) kb[u] = keys[u] >= 0 ? koff[keys[u]] : 0;
     // the batches in order (ranks stay in row order across batches)
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -267,18 +322,18 @@ __global__ void __launch_bounds__(TW * kWarp) km_transpose(KmArgs a) {
       const int64_t ee = e + u * kWarp + lane;
       const unsigned same = __match_any_sync(0xffffffffu, key);
       const int rank = __popc(same & lt);
-      int32_t pos = 0;
-      if (key >= 0) pos = off[key] + (int32_t)hist_get(myh, key) + rank;
+      int64_t pos = 0;
+      if (key >= 0) pos = (int64_t)kb[u] + half_get(cur[key >> 1], key) + rank;
       __syncwarp();
-      if (key >= 0 && rank == 0) {
-        // the group's first lane advances the key's cursor by the group size
-        uint32_t* hp = myh + (key >> 1);
-        atomicAdd(hp, (uint32_t)__popc(same) << ((key & 1) * 16));
-      }
+      if (key >= 0 && rank == 0) atomicAdd(&cur[key >> 1], (uint32_t)__popc(same) << ((key & 1) * 16));
       __syncwarp();
       if (key >= 0) {
-        const int64_t r = ee / a.topk;
-        a.key_rows[pos] = a.row_index ? a.row_index[r] : (int32_t)r;
+        if (pos >= lo && pos < hi) {
+          const int64_t r = row0 + (int64_t)(((float)(int)(ee - e0) + 0.5f) * inv_topk);
+          a.key_rows[pos] = a.row_index ? a.row_index[r] : (int32_t)r;
+        } else {
+          raise_device_status(a.status, kStatusIndexOutOfRange);  // inconsistent counts: duplicate keys in a row
+        }
       }
     }
   }
@@ -308,7 +363,7 @@ __global__ void __launch_bounds__(RW * kWarp, 4) km_keys(KmArgs a) {
       for (int t = 0; t < cnt; t += 4) {
         const int src = t + grp;
         const int32_t row = __shfl_sync(0xffffffffu, my, src & 31);
-        const bool ok = src < cnt;
+        const bool ok = src < cnt && row >= 0 && row < a.phys_rows;
         uint4 qu = make_uint4(0u, 0u, 0u, 0u), du = qu;
         float2 st = make_float2(0.f, 0.f);
         if (ok) {
@@ -386,10 +441,15 @@ __global__ void __launch_bounds__(RW * kWarp, 4) km_keys(KmArgs a) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-// Workspace layout (16-byte aligned parts): rowstat [phys rows] float2,
-// key_off [slices][m + 1] int32, key_rows [rows * topk] int32.
+// Transpose chunks: enough for uniform slices (slices * ceil(n / CH)) and
+// for grouped ones (ceil(rows / CH) + slices) alike.
+int64_t km_chunk_bound(int64_t rows, int64_t slices) { return (rows + CH - 1) / CH + slices; }
+
+// Workspace layout (256-byte aligned parts): rowstat [phys rows] float2,
+// key_off [slices][m + 1] int32, key_rows [rows * topk] int32, chunk
+// counters [chunks][(m + 1) / 2] uint32.
 struct KmLayout {
-  size_t rowstat, key_off, key_rows, total;
+  size_t rowstat, key_off, key_rows, chunk_cnt, total;
 };
 
 KmLayout km_layout(int64_t rows, int64_t phys_rows, int64_t slices, int64_t m, int topk) {
@@ -398,7 +458,8 @@ KmLayout km_layout(int64_t rows, int64_t phys_rows, int64_t slices, int64_t m, i
   L.rowstat = 0;
   L.key_off = up((size_t)phys_rows * sizeof(float2));
   L.key_rows = L.key_off + up((size_t)slices * (size_t)(m + 1) * 4);
-  L.total = L.key_rows + up((size_t)rows * (size_t)topk * 4);
+  L.chunk_cnt = L.key_rows + up((size_t)rows * (size_t)topk * 4);
+  L.total = L.chunk_cnt + up((size_t)km_chunk_bound(rows, slices) * (size_t)((m + 1) / 2) * 4);
   return L;
 }
 
@@ -423,16 +484,29 @@ int launch_km(const BwdLaunch& L, void* dk, void* dv, int out_acc, int accumulat
   a.rowstat = reinterpret_cast<float2*>(w + lay.rowstat);
   a.key_off = reinterpret_cast<int32_t*>(w + lay.key_off);
   a.key_rows = reinterpret_cast<int32_t*>(w + lay.key_rows);
+  a.chunk_cnt = reinterpret_cast<uint32_t*>(w + lay.chunk_cnt);
+  a.chunks = L.row_offsets ? km_chunk_bound(rows, L.slices) : L.slices * ((L.n + CH - 1) / CH);
+  a.phys_rows = rows;
   a.out_acc = out_acc;
   a.accumulate = accumulate;
   if (rows > 0) {
     km_rows<T><<<(unsigned)((rows + RW - 1) / RW), RW * kWarp, 0, L.stream>>>(a);
     if (cudaPeekAtLastError() != cudaSuccess) return SDK_ERR_CUDA;
   }
-  const size_t tsmem = (size_t)TW * (size_t)((L.m + 1) / 2) * 4 + (size_t)(L.m + 1) * 4;
-  if (cudaFuncSetAttribute(km_transpose, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsmem) != cudaSuccess)
+  const size_t hsm = (size_t)TW * (size_t)((L.m + 1) / 2) * 4;  // one histogram per warp
+  const size_t ssm = (size_t)((L.m + 1) / 2) * 4;
+  if (cudaFuncSetAttribute(km_count, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hsm) != cudaSuccess ||
+      cudaFuncSetAttribute(km_place, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hsm) != cudaSuccess ||
+      cudaFuncSetAttribute(km_scan, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssm) != cudaSuccess)
     return SDK_ERR_CUDA;
-  km_transpose<<<(unsigned)L.slices, TW * kWarp, tsmem, L.stream>>>(a);
+  const unsigned cblocks = (unsigned)((a.chunks + TW - 1) / TW);
+  if (a.chunks > 0) {
+    km_count<<<cblocks, TW * kWarp, hsm, L.stream>>>(a);
+    km_scan<<<(unsigned)L.slices, SCAN_NT, ssm, L.stream>>>(a);
+    km_place<<<cblocks, TW * kWarp, hsm, L.stream>>>(a);
+  } else {
+    km_scan<<<(unsigned)L.slices, SCAN_NT, ssm, L.stream>>>(a);
+  }
   if (cudaPeekAtLastError() != cudaSuccess) return SDK_ERR_CUDA;
   const int64_t keys = L.slices * L.m;
   km_keys<T><<<(unsigned)((keys + RW - 1) / RW), RW * kWarp, 0, L.stream>>>(a);
