@@ -1,61 +1,41 @@
 // Fused top-k attention forward on the 5th-generation tensor cores (sm_100a).
 //
-// One CTA owns 256 query rows of one (b, h) slice (d = dv = 64, bf16 or fp16)
-// as two 128-row tiles, A and B, and streams the slice's keys in tiles of 128:
+// One CTA owns 128 query rows of one (b, h) slice (d = dv = 64, bf16 or fp16)
+// and streams the slice's keys twice in tiles of 256:
 //
-//   warp 0       TMA producer: both Q tiles once, then each K tile into one
-//                128-byte-swizzled shared-memory buffer (the MMAs of a tile
-//                take a fraction of a microsecond, a tile's selection several,
-//                so one buffer never starves the pipeline);
+//   warp 0       TMA producer: the query tile once, then every K tile of
+//                both passes into a 4-stage ring of 128-byte-swizzled
+//                shared-memory buffers;
 //   warp 1       allocates 512 TMEM columns and issues tcgen05.mma
-//                (M=128, N=128, K=16 x 4) of S_A = Q_A·Kᵀ and S_B = Q_B·Kᵀ
-//                for every K tile, each into one of two TMEM accumulators of
-//                its query tile, committing to "S full" / "stage free"
-//                mbarriers;
+//                (M=128, N=256, K=16 x 4) of S = Q·Kᵀ for every K tile into
+//                one of two 256-column accumulators, committing to "S full"
+//                / "stage free" mbarriers;
 //   warps 2, 3   in the first CTA of each slice: the input magnitude check
-//                of the slice's keys (below); idle elsewhere;
-//   warps 4..7   selection for tile A, warps 8..11 for tile B (two selection
-//                warps per SM sub-partition): thread i of a group owns query
-//                row i of its tile (TMEM lane i), reads its 128 scores of the
-//                K tile with tcgen05.ld, and appends every key that beats the
-//                row's running threshold to a slot-major shared-memory list.
+//                of the slice's keys (below); for grouped rows: the gather of
+//                the query rows through the permutation;
+//   warps 4..11  selection: thread i of warp 4+j (j < 4) and of warp 8+j own
+//                query row 32j+i (TMEM lane); the first reads columns 0..127
+//                of each 256-key tile, the second columns 128..255.
 //
-// A list entry is 4 bytes: the upper 16 bits of the fp32 score's bit pattern
-// (its bf16 truncation, which names the score's bf16 "bucket") and the 16-bit
-// key index.  When a list could overflow it is compacted with a bucket pivot:
-// the highest of 16 sampled buckets that at least k listed keys reach.  Keys
-// below that bucket are dropped and the row's threshold becomes the lowest
-// score of the bucket; both steps are exact (no top-k key is ever dropped).
-// A row whose list cannot be shrunk that way (more than ~100 listed keys
-// share the cut bucket, which needs heavily tied scores) is marked and
-// re-selected exactly at the end, see below.
+// Pass 1 records, per row, the maxima of disjoint groups of G keys (G chosen
+// per call so that a row has at most 256 groups), rounded down to bf16.  The
+// k-th largest group maximum tau is a lower bound of the row's k-th largest
+// score: k different groups, so k different keys, reach it.  The two threads
+// of a row find it by a bisection over the bf16 values, exchanging partial
+// counts through shared memory.
 //
-// After the last tile each selection thread writes its row's list (at most
-// 176 entries, four per 16-byte store) and count to a candidate buffer in
-// HBM, and the CTA ends: the SM is free for the next CTA's stream while the
-// exact work runs elsewhere.  A second kernel, one warp per query row at high
-// occupancy, finishes every row:
+// Pass 2 recomputes the scores and keeps the key of every score that reaches
+// tau (a packed bf16 compare of the truncated scores: conservative), in the
+// thread's half of the row's candidate list in global memory.  For Gaussian
+// inputs about 1.15·k keys per row pass.  A second kernel, one warp per row,
+// re-scores the candidates exactly from the gathered key rows (one fixed
+// fp32 summation order), keeps the k best (larger score first, lower key
+// index on ties), and writes the LSE, the indices and the softmax-weighted
+// sum of the gathered value rows.  A row whose candidates overflow its list
+// (heavily tied scores) is re-selected exactly by its warp over all keys.
 //
-//   bucket cut   the k-th largest bucket of the row's entries, by 8-bit radix
-//                digits over a shared histogram (from the highest bit in
-//                which the row's buckets differ); entries of lower buckets
-//                cannot be in the top k and are dropped;
-//   re-score     each survivor's fp32 score is recomputed from the gathered
-//                key row (eight lanes per 128-byte row, one fixed summation
-//                order);
-//   exact cut    the k best by order-preserving keys (score, then lower key
-//                index on ties), by the same radix select;
-//   epilogue     row LSE, the k indices (in list order; the set is the
-//                reference's top-k set) and the softmax-weighted sum of the
-//                gathered value rows.
-//
-// Marked rows are re-selected by their warp: lanes score 32 keys at a time
-// with the same summation order and keep an exact candidate list sorted by a
-// warp bitonic network, as the CUDA-core kernel does.
-//
-// Selection runs on the raw dot products; scale = 1/(T·sqrt(d)) > 0 is
-// applied in the epilogue (for d = 64 and T a power of two the scale is a
-// power of two, so the order is exactly that of the scaled scores).
+// scale = 1/(T·sqrt(d)) > 0 is applied in the epilogue, or, with a segment
+// bias, to each exact score as fl(fl(dot·scale)+bias).
 #include <cuda.h>
 
 #include <mutex>
@@ -70,50 +50,53 @@ namespace {
 
 using namespace sm100;
 
-constexpr int TQ = 128;         // query rows per tile (TMEM lanes, MMA M)
-constexpr int NTILE = 2;        // query tiles per CTA
-constexpr int RS = TQ * NTILE;  // rows per CTA; row stride of the slot-major lists
-constexpr int TK = 128;         // keys per score tile (MMA N)
-constexpr int D = 64;           // feature width (one 128-byte swizzle row)
-constexpr int KSTAGES = 1;
-constexpr int CAP = 160;        // list slots per row (and candidate buffer entries per row)
-constexpr int FIX_CAP = 128;    // exact list of a row re-selected by one warp
-constexpr int kDenseHits = 8;   // a chunk row with more hits makes the warp append branch-free
+constexpr int TQ = 128;          // query rows per CTA (TMEM lanes, MMA M)
+constexpr int TK = 256;          // keys per score tile (MMA N)
+constexpr int HALF = TK / 2;     // keys of a tile per selection thread
+constexpr int D = 64;            // feature width (one 128-byte swizzle row)
+constexpr int KSTAGES = 4;
+constexpr int CAP = 128;         // candidate keys per row
+constexpr int CAPH = CAP / 2;    // candidate keys of each of the row's two selection threads
+constexpr int FIX_CAP = 128;     // exact list of a row re-selected by one warp
+constexpr int NGW = 64;          // group-maximum words per selection thread (two bf16 each)
 constexpr int NT = 384;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t TILE_BYTES = TK * D * 2;  // a K tile, also a Q tile
+constexpr uint32_t Q_BYTES = TQ * D * 2;
+constexpr uint32_t K_BYTES = TK * D * 2;
 
 constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + NTILE * (int)TILE_BYTES;
-constexpr int OFF_LIST = OFF_K + KSTAGES * (int)TILE_BYTES;
-constexpr int OFF_STAGE = OFF_LIST + CAP * RS * 4;  // per row: the current chunk's 32 buckets
-constexpr int OFF_BAR = OFF_STAGE + RS * 64;
-constexpr int NBARS = 1 + 2 * KSTAGES + 4 * NTILE;
+constexpr int OFF_K = OFF_Q + (int)Q_BYTES;
+constexpr int OFF_GM = OFF_K + KSTAGES * (int)K_BYTES;  // [half][word][row] group maxima
+constexpr int OFF_XCH = OFF_GM + 2 * NGW * TQ * 4;      // [slot][half][row] the tau search's exchange
+constexpr int OFF_BAR = OFF_XCH + 2 * 2 * TQ * 4;
+constexpr int NBARS = 1 + 2 * KSTAGES + 4;
 constexpr int OFF_MISC = OFF_BAR + NBARS * 8;
 constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
-static_assert(CAP % 4 == 0, "lists are written four entries per store");
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 static_assert(OFF_BAR % 8 == 0, "mbarrier alignment");
+static_assert(OFF_GM % 1024 == 0 && OFF_K % 1024 == 0, "swizzled tiles need 1024-byte alignment");
 
-// Count word of a row in the candidate buffer: the number of entries, or
-constexpr int32_t kCandDead = -1;     // list could not be shrunk: re-select exactly
+// Count words of a row in the candidate buffer, one per selection thread:
+// the number of keys it found (more than CAPH: its half of the list
+// overflowed, re-select the row exactly), or
 constexpr int32_t kCandAborted = -2;  // a pipeline wait timed out: nothing to finish
 
 struct TcArgs {
   const void* q;     // query rows, gathered through row_index when that is set
   const void* k;     // key rows, for the magnitude check
   const int32_t* row_index;  // nullable: logical row -> query row (grouped slices)
-  uint32_t* cand;    // [rows][CAP] list entries of each query row
-  int32_t* cand_n;   // [rows] entry count, kCandDead or kCandAborted
+  uint16_t* cand;    // [rows][2][CAPH] candidate keys of each query row, per selection thread
+  int32_t* cand_n;   // [rows][2] key counts or kCandAborted
   uint32_t* unsafe;  // [rows], at each slice's first row: 1 when a key of the slice fails the magnitude check
   SliceGeometry geo;
   int64_t m;
   int topk;
+  int glog;          // log2 of the keys per group maximum (5 .. 8)
   uint32_t big16;    // 16-bit magnitude field at which an element counts as unsafe
   unsigned int* status;
   uint64_t wait_limit_ns;  // bound of each pipeline wait (sdk_set_wait_limit)
-  // kBias: score(r, j) = dot * scale + seg_bias[r * segs + j / seg_len], with
-  // seg_len a multiple of TK so that each key tile lies in one segment
+  // kBias: score(r, j) = fl(fl(dot * scale) + seg_bias[r * segs + j / seg_len]),
+  // seg_len a multiple of HALF so that each thread's half tile lies in one segment
   const float* seg_bias;
   int64_t seg_len;
   int segs;
@@ -122,7 +105,7 @@ struct TcArgs {
 
 // Input magnitude check.  With every |q|, |k| < 2^60 and finite, each of the
 // 64 products is below 2^120 and their fp32 sum below 2^126, so no score can
-// overflow to inf or become NaN; the stream filter then needs no NaN
+// overflow to inf or become NaN; the stream passes then need no NaN
 // handling.  Rows whose inputs fail the check (a non-finite or huge element
 // in the query row or anywhere in the slice's keys) are re-selected exactly
 // by the finish kernel.  `big16` is the lowest 15-bit magnitude pattern that
@@ -134,269 +117,89 @@ __device__ __forceinline__ uint32_t big_halves(uint32_t w, uint32_t add) {
   return ((w & 0x7fff7fffu) + add) & 0x80008000u;
 }
 
+// ------------------------------------------------------------ pass helpers ---
+constexpr uint32_t kBf16NegInf = 0xff80u;
+constexpr uint32_t kBf16PosInf = 0x7f80u;
 
-// ---------------------------------------------------- bucketed list entries ---
-// Order-preserving form of an entry: the high 16 bits order the buckets like
-// their scores (negative scores complemented); the low 16 bits are not used.
-__device__ __forceinline__ uint32_t ord_entry(uint32_t e) {
-  return e ^ ((uint32_t)((int32_t)e >> 31) | 0x80000000u);
+// The largest bf16 value <= x (x not NaN): truncation, one step further from
+// zero for negative x with nonzero low bits.
+__device__ __forceinline__ uint32_t bf16_floor(float x) {
+  const uint32_t u = __float_as_uint(x);
+  return (u >> 16) + (((int32_t)u < 0 && (u & 0xffffu) != 0u) ? 1u : 0u);
 }
 
-// Threshold after a compaction that kept every key of bucket >= p (p is an
-// ordered bucket << 16): a later key x is dropped iff !(x > tau), i.e. iff its
-// ordered score is <= p.  At least k kept keys rank at or above p, and a later
-// key equal to them loses the index tie, so the drop is exact.
-__device__ __forceinline__ float tau_of_bucket(uint32_t p) {
-  if (p >= 0xff800000u) return __int_as_float(0x7f800000);  // only NaN ranks higher
-  if (p < 0x00800000u) return __int_as_float(0x7fc00000);   // at or below -inf: admit all
-  return __uint_as_float((p & 0x80000000u) ? (p & 0x7fffffffu) : ~p);
-}
+// Order-preserving 16-bit code of a bf16 value and its inverse.
+__device__ __forceinline__ uint32_t bf16_ord(uint32_t b) { return b ^ ((b & 0x8000u) ? 0xffffu : 0x8000u); }
+__device__ __forceinline__ uint32_t bf16_of_ord(uint32_t o) { return o ^ ((o & 0x8000u) ? 0x8000u : 0xffffu); }
 
-__device__ __forceinline__ void sort16_desc(uint32_t (&x)[16]) {
-#pragma unroll
-  for (int size = 2; size <= 16; size <<= 1)
-#pragma unroll
-    for (int st = size >> 1; st > 0; st >>= 1)
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int j = i ^ st;
-        if (j > i) {
-          const bool desc = (i & size) == 0;
-          const uint32_t hi = max(x[i], x[j]), lo = min(x[i], x[j]);
-          x[i] = desc ? hi : lo;
-          x[j] = desc ? lo : hi;
-        }
-      }
-}
-
-template <typename V>
-__device__ __forceinline__ V pick16(const V (&x)[16], int want) {
-  V v = x[15];
-#pragma unroll
-  for (int j = 0; j < 16; ++j)
-    if (j == want) v = x[j];
-  return v;
-}
-
-// Counts of row R's listed entries whose ordered form reaches each of four
-// pivots.  Eight entries per step and two sets of counters keep several
-// loads and adds in flight (the counters are the only dependency chains).
-__device__ __forceinline__ void count4(const uint32_t* list, int R, int cnt, const uint32_t (&p)[4], int (&c)[4]) {
-  int a[4] = {0, 0, 0, 0}, b[4] = {0, 0, 0, 0};
-  int s = 0;
-  for (; s + 8 <= cnt; s += 8) {
-    uint32_t o[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) o[i] = ord_entry(list[(s + i) * RS + R]);
-#pragma unroll
-    for (int i = 0; i < 8; i += 2)
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        a[q] += (int)(o[i] >= p[q]);
-        b[q] += (int)(o[i + 1] >= p[q]);
-      }
-  }
-  for (; s < cnt; ++s) {
-    const uint32_t o = ord_entry(list[s * RS + R]);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) a[q] += (int)(o >= p[q]);
-  }
-#pragma unroll
-  for (int q = 0; q < 4; ++q) c[q] = a[q] + b[q];
-}
-
-// Keep the entries whose ordered score reaches `pivot`, in place and in
-// order.  Entries are read eight at a time ahead of the predicated stores:
-// a store goes to a slot at or below the slot being read, so the batch
-// already holds anything a store could overwrite, and the loads no longer
-// wait on the stores one by one.
-__device__ __forceinline__ int keep_pass(uint32_t* list, int R, int cnt, uint32_t pivot) {
-  uint32_t w = 0;
-  const uint32_t base = smem_addr(list) + 4u * R;
-  int s = 0;
-  for (; s + 8 <= cnt; s += 8) {
-    uint32_t e[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) e[i] = list[(s + i) * RS + R];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t keep = (uint32_t)(ord_entry(e[i]) >= pivot);
-      st_shared_u32_if(base + w * (4u * RS), e[i], keep);
-      w += keep;
-    }
-  }
-  for (; s < cnt; ++s) {
-    const uint32_t e = list[s * RS + R];
-    const uint32_t keep = (uint32_t)(ord_entry(e) >= pivot);
-    st_shared_u32_if(base + w * (4u * RS), e, keep);
-    w += keep;
-  }
-  return (int)w;
-}
-
-// Shrink row R's list to the keys whose bucket reaches the highest of 16
-// sampled buckets that at least `topk` listed keys reach (four candidate
-// pivots per counting pass, starting near the sample rank expected to keep
-// topk + slack*cnt/16 keys).  Returns false when no sampled pivot qualifies
-// or nothing would be dropped.  Kept out of line: it runs rarely, and one
-// copy keeps the streaming loop small enough for the instruction cache.
-struct Compacted {
-  int cnt;
-  float tau;
-  bool shrank;
-};
-
-__device__ __noinline__ Compacted compact_bucket(const uint32_t* list_c, int R, int cnt, float tau, int topk,
-                                                 int slack) {
-  uint32_t* list = const_cast<uint32_t*>(list_c);
-  uint32_t smp[16];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) smp[j] = ord_entry(list[((j * cnt) >> 4) * RS + R]) & 0xffff0000u;
-  sort16_desc(smp);
-  int t = (16 * topk) / (cnt > 0 ? cnt : 1) + slack - 1;
-  t = t < 0 ? 0 : (t > 12 ? 12 : t);
-  uint32_t pivot = 0;
-  bool found = false;
-  for (int pass = 0; pass < 4 && !found; ++pass) {
-    uint32_t p[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) p[q] = pick16(smp, t + q);
-    int c[4];
-    count4(list, R, cnt, p, c);
-#pragma unroll
-    for (int q = 3; q >= 0; --q)
-      if (c[q] >= topk) {
-        pivot = p[q];
-        found = true;
-      }
-    t = t + 4 > 12 ? 12 : t + 4;
-  }
-  if (!found) return Compacted{cnt, tau, false};
-  const int w = keep_pass(list, R, cnt, pivot);
-  // both thresholds are exact; keep the higher
-  return Compacted{w, fmaxf(tau, tau_of_bucket(pivot)), w < cnt};
-}
-
-// Exact bucket cut, for lists the sampled pivots cannot shrink: the highest
-// bucket P that at least `topk` listed keys reach, found by narrowing
-// [lowest bucket, highest bucket + 1) with four pivots per counting pass
-// (the range shrinks five-fold per pass), then keep the keys of bucket >= P.
-// What remains is k keys plus the other keys of bucket P; needs cnt >= topk.
-__device__ __noinline__ Compacted compact_bucket_exact(const uint32_t* list_c, int R, int cnt, float tau, int topk) {
-  uint32_t* list = const_cast<uint32_t*>(list_c);
-  uint32_t lo = 0xffffu, hi = 0u;
-  for (int s = 0; s < cnt; ++s) {
-    const uint32_t b = ord_entry(list[s * RS + R]) >> 16;
-    lo = min(lo, b);
-    hi = max(hi, b);
-  }
-  hi += 1u;  // count(>= lo) = cnt >= topk, count(>= hi) = 0 < topk
-  while (hi - lo > 1u) {
-    const uint32_t span = hi - lo;
-    uint32_t p[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) p[q] = (lo + (span * (uint32_t)(q + 1)) / 5u) << 16;
-    int c[4];
-    count4(list, R, cnt, p, c);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      if (c[q] >= topk)
-        lo = max(lo, p[q] >> 16);
-      else
-        hi = min(hi, p[q] >> 16);
-    }
-  }
-  const uint32_t pivot = lo << 16;
-  const int w = keep_pass(list, R, cnt, pivot);
-  return Compacted{w, fmaxf(tau, tau_of_bucket(pivot)), w < cnt};
-}
-
-// Threshold of the stream filter in bucket form, both halves of a bf16x2:
-// the bucket of tau (the lowest score of the compaction pivot's bucket), or
-// -inf before the first compaction.  A key passes when its bucket, compared
-// as a bf16 number, reaches this one: every key with score > tau passes
-// (truncation is monotonic), plus the other keys of tau's own bucket.
-__device__ __forceinline__ uint32_t packed_threshold(float tau) {
-  const uint32_t b = (tau != tau) ? 0xff80u : (__float_as_uint(tau) >> 16);
-  return b * 0x00010001u;
-}
-
-// Hit mask of a 32-key chunk: bit i is set when key i's bucket reaches the
-// packed threshold.  Word j of `p` receives the buckets of keys j (low half)
-// and j + 16 (high half); one byte permute, one packed bf16 compare and one
-// logic op cover two keys.
-__device__ __forceinline__ uint32_t hit_mask(const uint32_t (&v)[32], uint32_t tb2, uint32_t (&p)[16]) {
+// Bit i set when key i's truncated score reaches the packed threshold tb2
+// (one bf16 in both halves).  Word j packs the upper halves of keys j and
+// j + 16; one byte permute, one packed compare and one logic op cover two
+// keys.  Truncation is monotonic and tb2 is a bf16 value, so every key whose
+// score reaches the threshold is set (and a few just below it, for negative
+// scores).
+__device__ __forceinline__ uint32_t hit_mask(const uint32_t (&v)[32], uint32_t tb2) {
   uint32_t m[4] = {0u, 0u, 0u, 0u};  // four independent chains, joined at the end
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    p[j] = __byte_perm(v[j], v[j + 16], 0x7632);
+    const uint32_t p = __byte_perm(v[j], v[j + 16], 0x7632);
     uint32_t w;
-    asm("set.ge.u32.bf16x2 %0, %1, %2;" : "=r"(w) : "r"(p[j]), "r"(tb2));
+    asm("set.ge.u32.bf16x2 %0, %1, %2;" : "=r"(w) : "r"(p), "r"(tb2));
     m[j & 3] |= w & (0x00010001u << j);
   }
   return (m[0] | m[1]) | (m[2] | m[3]);
 }
 
-// Append the keys of mask `m` of a chunk to the row's list, branch-free: each
-// key's slot is the running count and the store is a predicated instruction.
-// Used when some row of the warp has many hits in the chunk (early in the
-// stream, before the threshold has risen).
-__device__ __forceinline__ void append_dense(const uint32_t (&v)[32], uint32_t m, uint32_t key0, uint32_t base,
-                                             int& cnt) {
-  uint32_t slot = (uint32_t)cnt;
+// Maxima of the four 8-key groups of a 32-key chunk.
+__device__ __forceinline__ void max8x4(const uint32_t (&v)[32], float (&g)[4]) {
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const uint32_t take = (m >> i) & 1u;
-    st_shared_u32_if(base + slot * (4u * RS), __byte_perm(key0 + (uint32_t)i, v[i], 0x7610), take);
-    slot += take;
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t* x = v + 8 * j;
+    const float a = max3_nan(__uint_as_float(x[0]), __uint_as_float(x[1]), __uint_as_float(x[2]));
+    const float b = max3_nan(__uint_as_float(x[3]), __uint_as_float(x[4]), __uint_as_float(x[5]));
+    g[j] = max3_nan(a, b, max_nan(__uint_as_float(x[6]), __uint_as_float(x[7])));
   }
-  cnt = (int)slot;
 }
 
-// Append the keys of mask `m` one hit at a time.  The chunk's packed buckets
-// are first stored to the row's 64-byte stage (four 16-byte stores, chunk c
-// at position c ^ sw so that eight lanes' stores cover all 32 banks); each
-// hit then reads its bucket back by its bit position.  A lane loops only over
-// its own hits, so a warp pays for its row with the most hits, usually two
-// or three per chunk.
-__device__ __forceinline__ void append_sparse(const uint32_t (&p)[16], uint32_t m, uint32_t key0, uint32_t stage,
-                                              uint32_t sw, uint32_t base, int& cnt) {
-  if (m == 0u) return;
+// Number of packed bf16 values of `words` consecutive group-maximum words
+// (stride TQ*4 bytes from `addr`) that reach the packed threshold p2.
+__device__ __forceinline__ int count_ge(uint32_t addr, int words, uint32_t p2) {
+  int c0 = 0, c1 = 0;
+  int w = 0;
+  for (; w + 4 <= words; w += 4) {
+    uint32_t x[4];
 #pragma unroll
-  for (int c = 0; c < 4; ++c)
-    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(stage + ((16u * c) ^ sw)), "r"(p[4 * c]),
-                 "r"(p[4 * c + 1]), "r"(p[4 * c + 2]), "r"(p[4 * c + 3])
-                 : "memory");
-  // two hits per iteration (most lanes have at most two): both bucket reads
-  // are in flight together
-  uint32_t slot = (uint32_t)cnt;
-  do {
-    const uint32_t b0 = 31u - __clz(m);
-    m ^= 1u << b0;
-    const uint32_t two = m != 0u;
-    const uint32_t b1 = two ? 31u - __clz(m) : b0;
-    m &= ~(two << b1);
-    uint32_t k0b, k1b;
-    asm volatile("ld.shared.u16 %0, [%1];" : "=r"(k0b) : "r"(stage + ((((b0 << 2) & 60u) ^ sw) | ((b0 >> 3) & 2u))) : "memory");
-    asm volatile("ld.shared.u16 %0, [%1];" : "=r"(k1b) : "r"(stage + ((((b1 << 2) & 60u) ^ sw) | ((b1 >> 3) & 2u))) : "memory");
-    asm volatile("st.shared.u32 [%0], %1;" ::"r"(base + slot * (4u * RS)), "r"(__byte_perm(key0 + b0, k0b, 0x5410))
-                 : "memory");
-    st_shared_u32_if(base + (slot + 1u) * (4u * RS), __byte_perm(key0 + b1, k1b, 0x5410), two);
-    slot += 1u + two;
-  } while (m != 0u);
-  cnt = (int)slot;
+    for (int i = 0; i < 4; ++i)
+      asm volatile("ld.shared.u32 %0, [%1];" : "=r"(x[i]) : "r"(addr + (uint32_t)(w + i) * (TQ * 4u)) : "memory");
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t r;
+      asm("set.ge.u32.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(x[i]), "r"(p2));
+      if (i & 1) c1 += __popc(r); else c0 += __popc(r);
+    }
+  }
+  for (; w < words; ++w) {
+    uint32_t x, r;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(x) : "r"(addr + (uint32_t)w * (TQ * 4u)) : "memory");
+    asm("set.ge.u32.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(p2));
+    c0 += __popc(r);
+  }
+  return (c0 + c1) >> 4;  // 16 set bits per passing half
 }
 
-__device__ __forceinline__ float chunk_max(const uint32_t* v) {
-  float a[11];
-#pragma unroll
-  for (int g = 0; g < 10; ++g)
-    a[g] = max3_nan(__uint_as_float(v[3 * g]), __uint_as_float(v[3 * g + 1]), __uint_as_float(v[3 * g + 2]));
-  a[10] = max_nan(__uint_as_float(v[30]), __uint_as_float(v[31]));
-  const float b0 = max3_nan(a[0], a[1], a[2]), b1 = max3_nan(a[3], a[4], a[5]),
-              b2 = max3_nan(a[6], a[7], a[8]);
-  const float b3 = max_nan(a[9], a[10]);
-  return max_nan(max3_nan(b0, b1, b2), b3);
+// Packed pass-2 threshold of one thread's half tile with segment bias b: a
+// bf16 value t such that every raw dot d with fl(fl(d·scale) + b) >= tau
+// has trunc16(d) >= t.  tau = -inf (no bound) admits every key; b = -inf
+// with a finite tau admits none.  The margin covers the two roundings of the
+// final score and the rounding of the quotient.
+__device__ __forceinline__ uint32_t biased_threshold(float tau, float b, float scale) {
+  if (tau == __int_as_float(0xff800000)) return kBf16NegInf * 0x00010001u;
+  if (b == __int_as_float(0xff800000)) return kBf16PosInf * 0x00010001u;
+  const float num = tau - b;
+  const float margin = (fabsf(tau) + fabsf(b)) * 0x1p-16f + 0x1p-120f;
+  const float t = __fdiv_rd(num - margin, scale);
+  if (t != t) return kBf16NegInf * 0x00010001u;
+  return bf16_floor(t) * 0x00010001u;
 }
 
 // ------------------------------------------------------- exact re-scoring ---
@@ -596,13 +399,8 @@ __device__ __noinline__ void reselect_row(RowOut a, int64_t m, int topk, float s
   __syncwarp();
 }
 
-// kPrefilter: skip 32-key chunks in which no row of the warp has a hit.
-// That pays only for small k: with k >= 8, some row of the warp has a hit in
-// nearly every chunk and the test is pure overhead.
-// kBias: each row's scores of a key tile are shifted by the bias of the
-// tile's segment, fma(dot, scale, bias), before the filter (the finish kernel
-// recomputes the exact fl(fl(dot * scale) + bias)).
-template <typename T, bool kPrefilter, bool kBias>
+// kBias: scores shifted per (row, key segment); see TcArgs.
+template <typename T, bool kBias>
 __global__ void __launch_bounds__(NT, 1)
     fused_fwd_tc(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                  TcArgs a) {
@@ -611,24 +409,24 @@ __global__ void __launch_bounds__(NT, 1)
   uint8_t* sm = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
   uint8_t* qs = sm + OFF_Q;
   uint8_t* ks = sm + OFF_K;
-  uint32_t* list = reinterpret_cast<uint32_t*>(sm + OFF_LIST);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* k_empty = bars + 1 + KSTAGES;
-  uint64_t* s_full = bars + 1 + 2 * KSTAGES;  // [tile][buffer]
-  uint64_t* s_empty = s_full + 2 * NTILE;     // [tile][buffer]
+  uint64_t* s_full = bars + 1 + 2 * KSTAGES;  // [buffer]
+  uint64_t* s_empty = s_full + 2;             // [buffer]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + OFF_MISC + 4);
   volatile uint32_t* scan_big = reinterpret_cast<volatile uint32_t*>(sm + OFF_MISC + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int64_t slice, row0;
-  int count;  // rows of this CTA (RS, fewer at a slice's end, 0 for a surplus grouped CTA)
-  locate_tile(a.geo, blockIdx.x, RS, &slice, &row0, &count);
+  int count;  // rows of this CTA (TQ, fewer at a slice's end, 0 for a surplus grouped CTA)
+  locate_tile(a.geo, blockIdx.x, TQ, &slice, &row0, &count);
   if (count <= 0) return;
   const int64_t slice_row0 = slice_row_begin(a.geo, slice);
   const int ntiles = (int)((a.m + TK - 1) / TK);
+  const int jobs = 2 * ntiles;  // both passes
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -636,9 +434,9 @@ __global__ void __launch_bounds__(NT, 1)
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
     }
-    for (int b = 0; b < 2 * NTILE; ++b) {
+    for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&s_empty[b], 4 * kWarp);
+      mbar_init(&s_empty[b], 8 * kWarp);
     }
     *abort_flag = 0;
     mbar_fence_init();
@@ -656,22 +454,22 @@ __global__ void __launch_bounds__(NT, 1)
     if (lane == 0) {
       int issued = 0;
       if (!a.row_index) {  // else warps 2 and 3 gather the query rows
-        mbar_arrive_expect_tx(q_full, NTILE * TILE_BYTES);
-        for (int g = 0; g < NTILE; ++g) tma_load_2d(qs + g * TILE_BYTES, &tmap_q, 0, (int)(row0 + g * TQ), q_full);
+        mbar_arrive_expect_tx(q_full, Q_BYTES);
+        tma_load_2d(qs, &tmap_q, 0, (int)row0, q_full);
       }
-      for (int t = 0; t < ntiles; ++t) {
-        const int s = t % KSTAGES;
-        const uint32_t ph = (uint32_t)(t / KSTAGES) & 1u;
+      for (int j = 0; j < jobs; ++j) {
+        const int s = j % KSTAGES;
+        const uint32_t ph = (uint32_t)(j / KSTAGES) & 1u;
         if (!mbar_wait(&k_empty[s], ph ^ 1u, abort_flag, a.wait_limit_ns)) break;
-        mbar_arrive_expect_tx(&k_full[s], TILE_BYTES);
-        tma_load_2d(ks + s * TILE_BYTES, &tmap_k, 0, (int)(slice * a.m + (int64_t)t * TK), &k_full[s]);
+        mbar_arrive_expect_tx(&k_full[s], K_BYTES);
+        tma_load_2d(ks + s * K_BYTES, &tmap_k, 0, (int)(slice * a.m + (int64_t)(j % ntiles) * TK), &k_full[s]);
         ++issued;
       }
       if (*abort_flag) {
         // let the copies already in flight land before the CTA exits
-        for (int t = (issued > KSTAGES ? issued - KSTAGES : 0); t < issued; ++t) {
+        for (int j = (issued > KSTAGES ? issued - KSTAGES : 0); j < issued; ++j) {
           const uint64_t t0 = global_timer();
-          while (!mbar_try_wait(&k_full[t % KSTAGES], (uint32_t)(t / KSTAGES) & 1u) &&
+          while (!mbar_try_wait(&k_full[j % KSTAGES], (uint32_t)(j / KSTAGES) & 1u) &&
                  global_timer() - t0 < kWaitLimitNs) {
           }
         }
@@ -690,10 +488,9 @@ __global__ void __launch_bounds__(NT, 1)
       const int t = (int)threadIdx.x - 2 * kWarp;
       const T* qrows = static_cast<const T*>(a.q);
       const uint32_t qbase = smem_addr(qs);
-      for (int c = t; c < RS * (D / 8); c += 2 * kWarp) {
+      for (int c = t; c < TQ * (D / 8); c += 2 * kWarp) {
         const int r = c >> 3, ch = c & 7;
-        const uint32_t dst = qbase + (uint32_t)(r / TQ) * TILE_BYTES + (uint32_t)(r % TQ) * (D * 2) +
-                             ((uint32_t)(ch ^ (r & 7)) << 4);
+        const uint32_t dst = qbase + (uint32_t)r * (D * 2) + ((uint32_t)(ch ^ (r & 7)) << 4);
         if (r < count)
           cp_async_16(dst, qrows + (int64_t)a.row_index[row0 + r] * D + ch * 8);
         else
@@ -738,29 +535,21 @@ __global__ void __launch_bounds__(NT, 1)
       uint64_t* last_bar = nullptr;  // barrier of the last commit, for the abort path
       uint32_t last_ph = 0;
       if (mbar_wait(q_full, 0, abort_flag, a.wait_limit_ns)) {
-        for (int t = 0; t < ntiles; ++t) {
-          const int s = t % KSTAGES, b = t & 1;
-          const uint32_t ph_s = ((uint32_t)(t >> 1) & 1u);
-          if (!mbar_wait(&k_full[s], (uint32_t)(t / KSTAGES) & 1u, abort_flag, a.wait_limit_ns)) break;
-          const uint32_t k_addr = smem_addr(ks + s * TILE_BYTES);
-          bool stop = false;
+        for (int j = 0; j < jobs; ++j) {
+          const int s = j % KSTAGES, b = j & 1;
+          const uint32_t ph_b = (uint32_t)(j >> 1) & 1u;
+          if (!mbar_wait(&k_full[s], (uint32_t)(j / KSTAGES) & 1u, abort_flag, a.wait_limit_ns)) break;
+          if (!mbar_wait(&s_empty[b], ph_b ^ 1u, abort_flag, a.wait_limit_ns)) break;
+          tc_fence_after();
+          const uint32_t k_addr = smem_addr(ks + s * K_BYTES);
 #pragma unroll
-          for (int g = 0; g < NTILE; ++g) {
-            if (!mbar_wait(&s_empty[2 * g + b], ph_s ^ 1u, abort_flag, a.wait_limit_ns)) {
-              stop = true;
-              break;
-            }
-            tc_fence_after();
-#pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk)
-              mma_f16(tmem + (uint32_t)((2 * g + b) * TK), smem_desc_k128(q_addr + g * TILE_BYTES + kk * 32),
-                      smem_desc_k128(k_addr + kk * 32), idesc, kk > 0);
-            mma_commit(&s_full[2 * g + b]);
-            last_bar = &s_full[2 * g + b];
-            last_ph = ph_s;
-          }
-          if (stop) break;
+          for (int kk = 0; kk < D / 16; ++kk)
+            mma_f16(tmem + (uint32_t)(b * TK), smem_desc_k128(q_addr + kk * 32), smem_desc_k128(k_addr + kk * 32),
+                    idesc, kk > 0);
+          mma_commit(&s_full[b]);
           mma_commit(&k_empty[s]);
+          last_bar = &s_full[b];
+          last_ph = ph_b;
         }
       }
       if (*abort_flag && last_bar) {
@@ -771,117 +560,198 @@ __global__ void __launch_bounds__(NT, 1)
       }
     }
   } else if (warp >= 4) {
-    const int wg = (warp - 4) >> 2, quarter = warp & 3;
-    const int rl = quarter * kWarp + lane;  // row within the query tile == TMEM lane
-    const int R = wg * TQ + rl;              // list column
-    const int tile_left = count - wg * TQ;
-    const int rows = tile_left < 0 ? 0 : (tile_left < TQ ? tile_left : TQ);
-    const uint32_t tm = tmem + ((uint32_t)(quarter * kWarp) << 16) + (uint32_t)(2 * wg * TK);
-    uint64_t* my_full = s_full + 2 * wg;
-    uint64_t* my_empty = s_empty + 2 * wg;
-    const uint32_t lbase = smem_addr(list) + 4u * R;
-    const uint32_t sbase = smem_addr(sm + OFF_STAGE) + 64u * R;
-    const uint32_t sw = ((uint32_t)(R >> 1) & 3u) << 4;
-    float tau = __int_as_float(0x7fc00000);  // "no threshold yet"
-    uint32_t tb2 = packed_threshold(tau);
-    int cnt = 0;
-    bool dead = false;  // list could not be shrunk: exact re-selection at the end
+    const int h = (warp - 4) >> 2, quarter = warp & 3;
+    const int rl = quarter * kWarp + lane;  // row within the CTA == TMEM lane
+    const bool live = rl < count;
+    const int64_t gr = row0 + rl;
+    const uint32_t tm = tmem + ((uint32_t)(quarter * kWarp) << 16) + (uint32_t)(h * HALF);
+    const uint32_t pair_bar = 2u + (uint32_t)quarter;  // the two warps of this lane quarter
+    // group maxima: value v of this thread at word v/2, half v%2 of column rl
+    const uint32_t gm_base = smem_addr(sm + OFF_GM) + (uint32_t)(h * NGW * TQ + rl) * 4u;
+    uint32_t* xch = reinterpret_cast<uint32_t*>(sm + OFF_XCH);
+    const int gsh = a.glog - 5;  // a group is 2^gsh chunks of 32 keys of this thread
+    const float neg_inf_f = __int_as_float(0xff800000);
     bool ok = true;
-    for (int t = 0; t < ntiles; ++t) {
-      const int b = t & 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(&my_full[b], (uint32_t)(t >> 1) & 1u, abort_flag, a.wait_limit_ns));
-      if (!ok) break;
+
+    // Two 32-column chunks at a time: both TMEM loads, one wait, then the
+    // two chunks' independent work interleaves.  The TMEM buffer is released
+    // once the tile's last pair is in registers.  Half tiles past the last
+    // key (only the last tile of a slice) take the masked variant.
+    auto stream_tile = [&](int j, auto&& pair) -> bool {
+      const int b = j & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (uint32_t)(j >> 1) & 1u, abort_flag, a.wait_limit_ns)))
+        return false;
       tc_fence_after();
-      const int64_t key_tile = (int64_t)t * TK;
-      const int tile_valid = (int)((a.m - key_tile) < TK ? (a.m - key_tile) : TK);
-      float tile_bias = 0.f;
-      if (kBias && rl < rows)
-        tile_bias = __ldg(a.seg_bias + (row0 + wg * TQ + rl) * a.segs + key_tile / a.seg_len);
-      // One 32-column chunk at a time; the TMEM load of the next chunk is in
-      // flight while the current one is filtered.  The loop body holds two
-      // chunk steps (two register buffers) so that the hot path stays small
-      // enough for the instruction cache.  The TMEM buffer is released once
-      // its last chunk is in registers.
-      auto chunk_step = [&](uint32_t(&v)[32], int c) {
-        const int valid = tile_valid - c * 32;
-        if (kBias) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(fmaf(__uint_as_float(v[i]), a.scale, tile_bias));
-        }
-        if (kPrefilter) {
-          float mx;
-          if (valid >= 32) {
-            mx = chunk_max(v);
-          } else {
-            mx = __int_as_float(0xff800000);
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (i < valid) mx = max_nan(mx, __uint_as_float(v[i]));
-          }
-          if (!__any_sync(0xffffffffu, !(mx <= tau))) return;
-        }
-        uint32_t p[16];
-        uint32_t m = hit_mask(v, tb2, p);
-        if (dead) m = 0u;
-        if (valid < 32) m &= valid > 0 ? (1u << valid) - 1u : 0u;
-        const uint32_t key0 = (uint32_t)(key_tile + c * 32);
-        if (__any_sync(0xffffffffu, __popc(m) > kDenseHits))
-          append_dense(v, m, key0, lbase, cnt);
-        else
-          append_sparse(p, m, key0, sbase, sw, lbase, cnt);
-        // When one lane's list could overflow, every lane holding well over
-        // k keys compacts in the same pass: under SIMT the warp pays for the
-        // longest list either way.
-        if (__any_sync(0xffffffffu, !dead && cnt > CAP - 32)) {
-          // The next chunk's TMEM load may still be writing its registers:
-          // complete it before calling out of line.
-          tmem_wait_load();
-          if (!dead && cnt > a.topk + 16) {
-            Compacted r = compact_bucket(list, R, cnt, tau, a.topk, 2);
-            if (r.cnt > CAP - 32) r = compact_bucket_exact(list, R, r.cnt, r.tau, a.topk);
-            cnt = r.cnt;
-            tau = r.tau;
-            tb2 = packed_threshold(tau);
-            dead = cnt > CAP - 32;
-          }
-        }
-      };
-      uint32_t va[32], vb[32];
-      tmem_load_32cols(tm + b * TK, va);
-      tmem_wait_load(va);
+      const int t = j % ntiles;
+      const int64_t key_half = (int64_t)t * TK + h * HALF;
+      const int half_valid = (int)(a.m - key_half < HALF ? (a.m - key_half > 0 ? a.m - key_half : 0) : HALF);
 #pragma unroll 1
-      for (int cp = 0; cp < TK / 64; ++cp) {
-        const int c0 = 2 * cp;
-        tmem_load_32cols(tm + b * TK + (c0 + 1) * 32, vb);
-        chunk_step(va, c0);
-        tmem_wait_load(vb);
-        const bool last = cp == TK / 64 - 1;
-        if (!last) {
-          tmem_load_32cols(tm + b * TK + (c0 + 2) * 32, va);
-        } else {
+      for (int cp = 0; cp < HALF / 64; ++cp) {
+        uint32_t va[32], vb[32];
+        tmem_load_32cols(tm + b * TK + (2 * cp) * 32, va);
+        tmem_load_32cols(tm + b * TK + (2 * cp + 1) * 32, vb);
+        tmem_wait_load(va);
+        reg_fence(vb);
+        if (cp == HALF / 64 - 1) {
           tc_fence_before();
-          mbar_arrive(&my_empty[b]);
+          mbar_arrive(&s_empty[b]);
         }
-        chunk_step(vb, c0 + 1);
-        if (!last) tmem_wait_load(va);
+        if (half_valid >= HALF)
+          pair(va, vb, key_half + cp * 64, 64, std::true_type{});
+        else
+          pair(va, vb, key_half + cp * 64, half_valid - cp * 64, std::false_type{});
+      }
+      return true;
+    };
+
+    // ---- pass 1: group maxima (value v at word v/2, half v%2), rounded
+    // down to bf16; the finite values' range and count are kept for the tau
+    // search.
+    int nv = 0;             // values written
+    int pc = 0;             // pairs seen
+    float run = neg_inf_f;  // running maximum of a group spanning pairs
+    float lo_f = __int_as_float(0x7f800000), hi_f = neg_inf_f;
+    int nfin = 0;
+    auto track = [&](float x) {
+      const bool fin = x > neg_inf_f;  // NaN only in rows re-selected later
+      hi_f = fmaxf(hi_f, x);
+      lo_f = fminf(lo_f, fin ? x : __int_as_float(0x7f800000));
+      nfin += fin ? 1 : 0;
+    };
+    float bias1 = 0.f;
+    for (int j = 0; j < ntiles && ok; ++j) {
+      if (kBias && live) {
+        const int64_t key_half = (int64_t)j * TK + h * HALF;
+        bias1 = key_half < a.m ? __ldg(a.seg_bias + gr * a.segs + key_half / a.seg_len) : 0.f;
+      }
+      ok = stream_tile(j, [&](uint32_t(&va)[32], uint32_t(&vb)[32], int64_t, int valid, auto whole) {
+        if constexpr (!decltype(whole)::value) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if (i >= valid) va[i] = 0xff800000u;
+            if (i + 32 >= valid) vb[i] = 0xff800000u;
+          }
+        }
+        float ga[4], gb[4];
+        max8x4(va, ga);
+        max8x4(vb, gb);
+        float xa = max_nan(max3_nan(ga[0], ga[1], ga[2]), ga[3]);
+        float xb = max_nan(max3_nan(gb[0], gb[1], gb[2]), gb[3]);
+        if (kBias) {
+          xa = __fadd_rn(__fmul_rn(xa, a.scale), bias1);
+          xb = __fadd_rn(__fmul_rn(xb, a.scale), bias1);
+        }
+        if (gsh == 0) {  // one value per chunk: both in one word
+          asm volatile("st.shared.u32 [%0], %1;" ::"r"(gm_base + (uint32_t)pc * (TQ * 4u)),
+                       "r"(bf16_floor(xa) | (bf16_floor(xb) << 16))
+                       : "memory");
+          track(xa);
+          track(xb);
+          nv += 2;
+        } else {
+          run = max3_nan(run, xa, xb);
+          if (((pc + 1) & ((1 << (gsh - 1)) - 1)) == 0) {
+            asm volatile("st.shared.u16 [%0], %1;"
+                         ::"r"(gm_base + (uint32_t)(nv >> 1) * (TQ * 4u) + (uint32_t)(nv & 1) * 2u),
+                         "h"((unsigned short)bf16_floor(run))
+                         : "memory");
+            track(run);
+            ++nv;
+            run = neg_inf_f;
+          }
+        }
+        ++pc;
+      });
+    }
+    if (gsh >= 2 && (pc & ((1 << (gsh - 1)) - 1)) != 0) {  // a group cut short by the last tile
+      asm volatile("st.shared.u16 [%0], %1;"
+                   ::"r"(gm_base + (uint32_t)(nv >> 1) * (TQ * 4u) + (uint32_t)(nv & 1) * 2u),
+                   "h"((unsigned short)bf16_floor(run))
+                   : "memory");
+      track(run);
+      ++nv;
+    }
+    if (nv & 1) {  // pad the last word's upper half
+      asm volatile("st.shared.u16 [%0], %1;" ::"r"(gm_base + (uint32_t)(nv >> 1) * (TQ * 4u) + 2u),
+                   "h"((unsigned short)kBf16NegInf)
+                   : "memory");
+    }
+    uint32_t lo = nfin ? bf16_ord(bf16_floor(lo_f)) : 0xffffu;
+    uint32_t hi = nfin ? bf16_ord(bf16_floor(hi_f)) : 0u;
+    const int words = (nv + 1) >> 1;
+
+    // ---- tau: the k-th largest group maximum of the row (both threads'
+    // values), by bisection over ordered bf16 codes; L always satisfies
+    // count(>= L) >= k, H is the lowest code known to fail.  Both threads
+    // of a row compute the same L and H, so the two warps of a lane quarter
+    // meet the same number of barriers.
+    xch[(0 * 2 + h) * TQ + rl] = (lo & 0xffffu) | (hi << 16);
+    xch[(1 * 2 + h) * TQ + rl] = (uint32_t)nfin;
+    named_bar_sync(pair_bar, 2 * kWarp);
+    {
+      const uint32_t pr = xch[(0 * 2 + (1 - h)) * TQ + rl];
+      lo = min(lo, pr & 0xffffu);
+      hi = max(hi, pr >> 16);
+      nfin += (int)xch[(1 * 2 + (1 - h)) * TQ + rl];
+    }
+    uint32_t L = lo, H = hi + 1u;
+    const bool bounded = nfin >= a.topk;  // else: no bound, every key is a candidate
+    if (!bounded) {
+      L = 0u;
+      H = 1u;
+    }
+    while (__any_sync(0xffffffffu, H - L > 1u)) {
+      const bool act = H - L > 1u;
+      const uint32_t mid = (L + H) >> 1;
+      const uint32_t p2 = bf16_of_ord(mid) * 0x00010001u;
+      const int mine = act ? count_ge(gm_base, words, p2) : 0;
+      named_bar_sync(pair_bar, 2 * kWarp);  // the partner has read the previous exchange
+      xch[h * TQ + rl] = (uint32_t)mine;
+      named_bar_sync(pair_bar, 2 * kWarp);
+      const int c = mine + (int)xch[(1 - h) * TQ + rl];
+      if (act) {
+        if (c >= a.topk) L = mid; else H = mid;
       }
     }
-    // Hand the row to the finish kernel: its entry count (or kCandDead) and
-    // the entries, four per 16-byte store (slots past the count are unused).
-    if (rl < rows) {
-      const int64_t gr = row0 + (int64_t)wg * TQ + rl;
-      if (!ok) {
-        a.cand_n[gr] = kCandAborted;
-      } else if (dead) {
-        a.cand_n[gr] = kCandDead;
-      } else {
-        uint4* dst = reinterpret_cast<uint4*>(a.cand + gr * CAP);
-        for (int s = 0; s < cnt; s += 4)
-          dst[s >> 2] = make_uint4(list[s * RS + R], list[(s + 1) * RS + R], list[(s + 2) * RS + R],
-                                   list[(s + 3) * RS + R]);
-        a.cand_n[gr] = cnt;
+    const uint32_t tau_b = bounded ? bf16_of_ord(L) : kBf16NegInf;
+    const float tau = __uint_as_float(tau_b << 16);
+
+    // ---- pass 2: candidate keys, into this thread's half of the row's list
+    const uint32_t tb2_plain = tau_b * 0x00010001u;
+    uint16_t* crow = a.cand + gr * CAP + h * CAPH;
+    uint32_t cnt = 0;
+    for (int j = ntiles; j < jobs && ok; ++j) {
+      uint32_t tb2 = tb2_plain;
+      if (kBias && live) {
+        const int64_t key_half = (int64_t)(j - ntiles) * TK + h * HALF;
+        const float bias2 = key_half < a.m ? __ldg(a.seg_bias + gr * a.segs + key_half / a.seg_len) : 0.f;
+        tb2 = biased_threshold(tau, bias2, a.scale);
       }
+      ok = stream_tile(j, [&](uint32_t(&va)[32], uint32_t(&vb)[32], int64_t key0, int valid, auto whole) {
+        uint32_t ma = hit_mask(va, tb2), mb = hit_mask(vb, tb2);
+        if constexpr (!decltype(whole)::value) {
+          ma &= valid >= 32 ? 0xffffffffu : (valid > 0 ? (1u << valid) - 1u : 0u);
+          mb &= valid >= 64 ? 0xffffffffu : (valid > 32 ? (1u << (valid - 32)) - 1u : 0u);
+        }
+        if (!live) ma = mb = 0u;
+        // one hit of each lane per round, a warp-uniform number of rounds
+        const uint32_t rounds = __reduce_max_sync(0xffffffffu, (uint32_t)(__popc(ma) + __popc(mb)));
+        for (uint32_t rd = 0; rd < rounds; ++rd) {
+          const bool in_a = ma != 0u;
+          const uint32_t m = in_a ? ma : mb;
+          const bool hit = m != 0u;
+          const uint32_t i = hit ? 31u - __clz(m) : 0u;
+          const uint32_t bit = hit ? 1u << i : 0u;
+          if (in_a) ma ^= bit; else mb ^= bit;
+          if (hit && cnt < (uint32_t)CAPH) crow[cnt] = (uint16_t)((uint32_t)key0 + (in_a ? 0u : 32u) + i);
+          cnt += hit ? 1u : 0u;
+        }
+      });
     }
+    // Hand this half of the row to the finish kernel: its count (more than
+    // CAPH: overflowed) or kCandAborted.
+    named_bar_sync(pair_bar, 2 * kWarp);
+    if (live) a.cand_n[2 * gr + h] = *abort_flag ? kCandAborted : (int32_t)cnt;
   }
 
   __syncthreads();
@@ -895,11 +765,11 @@ __global__ void __launch_bounds__(NT, 1)
 
 // ------------------------------------------------------------ finish ---
 // One warp per query row (see the file comment).  Each warp keeps its row's
-// survivors (key, exact score) and a 256-bin histogram in shared memory; the
-// exact re-selection of marked rows reuses the survivor arrays.
-constexpr int FW = 8;                      // warps per finish block
-constexpr int NV = (CAP + kWarp - 1) / kWarp;  // list entries per lane
-constexpr int FUNR = 4;                    // survivors in flight per lane group
+// candidates (key, exact score) in shared memory; the exact re-selection of
+// a row whose list overflowed reuses the same arrays.
+constexpr int FW = 8;             // warps per finish block
+constexpr int FUNR = 4;           // key or value rows in flight per lane group
+constexpr int NV = CAP / kWarp;   // candidates per lane
 
 struct FinArgs {
   const void* q;
@@ -909,7 +779,7 @@ struct FinArgs {
   int32_t* top_idx;
   float* lse;
   float* top_scores;
-  const uint32_t* cand;
+  const uint16_t* cand;
   const int32_t* cand_n;
   const uint32_t* unsafe;  // at each slice's first row, from the stream kernel's key check
   const int32_t* row_index;  // nullable: logical row -> query/output row
@@ -924,80 +794,12 @@ struct FinArgs {
 };
 
 struct __align__(16) FinWarp {
-  float sc[CAP];  // survivors' exact scores, then the selection's
+  float sc[CAP];  // candidates' exact scores, then the selection's (list order)
   int si[CAP];    // their key indices
-  int hist[256];
+  float pw[64];   // softmax weight of each selection
+  float pad[4];
 };
-static_assert(sizeof(float) * CAP + sizeof(int) * CAP >= FIX_CAP * 8 + 16, "re-selection buffers exceed sc/si");
-
-// The need-th largest (1 <= need <= count) of the warp's values whose `ok`
-// is set, by 8-bit digits starting at the highest bit in which those values
-// differ, one 256-bin shared-memory histogram per digit.  Only the first
-// `nv` slots of each lane (warp-uniform) may be set.  *above receives how
-// many values are strictly larger.
-__device__ __forceinline__ uint32_t warp_kth_largest(const uint32_t (&v)[NV], const bool (&ok)[NV], int nv,
-                                                     int need, int* hist, int lane, int* above) {
-  uint32_t lo = 0xffffffffu, hi = 0u;
-#pragma unroll
-  for (int i = 0; i < NV; ++i)
-    if (i < nv && ok[i]) {
-      lo = min(lo, v[i]);
-      hi = max(hi, v[i]);
-    }
-  lo = __reduce_min_sync(0xffffffffu, lo);
-  hi = __reduce_max_sync(0xffffffffu, hi);
-  int gt = 0;
-  uint32_t prefix = lo;
-  if (hi != lo) {
-    const int top = 31 - __clz(hi ^ lo);
-    prefix = lo & ~(uint32_t)((2ull << top) - 1ull);  // the bits above `top`, common to all
-    for (int lowbit = top - 7;; lowbit -= 8) {
-      const int sh = lowbit < 0 ? 0 : lowbit;
-      const uint32_t dmask = (1u << (lowbit + 8 - sh)) - 1u;
-      reinterpret_cast<int4*>(hist)[2 * lane] = make_int4(0, 0, 0, 0);
-      reinterpret_cast<int4*>(hist)[2 * lane + 1] = make_int4(0, 0, 0, 0);
-      __syncwarp();
-#pragma unroll
-      for (int i = 0; i < NV; ++i)
-        if (i < nv && ok[i] && ((uint64_t)(v[i] ^ prefix) >> (lowbit + 8)) == 0)
-          atomicAdd(&hist[(v[i] >> sh) & dmask], 1);
-      __syncwarp();
-      // lane L holds bins 255-8L down to 248-8L
-      const int4 h0 = reinterpret_cast<const int4*>(hist)[62 - 2 * lane];
-      const int4 h1 = reinterpret_cast<const int4*>(hist)[63 - 2 * lane];
-      const int c[8] = {h1.w, h1.z, h1.y, h1.x, h0.w, h0.z, h0.y, h0.x};
-      int tot = 0;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) tot += c[i];
-      int incl = tot;
-#pragma unroll
-      for (int o = 1; o < kWarp; o <<= 1) {
-        const int t = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += t;
-      }
-      const int excl = incl - tot;
-      const int src = __ffs(__ballot_sync(0xffffffffu, excl < need && need <= incl)) - 1;
-      int dig = -1, before = 0, run = excl;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        if (dig < 0 && run + c[i] >= need) {
-          dig = 255 - 8 * lane - i;
-          before = run;
-        }
-        run += c[i];
-      }
-      dig = __shfl_sync(0xffffffffu, dig, src);
-      before = __shfl_sync(0xffffffffu, before, src);
-      prefix |= (uint32_t)dig << sh;
-      need -= before;
-      gt += before;
-      __syncwarp();
-      if (lowbit <= 0) break;
-    }
-  }
-  *above = gt;
-  return prefix;
-}
+static_assert(sizeof(float) * CAP + sizeof(int) * CAP >= FIX_CAP * 8, "re-selection buffers exceed sc/si");
 
 template <typename T>
 __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
@@ -1007,8 +809,8 @@ __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
   const unsigned lt = (1u << lane) - 1u;
   FinWarp& w = sw[warp];
   for (int64_t r = (int64_t)blockIdx.x * FW + warp; r < a.rows; r += (int64_t)gridDim.x * FW) {
-    const int cnt = a.cand_n[r];
-    if (cnt == kCandAborted) {
+    const int c0 = a.cand_n[2 * r], c1 = a.cand_n[2 * r + 1];
+    if (c0 == kCandAborted || c1 == kCandAborted) {
       // the stream kernel gave up on this row (a bounded wait ran out, device
       // status bit 2): defined outputs that no caller can mistake for a
       // result — NaN output and LSE, index -1 (the backward skips it)
@@ -1022,6 +824,7 @@ __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
       if (lane == 0) a.lse[r] = __int_as_float(0x7fc00000);
       continue;
     }
+    const int cnt = c0 + c1;
     const int64_t slice = slice_of_row(a.geo, r);
     const int64_t pr = a.row_index ? (int64_t)a.row_index[r] : r;  // query and output row
     const uint4 qg = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(a.q) + pr * D) + g);
@@ -1030,162 +833,107 @@ __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
                                                  big_halves(qg.z, add) | big_halves(qg.w, add)) != 0u) ||
                         a.unsafe[slice_row_begin(a.geo, slice)] != 0u;
     const float* brow = a.seg_bias ? a.seg_bias + r * a.segs : nullptr;
-    bool bias_nan = false;  // a NaN bias makes NaN scores, which the stream filter does not rank
+    bool bias_bad = false;  // NaN or +inf biases are ranked by the exact path only
     if (brow)
-      for (int j = lane; j < a.segs; j += kWarp) bias_nan |= brow[j] != brow[j];
-    if (cnt < 0 || unsafe || __any_sync(0xffffffffu, bias_nan)) {
+      for (int j = lane; j < a.segs; j += kWarp) bias_bad |= !(brow[j] < __int_as_float(0x7f800000));
+    if (c0 < 0 || c1 < 0 || c0 > CAPH || c1 > CAPH || cnt < a.topk || unsafe ||
+        __any_sync(0xffffffffu, bias_bad)) {
       uint8_t* fix = reinterpret_cast<uint8_t*>(&w);
       reselect_row<T>(RowOut{a.q, a.k, a.v, a.out, a.top_idx, a.lse, a.top_scores}, a.m, a.topk, a.scale, slice, r, pr,
-                      brow, a.seg_len,
-                      reinterpret_cast<float*>(fix), reinterpret_cast<int*>(fix + FIX_CAP * 4),
-                      reinterpret_cast<float*>(fix + FIX_CAP * 8), lane);
+                      brow, a.seg_len, reinterpret_cast<float*>(fix), reinterpret_cast<int*>(fix + FIX_CAP * 4),
+                      w.pad, lane);
       continue;
     }
-    // bucket cut: keep the entries whose bucket reaches the k-th largest
-    const int nv = (cnt + kWarp - 1) / kWarp;
-    uint32_t e[NV], o[NV];
-    bool ok[NV];
-    const uint32_t* crow = a.cand + r * CAP;
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int s = lane + kWarp * i;
-      ok[i] = false;
-      e[i] = 0u;
-      if (i < nv) {
-        ok[i] = s < cnt;
-        e[i] = ok[i] ? crow[s] : 0u;
-      }
-      o[i] = ord_entry(e[i]) >> 16;
-    }
-    int above = 0;
-    const uint32_t tb = cnt > a.topk ? warp_kth_largest(o, ok, nv, a.topk, w.hist, lane, &above) : 0u;
-    int S = 0;
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      if (i < nv) {
-        const bool keep = ok[i] && o[i] >= tb;
-        const unsigned b = __ballot_sync(0xffffffffu, keep);
-        if (keep) w.si[S + __popc(b & lt)] = (int)(e[i] & 0xffffu);
-        S += __popc(b);
-      }
-    }
+    // the candidates of both selection threads, in list order
+    const uint16_t* crow = a.cand + r * CAP;
+    for (int s = lane; s < cnt; s += kWarp) w.si[s] = (int)crow[s < c0 ? s : CAPH + (s - c0)];
     __syncwarp();
-    // exact scores: group grp re-scores survivors grp, grp + 4, ...
+    // exact scores: group grp re-scores candidates grp, grp + 4, ... from the
+    // gathered key rows (eight lanes per 128-byte row, one fixed summation order)
     const T* kbase = static_cast<const T*>(a.k) + slice * a.m * D;
-    for (int s0 = 0; s0 < S; s0 += 4 * FUNR) {
+    for (int s0 = 0; s0 < cnt; s0 += 4 * FUNR) {
       uint4 kc[FUNR];
 #pragma unroll
       for (int u = 0; u < FUNR; ++u) {
         const int s = s0 + 4 * u + grp;
         kc[u] = make_uint4(0u, 0u, 0u, 0u);
-        if (s < S) kc[u] = __ldg(reinterpret_cast<const uint4*>(kbase + (int64_t)w.si[s] * D) + g);
+        if (s < cnt) kc[u] = __ldg(reinterpret_cast<const uint4*>(kbase + (int64_t)w.si[s] * D) + g);
       }
 #pragma unroll
       for (int u = 0; u < FUNR; ++u) {
         const int s = s0 + 4 * u + grp;
         const float d = group_dot<T>(qg, kc[u]);
-        if (g == 0 && s < S)
-          w.sc[s] = brow ? __fadd_rn(__fmul_rn(d, a.scale), brow[w.si[s] / a.seg_len]) : d;
+        if (g == 0 && s < cnt) w.sc[s] = brow ? __fadd_rn(__fmul_rn(d, a.scale), brow[w.si[s] / a.seg_len]) : d;
       }
     }
     __syncwarp();
-    // exact cut to k: larger score first, lower key index on equal scores
-    int sel = S;
-    if (S > a.topk) {
-      const int sv = (S + kWarp - 1) / kWarp;
-      bool hk[NV];
-      float xs[NV];
-      int ks[NV];
-      uint64_t rk[NV];
+    float xs[NV];
+    int ks[NV];
+    uint64_t rk[NV];
+    bool hk[NV];
 #pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        const int s = lane + kWarp * i;
-        hk[i] = i < sv && s < S;
-        xs[i] = hk[i] ? w.sc[s] : 0.f;
-        ks[i] = hk[i] ? w.si[s] : 0;
-        rk[i] = hk[i] ? rank_key(xs[i], (uint32_t)ks[i]) : ~0ull;
-      }
-      if (S - a.topk <= 8) {
-        // few extra: drop the lowest-ranked one at a time (rank keys are
-        // distinct, so each round removes exactly one)
-        for (int d = S - a.topk; d > 0; --d) {
-          uint64_t mn = ~0ull;
-#pragma unroll
-          for (int i = 0; i < NV; ++i)
-            if (i < sv) mn = rk[i] < mn ? rk[i] : mn;
-          const uint32_t mh = __reduce_min_sync(0xffffffffu, (uint32_t)(mn >> 32));
-          const uint32_t ml = __reduce_min_sync(0xffffffffu, (uint32_t)(mn >> 32) == mh ? (uint32_t)mn : 0xffffffffu);
-          const uint64_t low = ((uint64_t)mh << 32) | ml;
-#pragma unroll
-          for (int i = 0; i < NV; ++i)
-            if (i < sv && rk[i] == low) {
-              rk[i] = ~0ull;
-              hk[i] = false;
-            }
-        }
-      } else {
-        uint32_t hv[NV], lv[NV];
-        bool lk[NV];
-#pragma unroll
-        for (int i = 0; i < NV; ++i) hv[i] = (uint32_t)(rk[i] >> 32);
-        int gt = 0;
-        const uint32_t ts = warp_kth_largest(hv, hk, sv, a.topk, w.hist, lane, &gt);
-        const int need = a.topk - gt;
-        int eq = 0;
-#pragma unroll
-        for (int i = 0; i < NV; ++i) {
-          lk[i] = hk[i] && hv[i] == ts;
-          lv[i] = (uint32_t)rk[i];
-          if (i < sv) eq += __popc(__ballot_sync(0xffffffffu, lk[i]));
-        }
-        uint32_t tl = 0u;  // the kept ties are those whose low word reaches tl
-        if (eq > need) {
-          int unused = 0;
-          tl = warp_kth_largest(lv, lk, sv, need, w.hist, lane, &unused);
-        }
-#pragma unroll
-        for (int i = 0; i < NV; ++i) hk[i] = hk[i] && (hv[i] > ts || (lk[i] && lv[i] >= tl));
-      }
-      __syncwarp();
-      int pos = 0;
-#pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        if (i < sv) {
-          const unsigned b = __ballot_sync(0xffffffffu, hk[i]);
-          if (hk[i]) {
-            const int p = pos + __popc(b & lt);
-            w.sc[p] = xs[i];
-            w.si[p] = ks[i];
-          }
-          pos += __popc(b);
-        }
-      }
-      __syncwarp();
-      sel = pos;
+    for (int i = 0; i < NV; ++i) {
+      const int s = lane + kWarp * i;
+      hk[i] = s < cnt;
+      xs[i] = hk[i] ? w.sc[s] : 0.f;
+      ks[i] = hk[i] ? w.si[s] : 0;
+      rk[i] = hk[i] ? rank_key(xs[i], (uint32_t)ks[i]) : ~0ull;
     }
+    __syncwarp();
+    // exact cut to k (larger score first, lower key index on ties): drop the
+    // lowest-ranked candidate until k remain (rank keys are distinct, so
+    // each round removes exactly one)
+    for (int dn = cnt - a.topk; dn > 0; --dn) {
+      uint64_t mn = ~0ull;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) mn = rk[i] < mn ? rk[i] : mn;
+      const uint32_t mh = __reduce_min_sync(0xffffffffu, (uint32_t)(mn >> 32));
+      const uint32_t ml = __reduce_min_sync(0xffffffffu, (uint32_t)(mn >> 32) == mh ? (uint32_t)mn : 0xffffffffu);
+      const uint64_t low = ((uint64_t)mh << 32) | ml;
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+        if (rk[i] == low) {
+          rk[i] = ~0ull;
+          hk[i] = false;
+        }
+    }
+    // compact the k kept, in list order
+    int pos = 0;
+    float mx = __int_as_float(0xff800000);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const unsigned bal = __ballot_sync(0xffffffffu, hk[i]);
+      if (hk[i]) {
+        const int p = pos + __popc(bal & lt);
+        w.sc[p] = xs[i];
+        w.si[p] = ks[i];
+        mx = fmaxf(mx, xs[i]);
+      }
+      pos += __popc(bal);
+    }
+    __syncwarp();
+    const int sel = pos;
+#pragma unroll
+    for (int o2 = 16; o2 > 0; o2 >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o2));
     // LSE; lane j holds selections j and j + 32 (k <= 64).  Biased scores are final.
     const float sc_mul = brow ? 1.f : a.scale;
     const bool v0 = lane < sel, v1 = lane + kWarp < sel;
     const float x0 = v0 ? w.sc[lane] : 0.f, x1 = v1 ? w.sc[lane + kWarp] : 0.f;
     const int k0 = v0 ? w.si[lane] : 0, k1 = v1 ? w.si[lane + kWarp] : 0;
-    float mx = fmaxf(v0 ? x0 : __int_as_float(0xff800000), v1 ? x1 : __int_as_float(0xff800000));
-#pragma unroll
-    for (int o2 = 16; o2 > 0; o2 >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o2));
     const float mxs = finite_or_zero(mx * sc_mul);
     float part = (v0 ? expf(x0 * sc_mul - mxs) : 0.f) + (v1 ? expf(x1 * sc_mul - mxs) : 0.f);
 #pragma unroll
     for (int o2 = 16; o2 > 0; o2 >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o2);
     const float lse = mxs + logf(part);
     if (lane == 0) a.lse[r] = lse;
-    float* pw = reinterpret_cast<float*>(w.hist);  // softmax weight of each selection
     int32_t* idx_row = a.top_idx + r * a.topk;
     if (v0) {
-      pw[lane] = expf(x0 * sc_mul - lse);
+      w.pw[lane] = expf(x0 * sc_mul - lse);
       idx_row[lane] = k0;
       if (a.top_scores) a.top_scores[r * a.topk + lane] = x0 * sc_mul;
     }
     if (v1) {
-      pw[lane + kWarp] = expf(x1 * sc_mul - lse);
+      w.pw[lane + kWarp] = expf(x1 * sc_mul - lse);
       idx_row[lane + kWarp] = k1;
       if (a.top_scores) a.top_scores[r * a.topk + lane + kWarp] = x1 * sc_mul;
     }
@@ -1203,7 +951,7 @@ __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
         vc[u] = make_uint4(0u, 0u, 0u, 0u);
         pj[u] = 0.f;
         if (j < sel) {
-          pj[u] = pw[j];
+          pj[u] = w.pw[j];
           vc[u] = __ldg(reinterpret_cast<const uint4*>(vbase + (int64_t)w.si[j] * D) + g);
         }
       }
@@ -1212,19 +960,19 @@ __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
         float f[8];
         unpack8<T>(vc[u], f);
 #pragma unroll
-        for (int h = 0; h < 8; ++h) acc[h] = fmaf(pj[u], f[h], acc[h]);
+        for (int hh = 0; hh < 8; ++hh) acc[hh] = fmaf(pj[u], f[hh], acc[hh]);
       }
     }
 #pragma unroll
-    for (int h = 0; h < 8; ++h) {
-      acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 8);
-      acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 16);
+    for (int hh = 0; hh < 8; ++hh) {
+      acc[hh] += __shfl_xor_sync(0xffffffffu, acc[hh], 8);
+      acc[hh] += __shfl_xor_sync(0xffffffffu, acc[hh], 16);
     }
     if (lane < 8) {
       uint4 u;
       T* ev = reinterpret_cast<T*>(&u);
 #pragma unroll
-      for (int h = 0; h < 8; ++h) ev[h] = from_acc<T>(acc[h]);
+      for (int hh = 0; hh < 8; ++hh) ev[hh] = from_acc<T>(acc[hh]);
       reinterpret_cast<uint4*>(static_cast<T*>(a.out) + pr * D)[g] = u;
     }
     __syncwarp();
@@ -1252,13 +1000,13 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// Row-major [rows, 64] 16-bit matrix, 128-row boxes, 128-byte swizzle.
-bool make_rows_map(CUtensorMap* map, const void* base, int64_t rows, bool bf16) {
+// Row-major [rows, 64] 16-bit matrix, boxes of `box_rows` rows, 128-byte swizzle.
+bool make_rows_map(CUtensorMap* map, const void* base, int64_t rows, bool bf16, int box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)D * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)D, (cuuint32_t)TQ};
+  const cuuint32_t box[2] = {(cuuint32_t)D, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   return fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
             const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -1268,6 +1016,18 @@ bool make_rows_map(CUtensorMap* map, const void* base, int64_t rows, bool bf16) 
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// log2 of the keys per group maximum: the smallest group (32 .. 256 keys)
+// that leaves each selection thread at most 2·NGW values.
+int group_log(int64_t m) {
+  const int64_t chunks = ((m + TK - 1) / TK) * (HALF / 32);  // 32-key chunks per selection thread
+  for (int gl = 5; gl < 8; ++gl)
+    if (((chunks + (1 << (gl - 5)) - 1) >> (gl - 5)) <= 2 * NGW) return gl;
+  return 8;
+}
+
+// candidate keys, two counts and the slice check word
+size_t workspace_per_row() { return (size_t)CAP * sizeof(uint16_t) + 12; }
+
 template <typename T>
 int launch(const FwdLaunch& L) {
   CUtensorMap tq, tk;
@@ -1276,8 +1036,8 @@ int launch(const FwdLaunch& L) {
   // grouped: n is the total row count, slice s owns rows [row_offsets[s], row_offsets[s+1])
   const int64_t rows = grouped ? L.n : L.slices * L.n;
   if (rows <= 0) return SDK_OK;
-  if (!make_rows_map(&tq, L.q, rows, bf16)) return SDK_ERR_CUDA;
-  if (!make_rows_map(&tk, L.k, L.slices * L.m, bf16)) return SDK_ERR_CUDA;
+  if (!make_rows_map(&tq, L.q, rows, bf16, TQ)) return SDK_ERR_CUDA;
+  if (!make_rows_map(&tk, L.k, L.slices * L.m, bf16, TK)) return SDK_ERR_CUDA;
   TcArgs a;
   a.q = L.q;
   a.k = L.k;
@@ -1285,22 +1045,22 @@ int launch(const FwdLaunch& L) {
   a.geo = SliceGeometry{L.row_offsets, L.slices, L.n};
   a.m = L.m;
   a.topk = L.topk;
+  a.glog = group_log(L.m);
   a.status = L.status;
   a.wait_limit_ns = wait_limit_ns();
   a.seg_bias = static_cast<const float*>(L.seg_bias);
   a.seg_len = L.seg_len;
   a.segs = L.segs;
   a.scale = (float)L.scale;
-  // grouped: at most ceil(rows / RS) + slices tiles; CTAs past the last exit at once
-  const int64_t grid = grouped ? (rows + RS - 1) / RS + L.slices : L.slices * ((L.n + RS - 1) / RS);
+  // grouped: at most ceil(rows / TQ) + slices tiles; CTAs past the last exit at once
+  const int64_t grid = grouped ? (rows + TQ - 1) / TQ + L.slices : L.slices * ((L.n + TQ - 1) / TQ);
   if (grid <= 0) return SDK_OK;
   if (grid > 0x7fffffff) return SDK_ERR_UNSUPPORTED;
   const bool bias = L.seg_bias != nullptr;
-  auto kern = L.topk < 8 ? (bias ? fused_fwd_tc<T, true, true> : fused_fwd_tc<T, true, false>)
-                         : (bias ? fused_fwd_tc<T, false, true> : fused_fwd_tc<T, false, false>);
+  auto kern = bias ? fused_fwd_tc<T, true> : fused_fwd_tc<T, false>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
     return SDK_ERR_CUDA;
-  const size_t need = (size_t)rows * (CAP * 4 + 8);
+  const size_t need = (size_t)rows * workspace_per_row();
   void* ws = L.workspace;
   const bool pooled = ws == nullptr;
   if (pooled) {
@@ -1310,10 +1070,10 @@ int launch(const FwdLaunch& L) {
   } else if (L.workspace_bytes < need || !aligned16(ws)) {
     return SDK_ERR_INVALID_ARGUMENT;
   }
-  // per row: CAP entries, a count and a flag (set at the first row of each slice)
-  a.cand = static_cast<uint32_t*>(ws);
-  a.cand_n = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + (size_t)rows * CAP * 4);
-  a.unsafe = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + (size_t)rows * (CAP * 4 + 4));
+  // per row: CAP candidate keys, two counts and a flag (set at the first row of each slice)
+  a.cand = static_cast<uint16_t*>(ws);
+  a.cand_n = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + (size_t)rows * CAP * sizeof(uint16_t));
+  a.unsafe = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + (size_t)rows * (CAP * sizeof(uint16_t) + 8));
   a.big16 = bf16 ? 0x5d80u : 0x7c00u;
   kern<<<(unsigned)grid, NT, SMEM_BYTES, L.stream>>>(tq, tk, a);
   int rc = cudaPeekAtLastError() == cudaSuccess ? SDK_OK : SDK_ERR_CUDA;
@@ -1344,8 +1104,7 @@ int launch(const FwdLaunch& L) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     // One resident wave, grid-stride: the warps of all SMs then walk the rows
     // together, so each slice's key and value rows are gathered while they
-    // are hot in L2 (a second wave re-reads them: 4.1 GB instead of 2.7 GB of
-    // DRAM reads at 128 slices).
+    // are hot in L2.
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fwd_tc_finish<T>, FW * kWarp, 0) != cudaSuccess ||
         per_sm < 1)
@@ -1372,8 +1131,8 @@ bool tensorcore_shape(int64_t rows, int64_t m, int d, int dv, int topk, int scor
 
 bool fwd_tensorcore_supports(const FwdLaunch& L) {
   if (L.n < 1) return false;
-  // a segment bias needs whole key tiles per segment
-  if (L.seg_bias && (L.segs < 1 || L.seg_len < 1 || L.seg_len % TK != 0 || L.seg_len * L.segs != L.m ||
+  // a segment bias needs whole half tiles per segment
+  if (L.seg_bias && (L.segs < 1 || L.seg_len < 1 || L.seg_len % HALF != 0 || L.seg_len * L.segs != L.m ||
                      !aligned16(L.seg_bias)))
     return false;
   if (!tensorcore_shape(L.row_offsets ? L.n : L.slices * L.n, L.m, L.d, L.dv, L.topk, L.score_grid, L.dtype))
@@ -1387,7 +1146,7 @@ size_t fwd_tensorcore_workspace(int64_t rows, int64_t m, int d, int dv, int topk
                                 int dtype) {
   (void)grouped;  // grouped and uniform slices need the same scratch per row
   if (!tensorcore_shape(rows, m, d, dv, topk, score_grid, dtype)) return 0;
-  return (size_t)rows * (CAP * 4 + 8);
+  return (size_t)rows * workspace_per_row();
 }
 
 int fwd_tensorcore(const FwdLaunch& L) {
