@@ -13,20 +13,21 @@
 //   warps 2, 3   in the first CTA of each slice: the input magnitude check
 //                of the slice's keys (below); for grouped rows: the gather of
 //                the query rows through the permutation;
-//   warps 4..11  selection: thread i of warp 4+j (j < 4) and of warp 8+j own
-//                query row 32j+i (TMEM lane); the first reads columns 0..127
-//                of each 256-key tile, the second columns 128..255.
+//   warps 4..19  selection: thread i of warps 4+j, 8+j, 12+j and 16+j
+//                (j < 4) own query row 32j+i (TMEM lane); warp 4+4c+j reads
+//                columns 64c..64c+63 of each 256-key tile.  Four selection
+//                warps per SM sub-partition hide each other's latencies.
 //
 // Pass 1 records, per row, the maxima of disjoint groups of G keys (G chosen
 // per call so that a row has at most 256 groups), rounded down to bf16.  The
 // k-th largest group maximum tau is a lower bound of the row's k-th largest
-// score: k different groups, so k different keys, reach it.  The two threads
-// of a row find it by a bisection over the bf16 values, exchanging partial
-// counts through shared memory.
+// score: k different groups, so k different keys, reach it.  The four
+// threads of a row find it by a bisection over the bf16 values, exchanging
+// partial counts through shared memory.
 //
 // Pass 2 recomputes the scores and keeps the key of every score that reaches
 // tau (a packed bf16 compare of the truncated scores: conservative), in the
-// thread's half of the row's candidate list in global memory.  For Gaussian
+// thread's quarter of the row's candidate list in global memory.  For Gaussian
 // inputs about 1.15·k keys per row pass.  A second kernel, one warp per row,
 // re-scores the candidates exactly from the gathered key rows (one fixed
 // fp32 summation order), keeps the k best (larger score first, lower key
@@ -52,23 +53,24 @@ using namespace sm100;
 
 constexpr int TQ = 128;          // query rows per CTA (TMEM lanes, MMA M)
 constexpr int TK = 256;          // keys per score tile (MMA N)
-constexpr int HALF = TK / 2;     // keys of a tile per selection thread
+constexpr int NSEL = 4;          // selection threads per query row
+constexpr int QK = TK / NSEL;    // keys of a tile per selection thread
 constexpr int D = 64;            // feature width (one 128-byte swizzle row)
 constexpr int KSTAGES = 4;
-constexpr int CAP = 128;         // candidate keys per row
-constexpr int CAPH = CAP / 2;    // candidate keys of each of the row's two selection threads
+constexpr int CAP = 192;         // candidate keys per row
+constexpr int CAPQ = CAP / NSEL; // candidate keys of each of the row's selection threads
 constexpr int FIX_CAP = 128;     // exact list of a row re-selected by one warp
-constexpr int NGW = 64;          // group-maximum words per selection thread (two bf16 each)
-constexpr int NT = 384;
+constexpr int NGW = 32;          // group-maximum words per selection thread (two bf16 each)
+constexpr int NT = 128 + NSEL * 4 * 32;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t Q_BYTES = TQ * D * 2;
 constexpr uint32_t K_BYTES = TK * D * 2;
 
 constexpr int OFF_Q = 0;
 constexpr int OFF_K = OFF_Q + (int)Q_BYTES;
-constexpr int OFF_GM = OFF_K + KSTAGES * (int)K_BYTES;  // [half][word][row] group maxima
-constexpr int OFF_XCH = OFF_GM + 2 * NGW * TQ * 4;      // [slot][half][row] the tau search's exchange
-constexpr int OFF_BAR = OFF_XCH + 2 * 2 * TQ * 4;
+constexpr int OFF_GM = OFF_K + KSTAGES * (int)K_BYTES;     // [thread][word][row] group maxima
+constexpr int OFF_XCH = OFF_GM + NSEL * NGW * TQ * 4;      // [slot][thread][row] the tau search's exchange
+constexpr int OFF_BAR = OFF_XCH + 2 * NSEL * TQ * 4;
 constexpr int NBARS = 1 + 2 * KSTAGES + 4;
 constexpr int OFF_MISC = OFF_BAR + NBARS * 8;
 constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
@@ -77,7 +79,7 @@ static_assert(OFF_BAR % 8 == 0, "mbarrier alignment");
 static_assert(OFF_GM % 1024 == 0 && OFF_K % 1024 == 0, "swizzled tiles need 1024-byte alignment");
 
 // Count words of a row in the candidate buffer, one per selection thread:
-// the number of keys it found (more than CAPH: its half of the list
+// the number of keys it found (more than CAPQ: its part of the list
 // overflowed, re-select the row exactly), or
 constexpr int32_t kCandAborted = -2;  // a pipeline wait timed out: nothing to finish
 
@@ -85,8 +87,8 @@ struct TcArgs {
   const void* q;     // query rows, gathered through row_index when that is set
   const void* k;     // key rows, for the magnitude check
   const int32_t* row_index;  // nullable: logical row -> query row (grouped slices)
-  uint16_t* cand;    // [rows][2][CAPH] candidate keys of each query row, per selection thread
-  int32_t* cand_n;   // [rows][2] key counts or kCandAborted
+  uint16_t* cand;    // [rows][NSEL][CAPQ] candidate keys of each query row, per selection thread
+  int32_t* cand_n;   // [rows][NSEL] key counts or kCandAborted
   uint32_t* unsafe;  // [rows], at each slice's first row: 1 when a key of the slice fails the magnitude check
   SliceGeometry geo;
   int64_t m;
@@ -96,7 +98,7 @@ struct TcArgs {
   unsigned int* status;
   uint64_t wait_limit_ns;  // bound of each pipeline wait (sdk_set_wait_limit)
   // kBias: score(r, j) = fl(fl(dot * scale) + seg_bias[r * segs + j / seg_len]),
-  // seg_len a multiple of HALF so that each thread's half tile lies in one segment
+  // seg_len a multiple of QK so that each thread's part of a tile lies in one segment
   const float* seg_bias;
   int64_t seg_len;
   int segs;
@@ -436,7 +438,7 @@ __global__ void __launch_bounds__(NT, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&s_empty[b], 8 * kWarp);
+      mbar_init(&s_empty[b], NSEL * 4 * kWarp);
     }
     *abort_flag = 0;
     mbar_fence_init();
@@ -560,12 +562,12 @@ __global__ void __launch_bounds__(NT, 1)
       }
     }
   } else if (warp >= 4) {
-    const int h = (warp - 4) >> 2, quarter = warp & 3;
+    const int h = (warp - 4) >> 2, quarter = warp & 3;  // column quarter, lane quarter
     const int rl = quarter * kWarp + lane;  // row within the CTA == TMEM lane
     const bool live = rl < count;
     const int64_t gr = row0 + rl;
-    const uint32_t tm = tmem + ((uint32_t)(quarter * kWarp) << 16) + (uint32_t)(h * HALF);
-    const uint32_t pair_bar = 2u + (uint32_t)quarter;  // the two warps of this lane quarter
+    const uint32_t tm = tmem + ((uint32_t)(quarter * kWarp) << 16) + (uint32_t)(h * QK);
+    const uint32_t row_bar = 2u + (uint32_t)quarter;  // the four warps of this lane quarter
     // group maxima: value v of this thread at word v/2, half v%2 of column rl
     const uint32_t gm_base = smem_addr(sm + OFF_GM) + (uint32_t)(h * NGW * TQ + rl) * 4u;
     uint32_t* xch = reinterpret_cast<uint32_t*>(sm + OFF_XCH);
@@ -573,33 +575,31 @@ __global__ void __launch_bounds__(NT, 1)
     const float neg_inf_f = __int_as_float(0xff800000);
     bool ok = true;
 
-    // Two 32-column chunks at a time: both TMEM loads, one wait, then the
-    // two chunks' independent work interleaves.  The TMEM buffer is released
-    // once the tile's last pair is in registers.  Half tiles past the last
-    // key (only the last tile of a slice) take the masked variant.
-    auto stream_tile = [&](int j, auto&& pair) -> bool {
+    // One 32-column chunk at a time; the other selection warps of the SM
+    // sub-partition cover the TMEM load latency.  The TMEM buffer is
+    // released once the tile's last chunk is in registers.  Chunks past the
+    // last key (only in the last tile of a slice) take the masked variant.
+    auto stream_tile = [&](int j, auto&& chunk) -> bool {
       const int b = j & 1;
       if (!__all_sync(0xffffffffu, mbar_wait(&s_full[b], (uint32_t)(j >> 1) & 1u, abort_flag, a.wait_limit_ns)))
         return false;
       tc_fence_after();
       const int t = j % ntiles;
-      const int64_t key_half = (int64_t)t * TK + h * HALF;
-      const int half_valid = (int)(a.m - key_half < HALF ? (a.m - key_half > 0 ? a.m - key_half : 0) : HALF);
-#pragma unroll 1
-      for (int cp = 0; cp < HALF / 64; ++cp) {
-        uint32_t va[32], vb[32];
-        tmem_load_32cols(tm + b * TK + (2 * cp) * 32, va);
-        tmem_load_32cols(tm + b * TK + (2 * cp + 1) * 32, vb);
-        tmem_wait_load(va);
-        reg_fence(vb);
-        if (cp == HALF / 64 - 1) {
+      const int64_t key_q = (int64_t)t * TK + h * QK;
+      const int q_valid = (int)(a.m - key_q < QK ? (a.m - key_q > 0 ? a.m - key_q : 0) : QK);
+#pragma unroll
+      for (int c = 0; c < QK / 32; ++c) {
+        uint32_t v[32];
+        tmem_load_32cols(tm + b * TK + c * 32, v);
+        tmem_wait_load(v);
+        if (c == QK / 32 - 1) {
           tc_fence_before();
           mbar_arrive(&s_empty[b]);
         }
-        if (half_valid >= HALF)
-          pair(va, vb, key_half + cp * 64, 64, std::true_type{});
+        if (q_valid >= QK)
+          chunk(v, key_q + c * 32, 32, std::true_type{});
         else
-          pair(va, vb, key_half + cp * 64, half_valid - cp * 64, std::false_type{});
+          chunk(v, key_q + c * 32, q_valid - c * 32, std::false_type{});
       }
       return true;
     };
@@ -608,69 +608,46 @@ __global__ void __launch_bounds__(NT, 1)
     // down to bf16; the finite values' range and count are kept for the tau
     // search.
     int nv = 0;             // values written
-    int pc = 0;             // pairs seen
-    float run = neg_inf_f;  // running maximum of a group spanning pairs
+    int cc = 0;             // chunks seen
+    float run = neg_inf_f;  // running maximum of a group spanning chunks
     float lo_f = __int_as_float(0x7f800000), hi_f = neg_inf_f;
     int nfin = 0;
-    auto track = [&](float x) {
+    auto put = [&](float x) {
+      asm volatile("st.shared.u16 [%0], %1;"
+                   ::"r"(gm_base + (uint32_t)(nv >> 1) * (TQ * 4u) + (uint32_t)(nv & 1) * 2u),
+                   "h"((unsigned short)bf16_floor(x))
+                   : "memory");
       const bool fin = x > neg_inf_f;  // NaN only in rows re-selected later
       hi_f = fmaxf(hi_f, x);
       lo_f = fminf(lo_f, fin ? x : __int_as_float(0x7f800000));
       nfin += fin ? 1 : 0;
+      ++nv;
     };
     float bias1 = 0.f;
     for (int j = 0; j < ntiles && ok; ++j) {
       if (kBias && live) {
-        const int64_t key_half = (int64_t)j * TK + h * HALF;
-        bias1 = key_half < a.m ? __ldg(a.seg_bias + gr * a.segs + key_half / a.seg_len) : 0.f;
+        const int64_t key_q = (int64_t)j * TK + h * QK;
+        bias1 = key_q < a.m ? __ldg(a.seg_bias + gr * a.segs + key_q / a.seg_len) : 0.f;
       }
-      ok = stream_tile(j, [&](uint32_t(&va)[32], uint32_t(&vb)[32], int64_t, int valid, auto whole) {
+      ok = stream_tile(j, [&](uint32_t(&v)[32], int64_t, int valid, auto whole) {
         if constexpr (!decltype(whole)::value) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            if (i >= valid) va[i] = 0xff800000u;
-            if (i + 32 >= valid) vb[i] = 0xff800000u;
-          }
+          for (int i = 0; i < 32; ++i)
+            if (i >= valid) v[i] = 0xff800000u;
         }
-        float ga[4], gb[4];
-        max8x4(va, ga);
-        max8x4(vb, gb);
-        float xa = max_nan(max3_nan(ga[0], ga[1], ga[2]), ga[3]);
-        float xb = max_nan(max3_nan(gb[0], gb[1], gb[2]), gb[3]);
-        if (kBias) {
-          xa = __fadd_rn(__fmul_rn(xa, a.scale), bias1);
-          xb = __fadd_rn(__fmul_rn(xb, a.scale), bias1);
+        float g[4];
+        max8x4(v, g);
+        float x = max_nan(max3_nan(g[0], g[1], g[2]), g[3]);
+        if (kBias) x = __fadd_rn(__fmul_rn(x, a.scale), bias1);
+        run = max_nan(run, x);
+        ++cc;
+        if ((cc & ((1 << gsh) - 1)) == 0) {
+          put(run);
+          run = neg_inf_f;
         }
-        if (gsh == 0) {  // one value per chunk: both in one word
-          asm volatile("st.shared.u32 [%0], %1;" ::"r"(gm_base + (uint32_t)pc * (TQ * 4u)),
-                       "r"(bf16_floor(xa) | (bf16_floor(xb) << 16))
-                       : "memory");
-          track(xa);
-          track(xb);
-          nv += 2;
-        } else {
-          run = max3_nan(run, xa, xb);
-          if (((pc + 1) & ((1 << (gsh - 1)) - 1)) == 0) {
-            asm volatile("st.shared.u16 [%0], %1;"
-                         ::"r"(gm_base + (uint32_t)(nv >> 1) * (TQ * 4u) + (uint32_t)(nv & 1) * 2u),
-                         "h"((unsigned short)bf16_floor(run))
-                         : "memory");
-            track(run);
-            ++nv;
-            run = neg_inf_f;
-          }
-        }
-        ++pc;
       });
     }
-    if (gsh >= 2 && (pc & ((1 << (gsh - 1)) - 1)) != 0) {  // a group cut short by the last tile
-      asm volatile("st.shared.u16 [%0], %1;"
-                   ::"r"(gm_base + (uint32_t)(nv >> 1) * (TQ * 4u) + (uint32_t)(nv & 1) * 2u),
-                   "h"((unsigned short)bf16_floor(run))
-                   : "memory");
-      track(run);
-      ++nv;
-    }
+    if ((cc & ((1 << gsh) - 1)) != 0) put(run);  // a group cut short by the last tile
     if (nv & 1) {  // pad the last word's upper half
       asm volatile("st.shared.u16 [%0], %1;" ::"r"(gm_base + (uint32_t)(nv >> 1) * (TQ * 4u) + 2u),
                    "h"((unsigned short)kBf16NegInf)
@@ -680,19 +657,21 @@ __global__ void __launch_bounds__(NT, 1)
     uint32_t hi = nfin ? bf16_ord(bf16_floor(hi_f)) : 0u;
     const int words = (nv + 1) >> 1;
 
-    // ---- tau: the k-th largest group maximum of the row (both threads'
-    // values), by bisection over ordered bf16 codes; L always satisfies
-    // count(>= L) >= k, H is the lowest code known to fail.  Both threads
-    // of a row compute the same L and H, so the two warps of a lane quarter
-    // meet the same number of barriers.
-    xch[(0 * 2 + h) * TQ + rl] = (lo & 0xffffu) | (hi << 16);
-    xch[(1 * 2 + h) * TQ + rl] = (uint32_t)nfin;
-    named_bar_sync(pair_bar, 2 * kWarp);
-    {
-      const uint32_t pr = xch[(0 * 2 + (1 - h)) * TQ + rl];
+    // ---- tau: the k-th largest group maximum of the row (all four
+    // threads' values), by bisection over ordered bf16 codes; L always
+    // satisfies count(>= L) >= k, H is the lowest code known to fail.  The
+    // four threads of a row compute the same L and H, so the four warps of a
+    // lane quarter meet the same number of barriers.
+    xch[(0 * NSEL + h) * TQ + rl] = (lo & 0xffffu) | (hi << 16);
+    xch[(1 * NSEL + h) * TQ + rl] = (uint32_t)nfin;
+    named_bar_sync(row_bar, NSEL * kWarp);
+    nfin = 0;
+#pragma unroll
+    for (int o = 0; o < NSEL; ++o) {
+      const uint32_t pr = xch[(0 * NSEL + o) * TQ + rl];
       lo = min(lo, pr & 0xffffu);
       hi = max(hi, pr >> 16);
-      nfin += (int)xch[(1 * 2 + (1 - h)) * TQ + rl];
+      nfin += (int)xch[(1 * NSEL + o) * TQ + rl];
     }
     uint32_t L = lo, H = hi + 1u;
     const bool bounded = nfin >= a.topk;  // else: no bound, every key is a candidate
@@ -705,10 +684,12 @@ __global__ void __launch_bounds__(NT, 1)
       const uint32_t mid = (L + H) >> 1;
       const uint32_t p2 = bf16_of_ord(mid) * 0x00010001u;
       const int mine = act ? count_ge(gm_base, words, p2) : 0;
-      named_bar_sync(pair_bar, 2 * kWarp);  // the partner has read the previous exchange
+      named_bar_sync(row_bar, NSEL * kWarp);  // the other threads have read the previous exchange
       xch[h * TQ + rl] = (uint32_t)mine;
-      named_bar_sync(pair_bar, 2 * kWarp);
-      const int c = mine + (int)xch[(1 - h) * TQ + rl];
+      named_bar_sync(row_bar, NSEL * kWarp);
+      int c = 0;
+#pragma unroll
+      for (int o = 0; o < NSEL; ++o) c += (int)xch[o * TQ + rl];
       if (act) {
         if (c >= a.topk) L = mid; else H = mid;
       }
@@ -716,42 +697,36 @@ __global__ void __launch_bounds__(NT, 1)
     const uint32_t tau_b = bounded ? bf16_of_ord(L) : kBf16NegInf;
     const float tau = __uint_as_float(tau_b << 16);
 
-    // ---- pass 2: candidate keys, into this thread's half of the row's list
+    // ---- pass 2: candidate keys, into this thread's part of the row's list
     const uint32_t tb2_plain = tau_b * 0x00010001u;
-    uint16_t* crow = a.cand + gr * CAP + h * CAPH;
+    uint16_t* crow = a.cand + gr * CAP + h * CAPQ;
     uint32_t cnt = 0;
     for (int j = ntiles; j < jobs && ok; ++j) {
       uint32_t tb2 = tb2_plain;
       if (kBias && live) {
-        const int64_t key_half = (int64_t)(j - ntiles) * TK + h * HALF;
-        const float bias2 = key_half < a.m ? __ldg(a.seg_bias + gr * a.segs + key_half / a.seg_len) : 0.f;
+        const int64_t key_q = (int64_t)(j - ntiles) * TK + h * QK;
+        const float bias2 = key_q < a.m ? __ldg(a.seg_bias + gr * a.segs + key_q / a.seg_len) : 0.f;
         tb2 = biased_threshold(tau, bias2, a.scale);
       }
-      ok = stream_tile(j, [&](uint32_t(&va)[32], uint32_t(&vb)[32], int64_t key0, int valid, auto whole) {
-        uint32_t ma = hit_mask(va, tb2), mb = hit_mask(vb, tb2);
-        if constexpr (!decltype(whole)::value) {
-          ma &= valid >= 32 ? 0xffffffffu : (valid > 0 ? (1u << valid) - 1u : 0u);
-          mb &= valid >= 64 ? 0xffffffffu : (valid > 32 ? (1u << (valid - 32)) - 1u : 0u);
-        }
-        if (!live) ma = mb = 0u;
+      ok = stream_tile(j, [&](uint32_t(&v)[32], int64_t key0, int valid, auto whole) {
+        uint32_t m = hit_mask(v, tb2);
+        if constexpr (!decltype(whole)::value) m &= valid >= 32 ? 0xffffffffu : (valid > 0 ? (1u << valid) - 1u : 0u);
+        if (!live) m = 0u;
         // one hit of each lane per round, a warp-uniform number of rounds
-        const uint32_t rounds = __reduce_max_sync(0xffffffffu, (uint32_t)(__popc(ma) + __popc(mb)));
+        const uint32_t rounds = __reduce_max_sync(0xffffffffu, (uint32_t)__popc(m));
         for (uint32_t rd = 0; rd < rounds; ++rd) {
-          const bool in_a = ma != 0u;
-          const uint32_t m = in_a ? ma : mb;
           const bool hit = m != 0u;
           const uint32_t i = hit ? 31u - __clz(m) : 0u;
-          const uint32_t bit = hit ? 1u << i : 0u;
-          if (in_a) ma ^= bit; else mb ^= bit;
-          if (hit && cnt < (uint32_t)CAPH) crow[cnt] = (uint16_t)((uint32_t)key0 + (in_a ? 0u : 32u) + i);
+          m ^= hit ? 1u << i : 0u;
+          if (hit && cnt < (uint32_t)CAPQ) crow[cnt] = (uint16_t)((uint32_t)key0 + i);
           cnt += hit ? 1u : 0u;
         }
       });
     }
-    // Hand this half of the row to the finish kernel: its count (more than
-    // CAPH: overflowed) or kCandAborted.
-    named_bar_sync(pair_bar, 2 * kWarp);
-    if (live) a.cand_n[2 * gr + h] = *abort_flag ? kCandAborted : (int32_t)cnt;
+    // Hand this part of the row to the finish kernel: its count (more than
+    // CAPQ: overflowed) or kCandAborted.
+    named_bar_sync(row_bar, NSEL * kWarp);
+    if (live) a.cand_n[NSEL * gr + h] = *abort_flag ? kCandAborted : (int32_t)cnt;
   }
 
   __syncthreads();
@@ -809,8 +784,9 @@ __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
   const unsigned lt = (1u << lane) - 1u;
   FinWarp& w = sw[warp];
   for (int64_t r = (int64_t)blockIdx.x * FW + warp; r < a.rows; r += (int64_t)gridDim.x * FW) {
-    const int c0 = a.cand_n[2 * r], c1 = a.cand_n[2 * r + 1];
-    if (c0 == kCandAborted || c1 == kCandAborted) {
+    const int4 cq = reinterpret_cast<const int4*>(a.cand_n)[r];
+    const int c0 = cq.x, c1 = cq.y, c2 = cq.z, c3 = cq.w;
+    if (c0 == kCandAborted || c1 == kCandAborted || c2 == kCandAborted || c3 == kCandAborted) {
       // the stream kernel gave up on this row (a bounded wait ran out, device
       // status bit 2): defined outputs that no caller can mistake for a
       // result — NaN output and LSE, index -1 (the backward skips it)
@@ -824,7 +800,7 @@ __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
       if (lane == 0) a.lse[r] = __int_as_float(0x7fc00000);
       continue;
     }
-    const int cnt = c0 + c1;
+    const int cnt = c0 + c1 + c2 + c3;
     const int64_t slice = slice_of_row(a.geo, r);
     const int64_t pr = a.row_index ? (int64_t)a.row_index[r] : r;  // query and output row
     const uint4 qg = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(a.q) + pr * D) + g);
@@ -836,7 +812,7 @@ __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
     bool bias_bad = false;  // NaN or +inf biases are ranked by the exact path only
     if (brow)
       for (int j = lane; j < a.segs; j += kWarp) bias_bad |= !(brow[j] < __int_as_float(0x7f800000));
-    if (c0 < 0 || c1 < 0 || c0 > CAPH || c1 > CAPH || cnt < a.topk || unsafe ||
+    if (min(min(c0, c1), min(c2, c3)) < 0 || max(max(c0, c1), max(c2, c3)) > CAPQ || cnt < a.topk || unsafe ||
         __any_sync(0xffffffffu, bias_bad)) {
       uint8_t* fix = reinterpret_cast<uint8_t*>(&w);
       reselect_row<T>(RowOut{a.q, a.k, a.v, a.out, a.top_idx, a.lse, a.top_scores}, a.m, a.topk, a.scale, slice, r, pr,
@@ -846,7 +822,9 @@ __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
     }
     // the candidates of both selection threads, in list order
     const uint16_t* crow = a.cand + r * CAP;
-    for (int s = lane; s < cnt; s += kWarp) w.si[s] = (int)crow[s < c0 ? s : CAPH + (s - c0)];
+    const int o1 = c0, o2 = c0 + c1, o3 = c0 + c1 + c2;
+    for (int s = lane; s < cnt; s += kWarp)
+      w.si[s] = (int)crow[s < o1 ? s : (s < o2 ? CAPQ + (s - o1) : (s < o3 ? 2 * CAPQ + (s - o2) : 3 * CAPQ + (s - o3)))];
     __syncwarp();
     // exact scores: group grp re-scores candidates grp, grp + 4, ... from the
     // gathered key rows (eight lanes per 128-byte row, one fixed summation order)
@@ -1019,14 +997,14 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 // log2 of the keys per group maximum: the smallest group (32 .. 256 keys)
 // that leaves each selection thread at most 2·NGW values.
 int group_log(int64_t m) {
-  const int64_t chunks = ((m + TK - 1) / TK) * (HALF / 32);  // 32-key chunks per selection thread
+  const int64_t chunks = ((m + TK - 1) / TK) * (QK / 32);  // 32-key chunks per selection thread
   for (int gl = 5; gl < 8; ++gl)
     if (((chunks + (1 << (gl - 5)) - 1) >> (gl - 5)) <= 2 * NGW) return gl;
   return 8;
 }
 
-// candidate keys, two counts and the slice check word
-size_t workspace_per_row() { return (size_t)CAP * sizeof(uint16_t) + 12; }
+// candidate keys, NSEL counts and the slice check word
+size_t workspace_per_row() { return (size_t)CAP * sizeof(uint16_t) + 4 * NSEL + 4; }
 
 template <typename T>
 int launch(const FwdLaunch& L) {
@@ -1070,10 +1048,10 @@ int launch(const FwdLaunch& L) {
   } else if (L.workspace_bytes < need || !aligned16(ws)) {
     return SDK_ERR_INVALID_ARGUMENT;
   }
-  // per row: CAP candidate keys, two counts and a flag (set at the first row of each slice)
+  // per row: CAP candidate keys, NSEL counts and a flag (set at the first row of each slice)
   a.cand = static_cast<uint16_t*>(ws);
   a.cand_n = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + (size_t)rows * CAP * sizeof(uint16_t));
-  a.unsafe = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + (size_t)rows * (CAP * sizeof(uint16_t) + 8));
+  a.unsafe = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + (size_t)rows * (CAP * sizeof(uint16_t) + 4 * NSEL));
   a.big16 = bf16 ? 0x5d80u : 0x7c00u;
   kern<<<(unsigned)grid, NT, SMEM_BYTES, L.stream>>>(tq, tk, a);
   int rc = cudaPeekAtLastError() == cudaSuccess ? SDK_OK : SDK_ERR_CUDA;
@@ -1131,8 +1109,8 @@ bool tensorcore_shape(int64_t rows, int64_t m, int d, int dv, int topk, int scor
 
 bool fwd_tensorcore_supports(const FwdLaunch& L) {
   if (L.n < 1) return false;
-  // a segment bias needs whole half tiles per segment
-  if (L.seg_bias && (L.segs < 1 || L.seg_len < 1 || L.seg_len % HALF != 0 || L.seg_len * L.segs != L.m ||
+  // a segment bias needs whole tile quarters per segment
+  if (L.seg_bias && (L.segs < 1 || L.seg_len < 1 || L.seg_len % QK != 0 || L.seg_len * L.segs != L.m ||
                      !aligned16(L.seg_bias)))
     return false;
   if (!tensorcore_shape(L.row_offsets ? L.n : L.slices * L.n, L.m, L.d, L.dv, L.topk, L.score_grid, L.dtype))
