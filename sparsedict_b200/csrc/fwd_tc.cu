@@ -315,21 +315,6 @@ __device__ __forceinline__ void write_row(const T* vbase, ScoreOf score_of, Inde
 
 __device__ __forceinline__ float finite_or_zero(float x) { return isfinite(x) ? x : 0.f; }
 
-// Order-preserving 64-bit rank key: larger key = ranks higher.  The high
-// word maps the float onto an unsigned order (NaN highest, -0 == +0); the
-// low word is the complemented key index, so equal scores rank the lower
-// index higher.
-__device__ __forceinline__ uint64_t rank_key(float x, uint32_t idx) {
-  uint32_t u;
-  if (x != x) {
-    u = 0xffffffffu;
-  } else {
-    u = __float_as_uint(x + 0.0f);
-    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  }
-  return ((uint64_t)u << 32) | (uint64_t)(0xffffffffu - idx);
-}
-
 // Exact re-selection of one row by a whole warp (rows whose bucketed list
 // could not be shrunk).  32 keys per step: eight group dots of four keys,
 // then lane L takes the score of key k0 + L; a lane keeps each key beating
@@ -800,12 +785,73 @@ struct __align__(16) FinWarp {
 };
 static_assert(sizeof(float) * CAP + sizeof(int) * CAP >= FIX_CAP * 8, "re-selection buffers exceed sc/si");
 
+// Order-preserving 32-bit form of a score (NaN highest, -0 == +0).
+__device__ __forceinline__ uint32_t ord_score(float x) {
+  if (x != x) return 0xffffffffu;
+  const uint32_t u = __float_as_uint(x + 0.0f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Keeps the `topk` best of a row's `cnt` candidates (larger score first,
+// lower key index on ties; cnt >= topk) and writes them, in list order, to
+// w.sc / w.si; returns the largest score.  The candidates are the four
+// selection threads' lists (counts c0, c1, c2 and the rest) read NVT per
+// lane.  The lowest-ranked candidate is dropped until topk remain: the
+// lowest ordered score, and among equal scores the highest key index.
+template <int NVT>
+__device__ __forceinline__ float cut_candidates(const uint16_t* crow, const float* srow, int c0, int c1, int c2,
+                                                int cnt, int topk, FinWarp& w, int lane) {
+  const int o1 = c0, o2 = c0 + c1, o3 = c0 + c1 + c2;
+  float xs[NVT];
+  int ks[NVT];
+  uint32_t os[NVT];
+  bool hk[NVT];
+#pragma unroll
+  for (int i = 0; i < NVT; ++i) {
+    const int s = lane + kWarp * i;
+    hk[i] = s < cnt;
+    const int at = s < o1 ? s : (s < o2 ? CAPQ + (s - o1) : (s < o3 ? 2 * CAPQ + (s - o2) : 3 * CAPQ + (s - o3)));
+    xs[i] = hk[i] ? srow[at] : 0.f;
+    ks[i] = hk[i] ? (int)crow[at] : 0;
+    os[i] = ord_score(xs[i]);
+  }
+  for (int dn = cnt - topk; dn > 0; --dn) {
+    uint32_t mn = 0xffffffffu;
+#pragma unroll
+    for (int i = 0; i < NVT; ++i) mn = hk[i] ? min(mn, os[i]) : mn;
+    mn = __reduce_min_sync(0xffffffffu, mn);
+    int kx = -1;
+#pragma unroll
+    for (int i = 0; i < NVT; ++i) kx = (hk[i] && os[i] == mn) ? max(kx, ks[i]) : kx;
+    kx = __reduce_max_sync(0xffffffffu, kx);
+#pragma unroll
+    for (int i = 0; i < NVT; ++i) hk[i] = hk[i] && !(os[i] == mn && ks[i] == kx);
+  }
+  const unsigned lt = (1u << lane) - 1u;
+  int pos = 0;
+  float mx = __int_as_float(0xff800000);
+#pragma unroll
+  for (int i = 0; i < NVT; ++i) {
+    const unsigned bal = __ballot_sync(0xffffffffu, hk[i]);
+    if (hk[i]) {
+      const int p = pos + __popc(bal & lt);
+      w.sc[p] = xs[i];
+      w.si[p] = ks[i];
+      mx = fmaxf(mx, xs[i]);
+    }
+    pos += __popc(bal);
+  }
+  __syncwarp();
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  return mx;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
   __shared__ FinWarp sw[FW];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane & 7, grp = lane >> 3;
-  const unsigned lt = (1u << lane) - 1u;
   FinWarp& w = sw[warp];
   for (int64_t r = (int64_t)blockIdx.x * FW + warp; r < a.rows; r += (int64_t)gridDim.x * FW) {
     const int4 cq = reinterpret_cast<const int4*>(a.cand_n)[r];
@@ -844,58 +890,11 @@ __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
                       w.pad, lane);
       continue;
     }
-    // the candidates of the four selection threads, in list order
-    const uint16_t* crow = a.cand + r * CAP;
-    const float* srow = a.cand_s + r * CAP;
-    const int o1 = c0, o2 = c0 + c1, o3 = c0 + c1 + c2;
-    float xs[NV];
-    int ks[NV];
-    uint64_t rk[NV];
-    bool hk[NV];
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int s = lane + kWarp * i;
-      hk[i] = s < cnt;
-      const int at = s < o1 ? s : (s < o2 ? CAPQ + (s - o1) : (s < o3 ? 2 * CAPQ + (s - o2) : 3 * CAPQ + (s - o3)));
-      xs[i] = hk[i] ? srow[at] : 0.f;
-      ks[i] = hk[i] ? (int)crow[at] : 0;
-      rk[i] = hk[i] ? rank_key(xs[i], (uint32_t)ks[i]) : ~0ull;
-    }
-    // exact cut to k (larger score first, lower key index on ties): drop the
-    // lowest-ranked candidate until k remain (rank keys are distinct, so
-    // each round removes exactly one)
-    for (int dn = cnt - a.topk; dn > 0; --dn) {
-      uint64_t mn = ~0ull;
-#pragma unroll
-      for (int i = 0; i < NV; ++i) mn = rk[i] < mn ? rk[i] : mn;
-      const uint32_t mh = __reduce_min_sync(0xffffffffu, (uint32_t)(mn >> 32));
-      const uint32_t ml = __reduce_min_sync(0xffffffffu, (uint32_t)(mn >> 32) == mh ? (uint32_t)mn : 0xffffffffu);
-      const uint64_t low = ((uint64_t)mh << 32) | ml;
-#pragma unroll
-      for (int i = 0; i < NV; ++i)
-        if (rk[i] == low) {
-          rk[i] = ~0ull;
-          hk[i] = false;
-        }
-    }
-    // compact the k kept, in list order
-    int pos = 0;
-    float mx = __int_as_float(0xff800000);
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const unsigned bal = __ballot_sync(0xffffffffu, hk[i]);
-      if (hk[i]) {
-        const int p = pos + __popc(bal & lt);
-        w.sc[p] = xs[i];
-        w.si[p] = ks[i];
-        mx = fmaxf(mx, xs[i]);
-      }
-      pos += __popc(bal);
-    }
-    __syncwarp();
-    const int sel = pos;
-#pragma unroll
-    for (int o2 = 16; o2 > 0; o2 >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o2));
+    // the k best candidates of the four selection threads, in list order
+    const float mx = cnt <= 3 * kWarp
+                         ? cut_candidates<3>(a.cand + r * CAP, a.cand_s + r * CAP, c0, c1, c2, cnt, a.topk, w, lane)
+                         : cut_candidates<NV>(a.cand + r * CAP, a.cand_s + r * CAP, c0, c1, c2, cnt, a.topk, w, lane);
+    const int sel = a.topk;
     // LSE; lane j holds selections j and j + 32 (k <= 64).  Biased scores are final.
     const float sc_mul = brow ? 1.f : a.scale;
     const bool v0 = lane < sel, v1 = lane + kWarp < sel;
