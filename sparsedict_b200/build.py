@@ -19,7 +19,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libsparsedict_b200.so"
 SOURCES = ["capi.cu", "fwd_generic.cu", "fwd_tc.cu", "bwd.cu", "bwd_km.cu", "stages.cu", "select_attn.cu",
-           "bwd_noalloc.cu"]
+           "bwd_noalloc.cu", "affinity_tc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -109,6 +109,13 @@ int bwd_keymajor(const BwdLaunch& L, void* dk, void* dv, int out_acc, int accumu
 int finalize_grad(const void* acc, void* out, int64_t count, double multiplier, int dtype,
                   cudaStream_t stream);
 
+// Dense fp16 affinity on the tensor cores (affinity_tc.cu): fp16, d >= 64,
+// 16-byte aligned rows; `affinity` routes such calls there.
+bool affinity_tensorcore_supports(const void* q, const void* k, int64_t n, int64_t m, int d, int64_t q_stride,
+                                  int64_t k_stride, int dtype);
+int affinity_tensorcore(const void* q, const void* k, float* scores, int64_t n, int64_t m, int d,
+                        int64_t q_stride, int64_t k_stride, cudaStream_t stream);
+
 // Stage ops (stages.cu).
 int affinity(const void* q, const void* k, float* scores, int64_t n, int64_t m, int d,
              int64_t q_stride, int64_t k_stride, int dtype, cudaStream_t stream);

@@ -1,7 +1,8 @@
 // Stand-alone stage ops of the top-k attention path and the top-1 router.
 //
 //   affinity   dense scores = q·kᵀ (fp32), reference tiled_affinity
-//              (kernels/fused_topk_attn.py:227-287)
+//              (kernels/fused_topk_attn.py:227-287); fp16 rows with d >= 64
+//              go to the tensor-core kernel of affinity_tc.cu
 //   select     per-row top-k of a score matrix, reference tiled_topk
 //              (kernels/fused_topk_attn.py:290-336)
 //   aggregate  softmax over selected scores and weighted gather of value
@@ -253,6 +254,8 @@ int aggregate_v(const void* ts, const void* ti, const void* v, float* out, int64
 
 int affinity(const void* q, const void* k, float* scores, int64_t n, int64_t m, int d, int64_t qs, int64_t ks,
              int dtype, cudaStream_t stream) {
+  if (affinity_tensorcore_supports(q, k, n, m, d, qs, ks, dtype))
+    return affinity_tensorcore(q, k, scores, n, m, d, qs, ks, stream);
   const dim3 grid((unsigned)((m + A_BN - 1) / A_BN), (unsigned)((n + A_BM - 1) / A_BM));
   if (grid.y > 65535u) return SDK_ERR_UNSUPPORTED;
   if (dtype == SDK_DTYPE_F32)

@@ -270,6 +270,35 @@ def test_tiled_affinity_matches_torch_fp16():
     assert torch.allclose(out, q.float() @ k.float().T, atol=1e-2, rtol=1e-2)
 
 
+@pytest.mark.parametrize("n,m,d", [(300, 1000, 64), (129, 257, 100), (1000, 4100, 200), (37, 700, 64)])
+def test_tiled_affinity_fp16_tensor_cores(n, m, d):
+    # fp16 rows with d >= 64 take the tcgen05 kernel: 128 x 256 score tiles,
+    # features past d and rows past the ends read as zero; the products of
+    # fp16 values are exact in fp32, so only the summation order differs.
+    g = torch.Generator().manual_seed(n + m + d)
+    q = torch.randn(n, d, generator=g).to(torch.float16)
+    k = torch.randn(m, d, generator=g).to(torch.float16)
+    out = tiled_affinity(q.to(DEV), k.to(DEV))
+    assert out.dtype == torch.float32 and out.shape == (n, m)
+    ref = q.double() @ k.double().T
+    np.testing.assert_allclose(out.cpu().double().numpy(), ref.numpy(), atol=1e-4, rtol=1e-5)
+    assert _native.device_status(clear=True) == 0
+
+
+def test_tiled_affinity_fp16_strided_rows_both_kernels():
+    # row strides of 104 halves (16-byte rows: tensor cores) and 100 halves
+    # (the CUDA-core kernel) give the same scores
+    torch.manual_seed(5)
+    qb = torch.randn(260, 104, device=DEV, dtype=torch.float16)
+    kb = torch.randn(300, 100, device=DEV, dtype=torch.float16)
+    q, k = qb[:, :96], kb[:, :96]
+    ref = q.double() @ k.double().T
+    out = tiled_affinity(q, k)
+    np.testing.assert_allclose(out.cpu().double().numpy(), ref.cpu().numpy(), atol=1e-4, rtol=1e-5)
+    out2 = tiled_affinity(q, k.contiguous())
+    np.testing.assert_allclose(out2.cpu().double().numpy(), ref.cpu().numpy(), atol=1e-4, rtol=1e-5)
+
+
 def test_tiled_affinity_fp32_strided_rows():
     torch.manual_seed(1)
     base = torch.randn(70, 48, device=DEV)
