@@ -5,7 +5,8 @@ Public API (the reference's names and signatures):
     tiled_affinity, tiled_topk, tiled_topk_aggregate
 plus routed dictionary attention (``routed_dictionary_attention``), the gated
 mixture over a bank of dictionary atoms (``gated_mixture_attention``, the
-``_mixture`` of SparseDict's MoE dictionary) and the row-sharded multi-GPU step
+``_mixture`` of SparseDict's MoE dictionary, with the model hooks of
+``sparsedict_b200.model_hooks``) and the row-sharded multi-GPU step
 (``sparsedict_b200.sharded``); the selection operators of SparseDict's
 ``topk_select`` module over given scores live in ``sparsedict_b200.selection``.
 """
@@ -20,6 +21,7 @@ from .kernels.fused_topk_attn import (
 from .kernels.hybrid_topk import _hybrid_topk_attention_with_aux, hybrid_topk_attention
 from ._ops import deterministic_backward, set_deterministic_backward
 from .mixture import GatedMixtureFunction, gated_mixture_attention
+from .model_hooks import fused_mixture, fused_token_attention, install_fused_mixture
 from .routed import RoutedDictionaryAttention, routed_dictionary_attention
 from .sharded import ShardedTopKAttention, ShardPlan
 
@@ -31,6 +33,9 @@ __all__ = [
     "set_deterministic_backward",
     "GatedMixtureFunction",
     "gated_mixture_attention",
+    "fused_mixture",
+    "fused_token_attention",
+    "install_fused_mixture",
     "RoutedDictionaryAttention",
     "routed_dictionary_attention",
     "fused_topk_attention",

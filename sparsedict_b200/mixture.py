@@ -22,15 +22,16 @@ import torch
 from . import _native, _ops
 
 
-def _gate_bias(gates: torch.Tensor, rows: int, experts: int, acc: torch.dtype, tiny: float) -> torch.Tensor:
+def _gate_bias(gates: torch.Tensor, rows: int, experts: int, acc: torch.dtype, tiny: float,
+               scale: float = 1.0) -> torch.Tensor:
     g = gates.reshape(rows, experts).to(acc)
-    bias = g.clamp_min(tiny).log()
+    bias = g.clamp_min(tiny).log() * scale
     return torch.where(g == 0, torch.full_like(bias, float("-inf")), bias).contiguous()
 
 
 class GatedMixtureFunction(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, queries, keys, values, gates, k):
+    def forward(ctx, queries, keys, values, gates, k, scale=1.0):
         b, n, dk = queries.shape
         e, m, _ = keys.shape
         c = values.shape[-1]
@@ -40,11 +41,12 @@ class GatedMixtureFunction(torch.autograd.Function):
         k2 = keys.reshape(1, e * m, dk)
         v2 = values.reshape(1, e * m, c)
         tiny = torch.finfo(queries.dtype).tiny
-        bias = None if gates is None else _gate_bias(gates, rows, e, acc, tiny)
-        out, idx, lse, _ = _ops.topk_attn_fwd(q2, k2, v2, k, 1.0, seg_bias=bias)
+        bias = None if gates is None else _gate_bias(gates, rows, e, acc, tiny, scale)
+        out, idx, lse, _ = _ops.topk_attn_fwd(q2, k2, v2, k, scale, seg_bias=bias)
         ctx.save_for_backward(q2, k2, v2, idx, lse, gates, bias)
         ctx.shape = (b, n, dk, e, m, c)
         ctx.tiny = tiny
+        ctx.scale = scale
         return out.reshape(b, n, c)
 
     @staticmethod
@@ -56,16 +58,18 @@ class GatedMixtureFunction(torch.autograd.Function):
         dbias = None
         if bias is not None and ctx.needs_input_grad[3]:
             dbias = torch.empty((rows, e), device=q2.device, dtype=bias.dtype)
-        dq, dk_acc, dv_acc = _ops.topk_attn_bwd(q2, k2, v2, dout, idx, lse, 1.0, seg_bias=bias, dseg_bias=dbias)
+        dq, dk_acc, dv_acc = _ops.topk_attn_bwd(q2, k2, v2, dout, idx, lse, ctx.scale, seg_bias=bias,
+                                                dseg_bias=dbias)
         dgates = None
         if dbias is not None:
             g = gates.reshape(rows, e).to(dbias.dtype)
             live = g >= ctx.tiny  # clamp_min passes the gradient; 0 gates are masked
-            dgates = torch.where(live, dbias / torch.where(live, g, torch.ones_like(g)), torch.zeros_like(g))
+            dgates = torch.where(live, dbias * ctx.scale / torch.where(live, g, torch.ones_like(g)),
+                                 torch.zeros_like(g))
             dgates = dgates.reshape(b, n, e).to(gates.dtype)
         dkeys = _ops.finalize_grad(dk_acc, k2.dtype).reshape(e, m, dk)
         dvalues = _ops.finalize_grad(dv_acc, v2.dtype).reshape(e, m, c)
-        return dq.reshape(b, n, dk), dkeys, dvalues, dgates, None
+        return dq.reshape(b, n, dk), dkeys, dvalues, dgates, None, None
 
 
 def gated_mixture_attention(
@@ -74,6 +78,7 @@ def gated_mixture_attention(
     values: torch.Tensor,
     top_k: int,
     gates: torch.Tensor | None = None,
+    scale: float = 1.0,
 ) -> torch.Tensor:
     """Softmax top-k mixture of each token over the projected atoms of all experts.
 
@@ -81,8 +86,11 @@ def gated_mixture_attention(
     ``(E, M, C)`` (the atom projections of ``_mixture``), optional ``gates``
     ``(B, N, E)``: a zero gate disables that expert for the token and nonzero
     gates are folded in additively (``+log g``), so the slots selected by the
-    top-k come out renormalised together.  Returns ``(B, N, C)``; differentiable
-    in queries, keys, values and gates.
+    top-k come out renormalised together.  ``scale`` multiplies the folded
+    score, ``(q·k + log g) * scale`` (SparseDict's token-routed restorer
+    divides by ``tau * sqrt(d_k)`` after the fold, moe_topk_restorer.py:165-170);
+    ``_mixture`` itself uses 1.  Returns ``(B, N, C)``; differentiable in
+    queries, keys, values and gates.
     """
     for name, t in (("queries", queries), ("keys", keys), ("values", values)):
         if not isinstance(t, torch.Tensor):
@@ -111,5 +119,7 @@ def gated_mixture_attention(
         raise ValueError("all inputs must be on one CUDA device")
     if not all(t.is_contiguous() for t in tensors):
         raise ValueError("inputs must be contiguous")
+    if not isinstance(scale, (int, float)) or isinstance(scale, bool) or not (scale > 0 and scale < float("inf")):
+        raise ValueError(f"scale must be a finite positive number; got {scale}")
     _native.load()
-    return GatedMixtureFunction.apply(queries, keys, values, gates, top_k)
+    return GatedMixtureFunction.apply(queries, keys, values, gates, top_k, float(scale))
