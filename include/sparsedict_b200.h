@@ -102,7 +102,7 @@ int sdk_topk_attn_fwd(const void* q, const void* k, const void* v, void* out, in
 /*
  * Scratch of the forward: the bf16/fp16 tensor-core path (d = dv = 64,
  * topk <= 64, m <= 65536, score_grid 0, uniform slices) hands each query row's
- * candidate list (192 keys with their scores, and four counts) from its streaming
+ * candidate list (192 two-byte keys and four counts) from its streaming
  * kernel to its finishing kernel.  Returns the bytes for `rows` query rows
  * (slices*n, or the grouped row count), 0 when the call will not take that
  * path.  `grouped` (row_offsets or row_index will be passed) does not change

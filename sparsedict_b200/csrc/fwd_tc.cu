@@ -25,19 +25,19 @@
 // threads of a row find it by a bisection over the bf16 values, exchanging
 // partial counts through shared memory.
 //
-// Pass 2 recomputes the scores and keeps every key whose score reaches tau
-// (a packed bf16 compare of the truncated scores: conservative), with its
-// fp32 tensor-core score (read back through a 128-byte shared-memory stage),
-// in the thread's quarter of the row's candidate list in global memory.  For
+// Pass 2 recomputes the scores and keeps the key of every score that reaches
+// tau (a packed bf16 compare of the truncated scores: conservative), in the
+// thread's quarter of the row's candidate list in global memory.  For
 // Gaussian inputs about 1.15·k keys per row pass.  A second kernel, one warp
-// per row, keeps the k best candidates (larger score first, lower key index
-// on ties) and writes the LSE, the indices and the softmax-weighted sum of
-// the gathered value rows.  A row whose candidates overflow its list
-// (heavily tied scores) is re-selected exactly by its warp over all keys.
+// per row, re-scores the candidates exactly from the gathered key rows (one
+// fixed fp32 summation order), keeps the k best (larger score first, lower
+// key index on ties), and writes the LSE, the indices and the
+// softmax-weighted sum of the gathered value rows.  A row whose candidates
+// overflow its list (heavily tied scores) is re-selected exactly by its warp
+// over all keys.
 //
-// Scores are the tensor cores' fp32 accumulations of the exact bf16/fp16
-// products; scale = 1/(T·sqrt(d)) > 0 is applied in the epilogue, or, with a
-// segment bias, to each candidate as fl(fl(dot·scale)+bias).
+// scale = 1/(T·sqrt(d)) > 0 is applied in the epilogue, or, with a segment
+// bias, to each exact score as fl(fl(dot·scale)+bias).
 #include <cuda.h>
 
 #include <mutex>
@@ -89,7 +89,6 @@ struct TcArgs {
   const void* k;     // key rows, for the magnitude check
   const int32_t* row_index;  // nullable: logical row -> query row (grouped slices)
   uint16_t* cand;    // [rows][NSEL][CAPQ] candidate keys of each query row, per selection thread
-  float* cand_s;     // [rows][NSEL][CAPQ] their scores (final scores with a bias)
   int32_t* cand_n;   // [rows][NSEL] key counts or kCandAborted
   uint32_t* unsafe;  // [rows], at each slice's first row: 1 when a key of the slice fails the magnitude check
   SliceGeometry geo;
@@ -557,10 +556,6 @@ __global__ void __launch_bounds__(NT, 1)
     const uint32_t row_bar = 2u + (uint32_t)quarter;  // the four warps of this lane quarter
     // group maxima: value v of this thread at word v/2, half v%2 of column rl
     const uint32_t gm_base = smem_addr(sm + OFF_GM) + (uint32_t)(h * NGW * TQ + rl) * 4u;
-    // pass-2 stage of this thread: 128 bytes, word `lane` of its group-maximum
-    // words for the quarter's rows (only this warp reads those in the tau search)
-    const uint32_t stage = smem_addr(sm + OFF_GM) + (uint32_t)((h * NGW + lane) * TQ + quarter * kWarp) * 4u;
-    const uint32_t sw4 = (uint32_t)(lane & 7) << 4;  // bank swizzle of the stage
     uint32_t* xch = reinterpret_cast<uint32_t*>(sm + OFF_XCH);
     const int gsh = a.glog - 5;  // a group is 2^gsh chunks of 32 keys of this thread
     const float neg_inf_f = __int_as_float(0xff800000);
@@ -687,19 +682,16 @@ __global__ void __launch_bounds__(NT, 1)
     }
     const uint32_t tau_b = bounded ? bf16_of_ord(L) : kBf16NegInf;
     const float tau = __uint_as_float(tau_b << 16);
-    __syncwarp();  // the warp's group-maximum words become its stages
 
     // ---- pass 2: candidate keys, into this thread's part of the row's list
     const uint32_t tb2_plain = tau_b * 0x00010001u;
     uint16_t* crow = a.cand + gr * CAP + h * CAPQ;
-    float* srow = a.cand_s + gr * CAP + h * CAPQ;
     uint32_t cnt = 0;
     for (int j = ntiles; j < jobs && ok; ++j) {
       uint32_t tb2 = tb2_plain;
-      float bias2 = 0.f;
       if (kBias && live) {
         const int64_t key_q = (int64_t)(j - ntiles) * TK + h * QK;
-        bias2 = key_q < a.m ? __ldg(a.seg_bias + gr * a.segs + key_q / a.seg_len) : 0.f;
+        const float bias2 = key_q < a.m ? __ldg(a.seg_bias + gr * a.segs + key_q / a.seg_len) : 0.f;
         tb2 = biased_threshold(tau, bias2, a.scale);
       }
       ok = stream_tile(j, [&](uint32_t(&v)[32], int64_t key0, int valid, auto whole) {
@@ -708,25 +700,11 @@ __global__ void __launch_bounds__(NT, 1)
         if (!live) m = 0u;
         // one hit of each lane per round, a warp-uniform number of rounds
         const uint32_t rounds = __reduce_max_sync(0xffffffffu, (uint32_t)__popc(m));
-        if (rounds == 0u) return;
-        // the chunk's scores, 16-byte piece p at p ^ (lane & 7) (eight lanes
-        // of a store phase cover all 32 banks)
-#pragma unroll
-        for (int p = 0; p < 8; ++p)
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(stage + (((uint32_t)p << 4) ^ sw4)),
-                       "r"(v[4 * p]), "r"(v[4 * p + 1]), "r"(v[4 * p + 2]), "r"(v[4 * p + 3])
-                       : "memory");
         for (uint32_t rd = 0; rd < rounds; ++rd) {
           const bool hit = m != 0u;
           const uint32_t i = hit ? 31u - __clz(m) : 0u;
           m ^= hit ? 1u << i : 0u;
-          float x;
-          asm volatile("ld.shared.f32 %0, [%1];" : "=f"(x) : "r"(stage + ((i << 2) ^ sw4)) : "memory");
-          if (kBias) x = __fadd_rn(__fmul_rn(x, a.scale), bias2);
-          if (hit && cnt < (uint32_t)CAPQ) {
-            crow[cnt] = (uint16_t)((uint32_t)key0 + i);
-            srow[cnt] = x;
-          }
+          if (hit && cnt < (uint32_t)CAPQ) crow[cnt] = (uint16_t)((uint32_t)key0 + i);
           cnt += hit ? 1u : 0u;
         }
       });
@@ -763,7 +741,6 @@ struct FinArgs {
   float* lse;
   float* top_scores;
   const uint16_t* cand;
-  const float* cand_s;
   const int32_t* cand_n;
   const uint32_t* unsafe;  // at each slice's first row, from the stream kernel's key check
   const int32_t* row_index;  // nullable: logical row -> query/output row
@@ -778,7 +755,7 @@ struct FinArgs {
 };
 
 struct __align__(16) FinWarp {
-  float sc[CAP];  // the selection's scores (list order)
+  float sc[CAP];  // candidates' exact scores, then the selection's (list order)
   int si[CAP];    // their key indices
   float pw[64];   // softmax weight of each selection
   float pad[4];
@@ -792,16 +769,13 @@ __device__ __forceinline__ uint32_t ord_score(float x) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// Keeps the `topk` best of a row's `cnt` candidates (larger score first,
-// lower key index on ties; cnt >= topk) and writes them, in list order, to
-// w.sc / w.si; returns the largest score.  The candidates are the four
-// selection threads' lists (counts c0, c1, c2 and the rest) read NVT per
+// Keeps the `topk` best of the row's `cnt` candidates in w.sc / w.si
+// (larger score first, lower key index on ties; cnt >= topk), in list order,
+// at the front of w.sc / w.si; returns the largest score.  NVT candidates per
 // lane.  The lowest-ranked candidate is dropped until topk remain: the
 // lowest ordered score, and among equal scores the highest key index.
 template <int NVT>
-__device__ __forceinline__ float cut_candidates(const uint16_t* crow, const float* srow, int c0, int c1, int c2,
-                                                int cnt, int topk, FinWarp& w, int lane) {
-  const int o1 = c0, o2 = c0 + c1, o3 = c0 + c1 + c2;
+__device__ __forceinline__ float cut_candidates(int cnt, int topk, FinWarp& w, int lane) {
   float xs[NVT];
   int ks[NVT];
   uint32_t os[NVT];
@@ -810,11 +784,11 @@ __device__ __forceinline__ float cut_candidates(const uint16_t* crow, const floa
   for (int i = 0; i < NVT; ++i) {
     const int s = lane + kWarp * i;
     hk[i] = s < cnt;
-    const int at = s < o1 ? s : (s < o2 ? CAPQ + (s - o1) : (s < o3 ? 2 * CAPQ + (s - o2) : 3 * CAPQ + (s - o3)));
-    xs[i] = hk[i] ? srow[at] : 0.f;
-    ks[i] = hk[i] ? (int)crow[at] : 0;
+    xs[i] = hk[i] ? w.sc[s] : 0.f;
+    ks[i] = hk[i] ? w.si[s] : 0;
     os[i] = ord_score(xs[i]);
   }
+  __syncwarp();  // every lane holds its candidates before the compaction below overwrites them
   for (int dn = cnt - topk; dn > 0; --dn) {
     uint32_t mn = 0xffffffffu;
 #pragma unroll
@@ -890,10 +864,33 @@ __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
                       w.pad, lane);
       continue;
     }
-    // the k best candidates of the four selection threads, in list order
-    const float mx = cnt <= 3 * kWarp
-                         ? cut_candidates<3>(a.cand + r * CAP, a.cand_s + r * CAP, c0, c1, c2, cnt, a.topk, w, lane)
-                         : cut_candidates<NV>(a.cand + r * CAP, a.cand_s + r * CAP, c0, c1, c2, cnt, a.topk, w, lane);
+    // the candidates of the four selection threads, in list order
+    const uint16_t* crow = a.cand + r * CAP;
+    const int o1 = c0, o2 = c0 + c1, o3 = c0 + c1 + c2;
+    for (int s = lane; s < cnt; s += kWarp)
+      w.si[s] = (int)crow[s < o1 ? s : (s < o2 ? CAPQ + (s - o1) : (s < o3 ? 2 * CAPQ + (s - o2) : 3 * CAPQ + (s - o3)))];
+    __syncwarp();
+    // exact scores: group grp re-scores candidates grp, grp + 4, ... from the
+    // gathered key rows (eight lanes per 128-byte row, one fixed summation order)
+    const T* kbase = static_cast<const T*>(a.k) + slice * a.m * D;
+    for (int s0 = 0; s0 < cnt; s0 += 4 * FUNR) {
+      uint4 kc[FUNR];
+#pragma unroll
+      for (int u = 0; u < FUNR; ++u) {
+        const int s = s0 + 4 * u + grp;
+        kc[u] = make_uint4(0u, 0u, 0u, 0u);
+        if (s < cnt) kc[u] = __ldg(reinterpret_cast<const uint4*>(kbase + (int64_t)w.si[s] * D) + g);
+      }
+#pragma unroll
+      for (int u = 0; u < FUNR; ++u) {
+        const int s = s0 + 4 * u + grp;
+        const float d = group_dot<T>(qg, kc[u]);
+        if (g == 0 && s < cnt) w.sc[s] = brow ? __fadd_rn(__fmul_rn(d, a.scale), brow[w.si[s] / a.seg_len]) : d;
+      }
+    }
+    __syncwarp();
+    // the k best, in list order
+    const float mx = cnt <= 3 * kWarp ? cut_candidates<3>(cnt, a.topk, w, lane) : cut_candidates<NV>(cnt, a.topk, w, lane);
     const int sel = a.topk;
     // LSE; lane j holds selections j and j + 32 (k <= 64).  Biased scores are final.
     const float sc_mul = brow ? 1.f : a.scale;
@@ -1005,8 +1002,8 @@ int group_log(int64_t m) {
   return 8;
 }
 
-// candidate keys and scores, NSEL counts and the slice check word
-size_t workspace_per_row() { return (size_t)CAP * (sizeof(uint16_t) + sizeof(float)) + 4 * NSEL + 4; }
+// candidate keys, NSEL counts and the slice check word
+size_t workspace_per_row() { return (size_t)CAP * sizeof(uint16_t) + 4 * NSEL + 4; }
 
 template <typename T>
 int launch(const FwdLaunch& L) {
@@ -1050,12 +1047,11 @@ int launch(const FwdLaunch& L) {
   } else if (L.workspace_bytes < need || !aligned16(ws)) {
     return SDK_ERR_INVALID_ARGUMENT;
   }
-  // per row: CAP candidate keys and scores, NSEL counts and a flag (set at the first row of each slice)
+  // per row: CAP candidate keys, NSEL counts and a flag (set at the first row of each slice)
   uint8_t* wb = static_cast<uint8_t*>(ws);
   a.cand = reinterpret_cast<uint16_t*>(wb);
-  a.cand_s = reinterpret_cast<float*>(wb + (size_t)rows * CAP * sizeof(uint16_t));
-  a.cand_n = reinterpret_cast<int32_t*>(wb + (size_t)rows * CAP * (sizeof(uint16_t) + sizeof(float)));
-  a.unsafe = reinterpret_cast<uint32_t*>(wb + (size_t)rows * (CAP * (sizeof(uint16_t) + sizeof(float)) + 4 * NSEL));
+  a.cand_n = reinterpret_cast<int32_t*>(wb + (size_t)rows * CAP * sizeof(uint16_t));
+  a.unsafe = reinterpret_cast<uint32_t*>(wb + (size_t)rows * (CAP * sizeof(uint16_t) + 4 * NSEL));
   a.big16 = bf16 ? 0x5d80u : 0x7c00u;
   kern<<<(unsigned)grid, NT, SMEM_BYTES, L.stream>>>(tq, tk, a);
   int rc = cudaPeekAtLastError() == cudaSuccess ? SDK_OK : SDK_ERR_CUDA;
@@ -1069,7 +1065,6 @@ int launch(const FwdLaunch& L) {
     f.lse = static_cast<float*>(L.lse);
     f.top_scores = static_cast<float*>(L.top_scores);
     f.cand = a.cand;
-    f.cand_s = a.cand_s;
     f.cand_n = a.cand_n;
     f.unsafe = a.unsafe;
     f.row_index = L.row_index;

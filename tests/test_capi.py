@@ -79,7 +79,7 @@ def test_forward_workspace_size_follows_the_tensor_core_shapes():
     # slices alike.
     lib = _native.load()
     size = lib.sdk_topk_attn_fwd_workspace_size
-    per_row = 192 * 6 + 20  # candidate keys and scores of the four selection threads, four counts, a check word
+    per_row = 192 * 2 + 20  # candidate keys of the four selection threads, four counts and a check word
     for code in (_native.DTYPE_BF16, _native.DTYPE_F16):
         assert size(1000, 16384, 64, 64, 64, 0, 0, code) == 1000 * per_row
         assert size(3, 100, 64, 64, 1, 0, 0, code) == 3 * per_row

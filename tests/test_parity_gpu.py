@@ -434,7 +434,7 @@ def test_tensor_core_forward_on_caller_workspace_matches_library_pool():
         return rc, out, idx, lse
 
     need = lib.sdk_topk_attn_fwd_workspace_size(bh * n, m, d, d, k, 0, 0, _native.DTYPE_BF16)
-    assert need == bh * n * (192 * 6 + 20)
+    assert need == bh * n * (192 * 2 + 20)
     buf = torch.empty(need + 16, device=DEV, dtype=torch.uint8)
     rc0, o0, i0, l0 = run(None, 0, pooled=True)
     rc1, o1, i1, l1 = run(buf.data_ptr(), need)
