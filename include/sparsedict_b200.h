@@ -148,6 +148,23 @@ int sdk_topk_attn_bwd(const void* q, const void* k, const void* v, const void* d
                       void* stream);
 
 /*
+ * Forward with a per-query number of selected keys (adaptive k): logical row
+ * r attends over its min(max(row_k[r], 1), topk) best keys, with the
+ * softmax, LSE and output over those alone; the remaining slots of its index
+ * row are -1 (and -inf in top_scores), which every backward entry point
+ * treats as empty.  SparseDict predicts a per-token k_i and collapses it to
+ * one budget before selection (models/moe_topk_restorer.py:333-338,
+ * _effective_top_k; per-token k is listed future work, observations.md:63-65);
+ * this keeps each token's own k.  row_k: device int32 [rows]; topk is the
+ * largest k of the call.  Otherwise as sdk_topk_attn_fwd.
+ */
+int sdk_topk_attn_fwd_adaptive(const void* q, const void* k, const void* v, void* out, int32_t* top_idx,
+                               void* lse, void* top_scores, const int32_t* row_offsets,
+                               const int32_t* row_index, int64_t slices, int64_t n, int64_t m, int32_t d,
+                               int32_t dv, int32_t topk, double scale, int32_t score_grid,
+                               const int32_t* row_k, int32_t dtype, void* stream);
+
+/*
  * Forward with an additive score bias per (query row, key segment): the gate
  * fold of DualDomainMoEDictionary._mixture
  * (models/modules/dual_domain_moe.py:158-173), which adds log(max(g, tiny))
@@ -157,7 +174,8 @@ int sdk_topk_attn_bwd(const void* q, const void* k, const void* v, const void* d
  *   score(r, j) = scale * q_r·k_j + seg_bias[r * segs + j / seg_len]
  * for logical row r; seg_bias is float (double for SDK_DTYPE_F64) and
  * seg_len * segs >= m.  Selection, lse and top_scores use the biased scores.
- * Runs on the CUDA-core kernel.
+ * bf16/fp16 with d = dv = 64 and segments of whole 64-key tile quarters run on
+ * the tensor cores, other shapes on the CUDA-core kernel.
  */
 int sdk_topk_attn_fwd_biased(const void* q, const void* k, const void* v, void* out, int32_t* top_idx,
                              void* lse, void* top_scores, const int32_t* row_offsets,

@@ -39,6 +39,8 @@ SIGNATURES = {
     "sdk_device_status": [ctypes.POINTER(ctypes.c_uint), _i32, _p],
     "sdk_set_wait_limit": [ctypes.c_uint64],
     "sdk_topk_attn_fwd": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _i32, _f64, _i32, _i32, _p],
+    "sdk_topk_attn_fwd_adaptive": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _i32, _f64, _i32,
+                                   _p, _i32, _p],
     "sdk_topk_attn_fwd_workspace_size": [_i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32],
     "sdk_topk_attn_fwd_ws": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _i32, _f64, _i32, _i32,
                              _p, ctypes.c_size_t, _p],

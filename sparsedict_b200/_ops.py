@@ -51,6 +51,7 @@ def topk_attn_fwd(
     row_index: torch.Tensor | None = None,
     out: torch.Tensor | None = None,
     seg_bias: torch.Tensor | None = None,
+    row_k: torch.Tensor | None = None,
 ):
     """Fused forward over ``q2 [rows or (S, n), d]``, ``k2 [S, m, d]``, ``v2 [S, m, dv]``.
 
@@ -58,7 +59,9 @@ def topk_attn_fwd(
     where ``rows`` is ``S * n`` (uniform slices) or the grouped row count.
     ``seg_bias [rows, segs]`` (accumulator dtype, optional) adds
     ``seg_bias[r, j // (m // segs)]`` to the scaled score of row ``r`` and
-    key ``j`` (``m`` must divide into ``segs`` equal segments).
+    key ``j`` (``m`` must divide into ``segs`` equal segments).  ``row_k
+    [rows]`` (int32, optional) gives each row its own number of selected keys
+    (at most ``topk``; the row's other index slots are -1).
     """
     slices, m, d = k2.shape
     dv = v2.shape[-1]
@@ -78,7 +81,10 @@ def topk_attn_fwd(
         head = (q2.data_ptr(), k2.data_ptr(), v2.data_ptr(), out.data_ptr(), idx.data_ptr(), lse.data_ptr(),
                 nat.ptr(scores), nat.ptr(row_offsets), nat.ptr(row_index),
                 slices, n, m, d, dv, topk, float(scale), int(score_grid))
-        if seg_bias is None:
+        if row_k is not None:
+            nat.call("sdk_topk_attn_fwd_adaptive", *head, row_k.data_ptr(), nat.TORCH_TO_SDK[q2.dtype],
+                     nat.stream_of(dev))
+        elif seg_bias is None:
             # scratch from torch's allocator, like every other buffer of the op
             code = nat.TORCH_TO_SDK[q2.dtype]
             nbytes = int(nat.load().sdk_topk_attn_fwd_workspace_size(

@@ -83,7 +83,9 @@ __global__ void __launch_bounds__(NT) sparse_bwd(BwdArgs<typename AccOf<T>::type
       int key = a.top_idx[r * a.topk + j];
       Acc p = 0, g = 0;
       if (key < 0 || key >= a.m) {
-        raise_device_status(a.status, kStatusIndexOutOfRange);
+        // -1 marks an empty slot (a row that keeps fewer keys, or one the
+        // forward gave up on); anything else out of range is flagged
+        if (key != -1) raise_device_status(a.status, kStatusIndexOutOfRange);
         key = -1;
       } else {
         const T* kr = kmat + (int64_t)key * a.d;
@@ -195,11 +197,12 @@ __global__ void __launch_bounds__(G8W * kWarp, 4) sparse_bwd_d64(BwdArgs<float> 
     int i0 = -1, i1 = -1;  // slots lane and lane + 32
     if (lane < a.topk) i0 = a.top_idx[r * a.topk + lane];
     if (lane + 32 < a.topk) i1 = a.top_idx[r * a.topk + lane + 32];
-    if ((lane < a.topk && (i0 < 0 || i0 >= a.m)) || (lane + 32 < a.topk && (i1 < 0 || i1 >= a.m))) {
+    // -1 marks an empty slot (a row that keeps fewer keys, or one the forward
+    // gave up on); anything else out of range is flagged
+    if ((lane < a.topk && (i0 < -1 || i0 >= a.m)) || (lane + 32 < a.topk && (i1 < -1 || i1 >= a.m)))
       raise_device_status(a.status, kStatusIndexOutOfRange);
-      if (i0 >= a.m) i0 = -1;
-      if (i1 >= a.m) i1 = -1;
-    }
+    if (i0 < 0 || i0 >= a.m) i0 = -1;
+    if (i1 < 0 || i1 >= a.m) i1 = -1;
 
     float part = 0.f;
 #pragma unroll 4

@@ -151,7 +151,8 @@ namespace {
 int fwd_impl(const void* q, const void* k, const void* v, void* out, int32_t* top_idx, void* lse, void* top_scores,
              const int32_t* row_offsets, const int32_t* row_index, int64_t slices, int64_t n, int64_t m, int32_t d,
              int32_t dv, int32_t topk, double scale, int32_t score_grid, const void* seg_bias, int64_t seg_len,
-             int32_t segs, int32_t dtype, void* stream, void* workspace = nullptr, size_t workspace_bytes = 0) {
+             int32_t segs, int32_t dtype, void* stream, void* workspace = nullptr, size_t workspace_bytes = 0,
+             const int32_t* row_k = nullptr) {
   if (!q || !k || !v || !out || !top_idx || !lse) return SDK_ERR_INVALID_ARGUMENT;
   if (!dtype_ok(dtype) || slices <= 0 || n < 0 || m <= 0 || d <= 0 || dv <= 0) return SDK_ERR_INVALID_ARGUMENT;
   if (topk < 1 || topk > m || m > 0x7ffffffe || !(scale > 0) || score_grid < 0) return SDK_ERR_INVALID_ARGUMENT;
@@ -164,6 +165,7 @@ int fwd_impl(const void* q, const void* k, const void* v, void* out, int32_t* to
   L.segs = segs;
   L.workspace = workspace;
   L.workspace_bytes = workspace_bytes;
+  L.row_k = row_k;
   if (fwd_tensorcore_supports(L)) return finish(fwd_tensorcore(L));
   return finish(fwd_generic(L));
 }
@@ -234,6 +236,15 @@ int sdk_topk_attn_fwd(const void* q, const void* k, const void* v, void* out, in
                       int32_t dtype, void* stream) {
   return fwd_impl(q, k, v, out, top_idx, lse, top_scores, row_offsets, row_index, slices, n, m, d, dv, topk, scale,
                   score_grid, nullptr, 0, 0, dtype, stream);
+}
+
+int sdk_topk_attn_fwd_adaptive(const void* q, const void* k, const void* v, void* out, int32_t* top_idx, void* lse,
+                               void* top_scores, const int32_t* row_offsets, const int32_t* row_index,
+                               int64_t slices, int64_t n, int64_t m, int32_t d, int32_t dv, int32_t topk,
+                               double scale, int32_t score_grid, const int32_t* row_k, int32_t dtype, void* stream) {
+  if (!row_k) return SDK_ERR_INVALID_ARGUMENT;
+  return fwd_impl(q, k, v, out, top_idx, lse, top_scores, row_offsets, row_index, slices, n, m, d, dv, topk, scale,
+                  score_grid, nullptr, 0, 0, dtype, stream, nullptr, 0, row_k);
 }
 
 size_t sdk_topk_attn_fwd_workspace_size(int64_t rows, int64_t m, int32_t d, int32_t dv, int32_t topk,

@@ -45,6 +45,7 @@ template <typename Acc> struct FwdArgs {
   const Acc* seg_bias;  // nullable: score bias per (logical row, key segment)
   int64_t seg_len;
   int segs;
+  const int32_t* row_k;  // nullable: per logical row, the number of keys to keep
 };
 
 template <typename Acc>
@@ -179,27 +180,30 @@ __global__ void __launch_bounds__(NT) fused_fwd_generic(FwdArgs<typename AccOf<T
     int* ri = ci + r * capp;
     compact_row(rv, ri, cnt[r], a.topk, &tau[r], lane);
     const int64_t lr = row0 + r;
+    // the row keeps its kr best (the list is in reference order); the other
+    // index slots are -1 (adaptive k)
+    const int kr = a.row_k ? min(max(a.row_k[lr], 1), a.topk) : a.topk;
     // softmax shift: the row maximum, or 0 when it is not finite (all
     // selected scores -inf gives LSE -inf)
     const Acc mx = isfinite(rv[0]) ? rv[0] : Acc(0);
     Acc part = 0;
-    for (int j = lane; j < a.topk; j += kWarp) part += exp_acc(rv[j] - mx);
+    for (int j = lane; j < kr; j += kWarp) part += exp_acc(rv[j] - mx);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
     const Acc total = part;
     for (int j = lane; j < a.topk; j += kWarp) {
-      a.top_idx[lr * a.topk + j] = ri[j];
-      if (a.top_scores) a.top_scores[lr * a.topk + j] = rv[j];
+      a.top_idx[lr * a.topk + j] = j < kr ? ri[j] : -1;
+      if (a.top_scores) a.top_scores[lr * a.topk + j] = j < kr ? rv[j] : neg_inf<Acc>();
     }
     if (lane == 0) a.lse[lr] = mx + log_acc(total);
     __syncwarp();
-    for (int j = lane; j < a.topk; j += kWarp) rv[j] = exp_acc(rv[j] - mx) / total;
+    for (int j = lane; j < kr; j += kWarp) rv[j] = exp_acc(rv[j] - mx) / total;
     __syncwarp();
     const int64_t pr = a.row_index ? (int64_t)a.row_index[lr] : lr;
     T* orow = static_cast<T*>(a.out) + pr * a.dv;
     for (int f = lane; f < a.dv; f += kWarp) {
       Acc o = 0;
-      for (int j = 0; j < a.topk; ++j) o = fma(rv[j], to_acc(vmat[(int64_t)ri[j] * a.dv + f]), o);
+      for (int j = 0; j < kr; ++j) o = fma(rv[j], to_acc(vmat[(int64_t)ri[j] * a.dv + f]), o);
       orow[f] = cvt_out<T>(o);
     }
   }
@@ -233,6 +237,7 @@ int launch(const FwdLaunch& L) {
   a.seg_bias = static_cast<const Acc*>(L.seg_bias);
   a.seg_len = L.seg_len;
   a.segs = L.segs;
+  a.row_k = L.row_k;
   const int64_t tiles = L.row_offsets ? (L.n + BQ - 1) / BQ + L.slices : L.slices * ((L.n + BQ - 1) / BQ);
   if (tiles <= 0) return SDK_OK;
   auto kern = fused_fwd_generic<T>;

@@ -332,7 +332,7 @@ struct RowOut {
 template <typename T>
 __device__ __noinline__ void reselect_row(RowOut a, int64_t m, int topk, float scale, int64_t slice, int64_t gr, int64_t pr,
                                           const float* bias_row, int64_t seg_len, float* fv, int* fi, float* ftau,
-                                          int lane) {
+                                          int lane, int stride) {
   const int g = lane & 7, grp = lane >> 3;
   const uint4 qg = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(a.q) + pr * D) + g);
   const T* kbase = static_cast<const T*>(a.k) + slice * m * D;
@@ -382,8 +382,8 @@ __device__ __noinline__ void reselect_row(RowOut a, int64_t m, int topk, float s
   const float lse = mxs + logf(part);
   if (lane == 0) a.lse[gr] = lse;
   write_row<T>(static_cast<const T*>(a.v) + slice * m * D, [&](int j) { return fv[j]; }, [&](int j) { return fi[j]; },
-               c0, scale, lse, static_cast<T*>(a.out) + pr * D, a.top_idx + gr * topk,
-               a.top_scores ? a.top_scores + gr * topk : nullptr, lane);
+               c0, scale, lse, static_cast<T*>(a.out) + pr * D, a.top_idx + gr * stride,
+               a.top_scores ? a.top_scores + gr * stride : nullptr, lane);
   __syncwarp();
 }
 
@@ -745,6 +745,7 @@ struct FinArgs {
   const uint32_t* unsafe;  // at each slice's first row, from the stream kernel's key check
   const int32_t* row_index;  // nullable: logical row -> query/output row
   const float* seg_bias;     // nullable: per (logical row, key segment), as in TcArgs
+  const int32_t* row_k;      // nullable: per logical row, the number of keys to keep
   int64_t seg_len;
   int segs;
   SliceGeometry geo;
@@ -856,12 +857,18 @@ __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
     bool bias_bad = false;  // NaN or +inf biases are ranked by the exact path only
     if (brow)
       for (int j = lane; j < a.segs; j += kWarp) bias_bad |= !(brow[j] < __int_as_float(0x7f800000));
+    // keys this row keeps (adaptive k); its other index slots are -1
+    const int kr = a.row_k ? min(max(a.row_k[r], 1), a.topk) : a.topk;
+    for (int j = kr + lane; j < a.topk; j += kWarp) {
+      a.top_idx[r * a.topk + j] = -1;
+      if (a.top_scores) a.top_scores[r * a.topk + j] = __int_as_float(0xff800000);
+    }
     if (min(min(c0, c1), min(c2, c3)) < 0 || max(max(c0, c1), max(c2, c3)) > CAPQ || cnt < a.topk || unsafe ||
         __any_sync(0xffffffffu, bias_bad)) {
       uint8_t* fix = reinterpret_cast<uint8_t*>(&w);
-      reselect_row<T>(RowOut{a.q, a.k, a.v, a.out, a.top_idx, a.lse, a.top_scores}, a.m, a.topk, a.scale, slice, r, pr,
+      reselect_row<T>(RowOut{a.q, a.k, a.v, a.out, a.top_idx, a.lse, a.top_scores}, a.m, kr, a.scale, slice, r, pr,
                       brow, a.seg_len, reinterpret_cast<float*>(fix), reinterpret_cast<int*>(fix + FIX_CAP * 4),
-                      w.pad, lane);
+                      w.pad, lane, a.topk);
       continue;
     }
     // the candidates of the four selection threads, in list order
@@ -890,8 +897,8 @@ __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
     }
     __syncwarp();
     // the k best, in list order
-    const float mx = cnt <= 3 * kWarp ? cut_candidates<3>(cnt, a.topk, w, lane) : cut_candidates<NV>(cnt, a.topk, w, lane);
-    const int sel = a.topk;
+    const float mx = cnt <= 3 * kWarp ? cut_candidates<3>(cnt, kr, w, lane) : cut_candidates<NV>(cnt, kr, w, lane);
+    const int sel = kr;
     // LSE; lane j holds selections j and j + 32 (k <= 64).  Biased scores are final.
     const float sc_mul = brow ? 1.f : a.scale;
     const bool v0 = lane < sel, v1 = lane + kWarp < sel;
@@ -1069,6 +1076,7 @@ int launch(const FwdLaunch& L) {
     f.unsafe = a.unsafe;
     f.row_index = L.row_index;
     f.seg_bias = a.seg_bias;
+    f.row_k = L.row_k;
     f.seg_len = L.seg_len;
     f.segs = L.segs;
     f.geo = a.geo;

@@ -40,6 +40,10 @@ struct FwdLaunch {
   const void* seg_bias = nullptr;
   int64_t seg_len = 0;
   int segs = 0;
+  // Optional per-row number of selected keys (adaptive k): logical row r keeps
+  // its min(max(row_k[r], 1), topk) best keys; the other slots of its index row
+  // are -1 (and -inf in top_scores).  Null: topk for every row.
+  const int32_t* row_k = nullptr;
   // Scratch of the tensor-core forward (fwd_tensorcore_workspace bytes, 16-byte
   // aligned); null: stream-ordered scratch from this library's memory pool.
   void* workspace = nullptr;

@@ -159,3 +159,25 @@ def test_selection_operators_check_arguments():
         selection.straight_through_topk(torch.rand(3, 5), 6)
     with pytest.raises(ValueError, match="CUDA"):
         selection.gumbel_perturbed_topk(torch.rand(3, 5), 2)
+
+
+@pytest.mark.parametrize("kq,error,message", [
+    ([[[1, 2, 3]]], TypeError, "k_per_query must be a torch.Tensor"),
+    (torch.ones(1, 1, 3), ValueError, "integer dtype"),
+    (torch.ones(1, 1, 4, dtype=torch.int32), ValueError, "must have shape"),
+    (torch.zeros(1, 1, 3, dtype=torch.int32), ValueError, r"values must lie in \[1, 2\]"),
+])
+def test_adaptive_topk_rejects_invalid_budgets(kq, error, message):
+    from sparsedict_b200 import adaptive_topk_attention
+
+    q, k, v = torch.randn(1, 1, 3, 4), torch.randn(1, 1, 5, 4), torch.randn(1, 1, 5, 4)
+    with pytest.raises(error, match=message):
+        adaptive_topk_attention(q, k, v, kq, k_max=2)
+
+
+def test_adaptive_topk_requires_cuda():
+    from sparsedict_b200 import adaptive_topk_attention
+
+    q, k, v = torch.randn(1, 1, 3, 4), torch.randn(1, 1, 5, 4), torch.randn(1, 1, 5, 4)
+    with pytest.raises(ValueError, match="CUDA"):
+        adaptive_topk_attention(q, k, v, torch.ones(1, 1, 3, dtype=torch.int32))
