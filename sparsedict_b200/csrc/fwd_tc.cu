@@ -36,9 +36,11 @@
 // overflow its list (heavily tied scores) is re-selected exactly by its warp
 // over all keys.
 //
-// scale = 1/(T·sqrt(d)) > 0 is applied in the epilogue, or, with a segment
-// bias, to each exact score as fl(fl(dot·scale)+bias).
+// scale = 1/(T·sqrt(d)) > 0 is applied to each exact score, fl(dot·scale),
+// or with a segment bias fl(fl(dot·scale)+bias), before the ranking.
 #include <cuda.h>
+
+#include <cmath>
 
 #include <mutex>
 #include <type_traits>
@@ -104,6 +106,7 @@ struct TcArgs {
   int64_t seg_len;
   int segs;
   float scale;
+  int widen;  // scale is not a power of two (see the filter threshold)
 };
 
 // Input magnitude check.  With every |q|, |k| < 2^60 and finite, each of the
@@ -353,8 +356,9 @@ __device__ __noinline__ void reselect_row(RowOut a, int64_t m, int topk, float s
     }
     const int64_t key = k0 + lane;
     const bool valid = key < m;
-    // biased: the final score, scaled then shifted by the key's segment bias
-    if (bias_row && valid) s = __fadd_rn(__fmul_rn(s, scale), bias_row[key / seg_len]);
+    // the final score: scaled, then shifted by the key's segment bias
+    s = __fmul_rn(s, scale);
+    if (bias_row && valid) s = __fadd_rn(s, bias_row[key / seg_len]);
     const bool pass = valid && !(s <= tau);
     const unsigned bal = __ballot_sync(0xffffffffu, pass);
     if (pass) {
@@ -371,18 +375,17 @@ __device__ __noinline__ void reselect_row(RowOut a, int64_t m, int topk, float s
   }
   __syncwarp();
   c0 = compact_row(fv, fi, c0, topk, ftau, lane);  // sorted, c0 == topk (topk <= m)
-  if (bias_row) scale = 1.f;  // the list already holds final scores
   // softmax shift: the row maximum, or 0 when it is not finite (all scores
   // -inf gives LSE -inf; a NaN or +inf maximum gives NaN / +inf)
-  const float mxs = finite_or_zero(fv[0] * scale);
+  const float mxs = finite_or_zero(fv[0]);
   float part = 0.f;
-  for (int j = lane; j < c0; j += kWarp) part += expf(fv[j] * scale - mxs);
+  for (int j = lane; j < c0; j += kWarp) part += expf(fv[j] - mxs);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
   const float lse = mxs + logf(part);
   if (lane == 0) a.lse[gr] = lse;
   write_row<T>(static_cast<const T*>(a.v) + slice * m * D, [&](int j) { return fv[j]; }, [&](int j) { return fi[j]; },
-               c0, scale, lse, static_cast<T*>(a.out) + pr * D, a.top_idx + gr * stride,
+               c0, 1.f, lse, static_cast<T*>(a.out) + pr * D, a.top_idx + gr * stride,
                a.top_scores ? a.top_scores + gr * stride : nullptr, lane);
   __syncwarp();
 }
@@ -680,6 +683,12 @@ __global__ void __launch_bounds__(NT, 1)
         if (c >= a.topk) L = mid; else H = mid;
       }
     }
+    // Rows are ranked on fl(dot·scale).  When scale is not a power of two,
+    // that rounding can tie a key below tau with one at or above it (and the
+    // lower key index wins the tie), so the filter then starts one bf16 step
+    // lower: every dot whose scaled value equals that of a dot >= tau lies
+    // within a few fp32 ulps of it.
+    if (!kBias && a.widen && L > bf16_ord(kBf16NegInf)) L -= 1u;
     const uint32_t tau_b = bounded ? bf16_of_ord(L) : kBf16NegInf;
     const float tau = __uint_as_float(tau_b << 16);
 
@@ -892,34 +901,36 @@ __global__ void __launch_bounds__(FW * kWarp, 4) fwd_tc_finish(FinArgs a) {
       for (int u = 0; u < FUNR; ++u) {
         const int s = s0 + 4 * u + grp;
         const float d = group_dot<T>(qg, kc[u]);
-        if (g == 0 && s < cnt) w.sc[s] = brow ? __fadd_rn(__fmul_rn(d, a.scale), brow[w.si[s] / a.seg_len]) : d;
+        // the final score, as the generic kernel forms it: fl(dot·scale),
+        // shifted by the key's segment bias when there is one
+        const float x = __fmul_rn(d, a.scale);
+        if (g == 0 && s < cnt) w.sc[s] = brow ? __fadd_rn(x, brow[w.si[s] / a.seg_len]) : x;
       }
     }
     __syncwarp();
     // the k best, in list order
     const float mx = cnt <= 3 * kWarp ? cut_candidates<3>(cnt, kr, w, lane) : cut_candidates<NV>(cnt, kr, w, lane);
     const int sel = kr;
-    // LSE; lane j holds selections j and j + 32 (k <= 64).  Biased scores are final.
-    const float sc_mul = brow ? 1.f : a.scale;
+    // LSE; lane j holds selections j and j + 32 (k <= 64)
     const bool v0 = lane < sel, v1 = lane + kWarp < sel;
     const float x0 = v0 ? w.sc[lane] : 0.f, x1 = v1 ? w.sc[lane + kWarp] : 0.f;
     const int k0 = v0 ? w.si[lane] : 0, k1 = v1 ? w.si[lane + kWarp] : 0;
-    const float mxs = finite_or_zero(mx * sc_mul);
-    float part = (v0 ? expf(x0 * sc_mul - mxs) : 0.f) + (v1 ? expf(x1 * sc_mul - mxs) : 0.f);
+    const float mxs = finite_or_zero(mx);
+    float part = (v0 ? expf(x0 - mxs) : 0.f) + (v1 ? expf(x1 - mxs) : 0.f);
 #pragma unroll
     for (int o2 = 16; o2 > 0; o2 >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o2);
     const float lse = mxs + logf(part);
     if (lane == 0) a.lse[r] = lse;
     int32_t* idx_row = a.top_idx + r * a.topk;
     if (v0) {
-      w.pw[lane] = expf(x0 * sc_mul - lse);
+      w.pw[lane] = expf(x0 - lse);
       idx_row[lane] = k0;
-      if (a.top_scores) a.top_scores[r * a.topk + lane] = x0 * sc_mul;
+      if (a.top_scores) a.top_scores[r * a.topk + lane] = x0;
     }
     if (v1) {
-      w.pw[lane + kWarp] = expf(x1 * sc_mul - lse);
+      w.pw[lane + kWarp] = expf(x1 - lse);
       idx_row[lane + kWarp] = k1;
-      if (a.top_scores) a.top_scores[r * a.topk + lane + kWarp] = x1 * sc_mul;
+      if (a.top_scores) a.top_scores[r * a.topk + lane + kWarp] = x1;
     }
     __syncwarp();
     // softmax-weighted sum of the value rows: group grp takes selections
@@ -1036,6 +1047,10 @@ int launch(const FwdLaunch& L) {
   a.seg_len = L.seg_len;
   a.segs = L.segs;
   a.scale = (float)L.scale;
+  {
+    int e2 = 0;
+    a.widen = std::frexp(a.scale, &e2) != 0.5f;
+  }
   // grouped: at most ceil(rows / TQ) + slices tiles; CTAs past the last exit at once
   const int64_t grid = grouped ? (rows + TQ - 1) / TQ + L.slices : L.slices * ((L.n + TQ - 1) / TQ);
   if (grid <= 0) return SDK_OK;

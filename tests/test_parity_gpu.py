@@ -21,6 +21,7 @@ import oracle
 from sparsedict_b200 import (
     FusedTopKAttentionFunction,
     _native,
+    _ops,
     fused_topk_attention,
     hybrid_topk_attention,
     tiled_affinity,
@@ -219,6 +220,46 @@ def test_ties_and_minus_inf_rows_follow_the_reference_order():
     v = torch.arange(9 * 2, dtype=torch.float32).reshape(1, 1, 9, 2)
     _, idx, _, _ = _hybrid_topk_attention_with_aux(q.to(DEV), k.to(DEV), v.to(DEV), 5, 1.0)
     assert idx[0, 0].tolist() == [0, 2, 4, 7, 3]
+
+
+def _merging_temperature(hi, lo):
+    """A temperature whose fp32 scale 1/(8T) (d = 64) is not a power of two and
+    rounds the scores ``hi`` > ``lo`` to one fp32 value."""
+    for t in np.linspace(0.55, 1.45, 9001):
+        s = np.float32(1.0 / (float(t) * 8.0))
+        if math.frexp(float(s))[0] != 0.5 and hi * s == lo * s:
+            return float(t)
+    raise AssertionError("no temperature merges the two scores")
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("topk", [1, 2])
+def test_scores_tied_by_the_scale_pick_the_lower_index(dtype, topk):
+    # key 3 scores 1.75 - 2^-23 and key 300 scores 1.75; the scale rounds both
+    # to one fp32 value, so the reference's order (larger scaled score, lower
+    # index on ties) keeps key 3, whose raw score lies below the tensor-core
+    # filter's bf16 bound 1.75.  At k = 2 key 100 (score 3) takes the first slot.
+    hi = np.float32(1.75)
+    lo = np.nextafter(hi, np.float32(0))
+    temperature = _merging_temperature(hi, lo)
+    m, d = 512, 64
+    q = torch.zeros(1, 1, 128, d)
+    q[..., 0] = 1.0
+    q[..., 1] = 2.0 ** -23
+    k = torch.zeros(1, 1, m, d)
+    k[0, 0, 300, 0] = 1.75
+    k[0, 0, 3, 0] = 1.75
+    k[0, 0, 3, 1] = -1.0
+    if topk == 2:
+        k[0, 0, 100, 0] = 3.0
+    v = torch.arange(m * d, dtype=torch.float32).reshape(1, 1, m, d) / (m * d)
+    scale = 1.0 / (temperature * math.sqrt(d))
+    _, idx, _, ts = _ops.topk_attn_fwd(_flat(q).to(DEV, dtype), _flat(k).to(DEV, dtype), _flat(v).to(DEV, dtype),
+                                       topk, scale, want_scores=True)
+    # the tensor-core forward keeps its selections in candidate-list order
+    expected = [3] if topk == 1 else [3, 100]
+    assert all(sorted(row) == expected for row in idx.tolist())
+    assert (ts[idx == 3] == float(hi * np.float32(scale))).all()
 
 
 # --- hybrid ------------------------------------------------------------------
