@@ -431,6 +431,17 @@ def cpu_routed_sample(tokens=ROUTED_CFG["N"], seed=0):
         ("" if tokens == c["N"] else "; queries/s extrapolated")
 
 
+def tensor_peak_key(clock_summary):
+    """The burst bf16 peak is the denominator for a step that keeps the maximum SM
+    clock (the forward runs for milliseconds inside a sub-second loop); a clock
+    record that shows the power cap, or a median clock well below the maximum,
+    selects the sustained figure measured under the cap."""
+    capped = "sw_power_cap" in (clock_summary.get("reasons") or []) or (
+        clock_summary.get("sm_mhz") and clock_summary.get("sm_max_mhz")
+        and clock_summary["sm_mhz"] < 0.9 * clock_summary["sm_max_mhz"])
+    return "bf16_tflops_sustained" if capped else "bf16_tflops"
+
+
 def run_routed_arm(args):
     import torch
     import torch.distributed as dist
@@ -544,7 +555,9 @@ def run_routed_arm(args):
     peaks = load_peaks()
     flops = 2.0 * c["N"] * c["M"] * c["d"]  # each token against the M atoms of its expert
     achieved = flops / (fwd_ms / 1000.0) / 1e12
-    peak_tc = peaks["bf16_tflops"]
+    clock_summary = clocks.summary()
+    peak_key = tensor_peak_key(clock_summary)
+    peak_tc = peaks[peak_key]
     line = {
         "metric": ROUTED_METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1000 * elapsed / args.steps, "higher_is_better": True,
@@ -554,7 +567,7 @@ def run_routed_arm(args):
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tc, "unit": "TFLOP/s",
                      "frac": achieved / peak_tc, "traffic": None,
                      "kernel": "forward (routing + stream + finish kernels)", "fwd_ms": fwd_ms,
-                     "peak_source": f"{peaks['source']} bf16_tflops"},
+                     "peak_source": f"{peaks['source']} {peak_key}"},
         # per step: the router's count, scan and place kernels, the forward's stream
         # and finishing kernels, the backward's scatter kernel and the
         # dictionary-gradient conversion
@@ -659,15 +672,8 @@ def run_native_arm(args):
     # finishing kernel: exact re-score, softmax, value gather), one call = two launches
     fwd_flops_per_launch = flops_tc / world
     achieved = fwd_flops_per_launch / (fwd_ms / 1000.0) / 1e12
-    # The burst bf16 peak is the denominator for a step that keeps the maximum SM
-    # clock (the forward runs for milliseconds inside a sub-second loop); a clock
-    # record that shows the power cap, or a median clock well below the maximum,
-    # selects the sustained figure measured under the cap.
     clock_summary = clocks.summary()
-    capped = "sw_power_cap" in (clock_summary.get("reasons") or []) or (
-        clock_summary.get("sm_mhz") and clock_summary.get("sm_max_mhz")
-        and clock_summary["sm_mhz"] < 0.9 * clock_summary["sm_max_mhz"])
-    peak_key = "bf16_tflops_sustained" if capped else "bf16_tflops"
+    peak_key = tensor_peak_key(clock_summary)
     peak_tc = peaks[peak_key]
     # ncu-measured DRAM bytes of one headline forward call (profiles/traffic.json)
     traffic = load_traffic().get("forward_B16_H8_N16384_k64") if (c["B"], c["H"], world) == (CFG["B"], CFG["H"], 1) else None
