@@ -63,6 +63,16 @@ def test_invalid_arguments_are_rejected_before_any_device_work():
     assert rc == _native.SDK_ERR_INVALID_ARGUMENT
     rc = lib.sdk_topk_aggregate(fake, fake, fake, fake, 4, 2, 8, 16, 2, 2, 16, 0, 48, 0, None)
     assert rc == _native.SDK_ERR_INVALID_ARGUMENT
+    # per-row budgets: the row_k array is required; the common checks still apply
+    rc = lib.sdk_topk_attn_fwd_adaptive(fake, fake, fake, fake, fake, fake, None, None, None,
+                                        1, 4, 8, 16, 16, 2, 0.25, 0, None, 0, None)
+    assert rc == _native.SDK_ERR_INVALID_ARGUMENT
+    rc = lib.sdk_topk_attn_fwd_adaptive(fake, fake, fake, fake, fake, fake, None, None, None,
+                                        1, 4, 8, 16, 16, 9, 0.25, 0, fake, 0, None)
+    assert rc == _native.SDK_ERR_INVALID_ARGUMENT
+    rc = lib.sdk_topk_attn_fwd_adaptive(None, fake, fake, fake, fake, fake, None, None, None,
+                                        1, 4, 8, 16, 16, 2, 0.25, 0, fake, 0, None)
+    assert rc == _native.SDK_ERR_INVALID_ARGUMENT
 
 
 @pytest.mark.parametrize("dtype", [0, 1, 2, 3])
