@@ -39,7 +39,7 @@ enum {
 enum {
   SDK_OK = 0,
   SDK_ERR_INVALID_ARGUMENT = 1, /* a size, pointer or dtype the call cannot accept */
-  SDK_ERR_UNSUPPORTED = 2,      /* valid request outside this build's kernels (e.g. k too large) */
+  SDK_ERR_UNSUPPORTED = 2,      /* valid request outside the library's kernels (e.g. k too large) */
   SDK_ERR_CUDA = 3,             /* a CUDA runtime call or launch failed */
   SDK_ERR_NO_DEVICE = 4,        /* no sm_100 device is current */
   SDK_ERR_TOO_LARGE = 5,        /* request exceeds the fixed scratch of sdk_topk_attn_bwd_noalloc */

@@ -1,6 +1,6 @@
 """CPU oracle for SparseDict's top-k sparse attention (test infrastructure).
 
-This module is the checker, never the product: only ``tests/``,
+This module checks the product and is never part of it: only ``tests/``,
 ``__graft_entry__.smoke()`` and the CPU-baseline legs of ``bench.py`` may
 import it.  The CUDA path in ``sparsedict_b200`` never calls into it.
 

@@ -111,7 +111,7 @@ const char* sdk_status_string(int status) {
   switch (status) {
     case SDK_OK: return "ok";
     case SDK_ERR_INVALID_ARGUMENT: return "invalid argument";
-    case SDK_ERR_UNSUPPORTED: return "unsupported by this build's kernels";
+    case SDK_ERR_UNSUPPORTED: return "unsupported by the library's kernels";
     case SDK_ERR_CUDA: return "CUDA error";
     case SDK_ERR_NO_DEVICE: return "no sm_100 CUDA device is current";
     case SDK_ERR_TOO_LARGE: return "request exceeds the fixed scratch capacity of the no-allocation entry point";
